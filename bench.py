@@ -1,0 +1,407 @@
+#!/usr/bin/env python
+"""Benchmark of the SF37 KV-cache hot path on B200.
+
+Default workload: one decode step of a synthetic
+48-layer stack, 64 query heads / 8 KV heads, head_dim 128, f16 KV caches with
+32768 cached positions, batch 1.  Per layer and step: append one K/V row,
+then GQA attention over 32769+ positions (the position advances every
+step).  One step = one sf37kv_decode() call over all 48 layers.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+
+N > 1 (under torchrun): KV heads sharded 8/N per GPU, per-head attention
+outputs all-gathered over NCCL every step; total work is fixed (strong).
+
+Output: one JSON line on rank 0 (see the repository's build contract).
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "decode-attn KV-read GB/s (% of 8 TB/s) and tokens/s at 32K ctx, 1/2/4/8 B200"
+LAYERS, QH, KVH, HD, CTX = 48, 64, 8, 128, 32768
+
+
+def _peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def _traffic_from_profiles(name):
+    """Per-launch DRAM bytes of the dominant kernel from the committed ncu
+    summary (a line 'traffic_bytes_per_launch: N'), or None."""
+    p = os.path.join(ROOT, "profiles", name)
+    if not os.path.exists(p):
+        return None
+    for line in open(p):
+        if line.strip().startswith("traffic_bytes_per_launch:"):
+            try:
+                return float(line.split(":", 1)[1].strip())
+            except ValueError:
+                return None
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi sampling during the timed region."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ---------------------------------------------------------------- CPU legs
+_CPU_DATA = {}
+
+
+def cpu_reference_step_time(threads, layers_sample, rows):
+    """One decode step of `layers_sample` layers through the reference's own
+    CPU code (kv_cache_push + attention_decode + gate, oracle/_ref), spread
+    over `threads` threads (one layer per thread at a time).  Each layer has
+    its own fp32 cache holding f16-valued N(0,1) data.  Returns seconds."""
+    import ctypes
+    import oracle
+    R = oracle.ref()
+    kd = KVH * HD
+    cap = rows
+    key = (layers_sample, rows)
+    if key not in _CPU_DATA:
+        rng = np.random.default_rng(0)
+        k0 = rng.standard_normal((cap, kd), dtype=np.float32).astype(np.float16).astype(np.float32)
+        v0 = rng.standard_normal((cap, kd), dtype=np.float32).astype(np.float16).astype(np.float32)
+        d = dict(k=[k0] + [k0.copy() for _ in range(layers_sample - 1)],
+                 v=[v0] + [v0.copy() for _ in range(layers_sample - 1)],
+                 q=[rng.standard_normal((QH, HD), dtype=np.float32) for _ in range(layers_sample)],
+                 g=[rng.standard_normal((QH,), dtype=np.float32) for _ in range(layers_sample)],
+                 o=[np.zeros((QH, HD), np.float32) for _ in range(layers_sample)],
+                 kn=[rng.standard_normal((kd,), dtype=np.float32) for _ in range(layers_sample)],
+                 vn=[rng.standard_normal((kd,), dtype=np.float32) for _ in range(layers_sample)])
+
+        def parr(lst):
+            a = (ctypes.c_void_p * len(lst))()
+            for i, x in enumerate(lst):
+                a[i] = x.ctypes.data
+            return a
+        d["p"] = {n: parr(d[n]) for n in ("k", "v", "q", "g", "o", "kn", "vn")}
+        d["sliding"] = (ctypes.c_int * layers_sample)(*([0] * layers_sample))
+        _CPU_DATA[key] = d
+    d = _CPU_DATA[key]
+    p = d["p"]
+    # cap-1 live rows; the push of this step fills the last row
+    n_live = (ctypes.c_uint32 * layers_sample)(*([cap - 1] * layers_sample))
+    t0 = time.perf_counter()
+    ok = R.sf37ref_decode_step_layers(p["k"], p["v"], n_live, cap, p["kn"], p["vn"], p["q"], p["g"],
+                                      p["o"], d["sliding"], QH, layers_sample, threads)
+    dt = time.perf_counter() - t0
+    assert ok
+    return dt
+
+
+def _cpu_plan():
+    threads = os.cpu_count() or 1
+    sample_layers = max(1, min(LAYERS, threads, 16))
+    return min(threads, sample_layers), sample_layers
+
+
+def cpu_baseline(rows):
+    import oracle
+    if not oracle.ref_available():
+        return None
+    threads, sample_layers = _cpu_plan()
+    cpu_reference_step_time(threads, sample_layers, rows)  # warm (page-in)
+    dt = min(cpu_reference_step_time(threads, sample_layers, rows) for _ in range(3))
+    full = dt * LAYERS / sample_layers
+    return {"value": 1.0 / full, "unit": "tokens/s", "cores": threads,
+            "kind": "reference",
+            "sample": f"{sample_layers} of {LAYERS} layers x {rows} rows (one decode step through the "
+                      f"reference's own kv_cache_push+attention_decode+gate, fp32 cache holding f16 "
+                      f"values), extrapolated linearly to {LAYERS} layers",
+            "kv_read_GBps": sample_layers * rows * KVH * HD * 2 * 4 / dt / 1e9}
+
+
+def run_reference(args, rank, world):
+    """--impl reference: the reference's own CPU implementation of the path."""
+    if rank != 0:
+        return
+    import oracle
+    if not oracle.ref_available():
+        print(json.dumps({"impl": "reference",
+                          "unavailable": "oracle/_ref/libsf37ref.so was not built (needs the reference tree)"}))
+        return
+    threads, sample_layers = _cpu_plan()
+    rows = CTX + 1
+    for _ in range(args.warmup):
+        cpu_reference_step_time(threads, sample_layers, rows)
+    ts = [cpu_reference_step_time(threads, sample_layers, rows) for _ in range(args.steps)]
+    step = sum(ts) / len(ts) * LAYERS / sample_layers
+    val = 1.0 / step
+    line = {"impl": "reference", "metric": METRIC, "value": val, "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": step * 1e3,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic N(0,1) f16-valued K/V, fp32 query (seeded)",
+            "config": {"workload": "cfg2: 48-layer decode step at 32768 cached tokens, 64 Q / 8 KV "
+                                   "heads, d 128, batch 1", "layers": LAYERS, "ctx": CTX},
+            "cpu_baseline": {"value": val, "unit": "tokens/s", "cores": threads,
+                             "kind": "reference",
+                             "sample": f"{sample_layers} of {LAYERS} layers per step, extrapolated"},
+            "e2e": {"value": val, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------- GPU leg
+def run_ours(args, rank, world):
+    import torch
+    import torch.distributed as dist
+    from sf37_b200 import kv
+
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(dev)
+    assert KVH % world == 0, "world size must divide the 8 KV heads"
+    kvh_l = KVH // world
+    qh_l = QH // world
+    kd = kvh_l * HD
+    steps, warm = args.steps, args.warmup
+    cap = CTX + warm + steps + 8
+    g = torch.Generator(device=dev)
+    g.manual_seed(1234 + rank)
+    stream = torch.cuda.current_stream(dev)
+
+    # Caches: KV rows 0..CTX-1 filled with N(0,1) (f16 RNE); every step appends one row.
+    kc, vc = [], []
+    for _ in range(LAYERS):
+        k = torch.empty(cap, kd, dtype=torch.float16, device=dev)
+        v = torch.empty(cap, kd, dtype=torch.float16, device=dev)
+        k.normal_(generator=g)
+        v.normal_(generator=g)
+        kc.append(k)
+        vc.append(v)
+    q = torch.randn(LAYERS, qh_l, HD, device=dev, generator=g)
+    gate = torch.randn(LAYERS, qh_l, device=dev, generator=g)
+    kn = torch.randn(LAYERS, kd, device=dev, generator=g)
+    vn = torch.randn(LAYERS, kd, device=dev, generator=g)
+    out = torch.empty(LAYERS, qh_l, HD, device=dev)
+    gathered = torch.empty(world, LAYERS, qh_l, HD, device=dev)
+
+    def descs(pos, with_append=True):
+        return kv.decode_layers_desc([
+            dict(k_cache=kc[l], v_cache=vc[l], cap=cap, pos=pos, q=q[l], gate=gate[l], out=out[l],
+                 k_new=kn[l] if with_append else None, v_new=vn[l] if with_append else None)
+            for l in range(LAYERS)])
+
+    all_desc = [descs(CTX + i) for i in range(warm + steps)]
+
+    def step(i):
+        kv.decode(all_desc[i], qh_l, kvh_l, HD, kv.F16, stream)
+        if world > 1:
+            dist.all_gather_into_tensor(gathered, out)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+
+    for i in range(warm):
+        step(i)
+    barrier()
+    n0 = kv.launch_count()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(dev.index) as clk:
+        ev0.record(stream)
+        for i in range(warm, warm + steps):
+            step(i)
+        ev1.record(stream)
+        barrier()
+    launches = kv.launch_count() - n0
+    ms = ev0.elapsed_time(ev1) / steps
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    rows_mean = CTX + 1 + warm + (steps - 1) / 2.0
+    kv_bytes_step = LAYERS * rows_mean * KVH * HD * 2 * 2  # whole job, f16 K+V
+    tok_s = 1000.0 / ms
+
+    # Roofline leg: the attention kernel alone (no append), one launch per
+    # call, CUDA events on the launching stream around each launch.
+    att_desc = descs(CTX + warm + steps - 1, with_append=False)
+    for _ in range(3):
+        kv.decode(att_desc, qh_l, kvh_l, HD, kv.F16, stream)
+    torch.cuda.synchronize(dev)
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(steps)]
+    for a, b in evs:
+        a.record(stream)
+        kv.decode(att_desc, qh_l, kvh_l, HD, kv.F16, stream)
+        b.record(stream)
+    torch.cuda.synchronize(dev)
+    att_ms = sum(a.elapsed_time(b) for a, b in evs) / steps
+    rows_att = CTX + warm + steps
+    att_bytes = LAYERS * (rows_att * kd * 2 * 2 + qh_l * HD * 4 * 2 + qh_l * 4)
+    peak, peak_kind = _peaks()
+    achieved = att_bytes / (att_ms * 1e-3) / 1e9
+    traffic = _traffic_from_profiles("decode_f16_cfg2.md")
+
+    # End-to-end leg through the C ABI with host buffers: pinned host inputs
+    # (q, gate, new K/V rows) copied in, outputs copied out, every step.
+    h_q = torch.empty_like(q, device="cpu").pin_memory()
+    h_gate = torch.empty_like(gate, device="cpu").pin_memory()
+    h_kn = torch.empty_like(kn, device="cpu").pin_memory()
+    h_vn = torch.empty_like(vn, device="cpu").pin_memory()
+    h_out = torch.empty(LAYERS, QH, HD).pin_memory() if world > 1 else \
+        torch.empty_like(out, device="cpu").pin_memory()
+    for t_ in (h_q, h_gate, h_kn, h_vn):
+        t_.normal_()
+    h2d = sum(t_.numel() * t_.element_size() for t_ in (h_q, h_gate, h_kn, h_vn))
+    d2h = h_out.numel() * h_out.element_size()
+    e2e_desc = [descs(CTX + warm + steps + (i % 4)) for i in range(4)]
+
+    def e2e_step(i):
+        q.copy_(h_q, non_blocking=True)
+        gate.copy_(h_gate, non_blocking=True)
+        kn.copy_(h_kn, non_blocking=True)
+        vn.copy_(h_vn, non_blocking=True)
+        kv.decode(e2e_desc[i % 4], qh_l, kvh_l, HD, kv.F16, stream)
+        if world > 1:
+            dist.all_gather_into_tensor(gathered, out)
+            h_out.view(LAYERS, world, qh_l, HD).copy_(gathered.permute(1, 0, 2, 3), non_blocking=True)
+        else:
+            h_out.copy_(out, non_blocking=True)
+
+    for i in range(3):
+        e2e_step(i)
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(steps):
+        e2e_step(i)
+    e1.record(stream)
+    barrier()
+    e2e_ms = e0.elapsed_time(e1) / steps
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+
+    if rank != 0:
+        return
+    cpu = cpu_baseline(CTX + 1) if world == 1 and not args.no_cpu else None
+    clocks = clk.summary()
+    line = {
+        "metric": METRIC, "value": tok_s, "unit": "tokens/s", "n_gpus": world, "steps": steps,
+        "warmup": warm, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f16",
+        "data": "synthetic: N(0,1) f16 K/V caches and fp32 q/gate/new rows from torch's seeded CUDA "
+                "generator",
+        "config": {"workload": "cfg2: 48-layer decode step (append + GQA attention) at 32768 cached "
+                               "tokens, 64 Q / 8 KV heads, d 128, batch 1",
+                   "layers": LAYERS, "ctx": CTX, "q_heads": QH, "kv_heads": KVH, "head_dim": HD,
+                   "kv_heads_per_gpu": kvh_l,
+                   "parallelism": f"kv-head shard x{world}" + (" + NCCL all-gather" if world > 1 else ""),
+                   "l2": "no flush needed: 6.4 GB of KV per step >> 126 MB L2"},
+        "kv_read_GBps": kv_bytes_step / (ms * 1e-3) / 1e9,
+        "kv_read_frac_of_8TBps": kv_bytes_step / (ms * 1e-3) / 8e12,
+        "roofline": {"bound": "hbm", "kernel": "decode_f16_kernel", "achieved": achieved,
+                     "peak": peak, "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / peak,
+                     "traffic": traffic, "launch_ms": att_ms,
+                     "algorithmic_bytes_per_launch": att_bytes},
+        "e2e": {"value": 1000.0 / e2e_ms, "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
+        "gpu_launches": launches,
+        "clocks": clocks,
+    }
+    if cpu:
+        line["cpu_baseline"] = cpu
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+    if world > 1:
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+        dist.init_process_group("nccl")
+    run_ours(args, rank, world)
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

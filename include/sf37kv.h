@@ -1,0 +1,155 @@
+/*
+ * Native C ABI of libsf37kv: the B200 KV-cache hot path beyond the
+ * reference's fp32 drop-in entry points (sf37_cuda_kv.h).
+ *
+ * Adds what the reference ABI cannot express:
+ *   - f16 caches (the throughput mode; the reference caches are f32 only),
+ *   - multi-layer batched calls (one launch for many independent layers),
+ *   - explicit CUDA streams (passed as void*, NULL = the library stream),
+ *   - error codes plus sf37kv_last_error() instead of stderr-only failures,
+ *   - bf16 queries for chunked prefill,
+ *   - KV-head slices for the multi-GPU layout (a GPU that owns heads
+ *     [h0, h0+n) of every layer simply passes kv_heads = n and its slice of
+ *     the queries: see sf37kv_decode()).
+ *
+ * All pointers are device pointers unless named host_*; all sizes are
+ * element counts unless named *_bytes.  Every call is asynchronous on its
+ * stream unless documented otherwise.
+ */
+#ifndef SF37KV_H
+#define SF37KV_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+    SF37KV_OK = 0,
+    SF37KV_EINVAL = 1,       /* bad argument; nothing was launched */
+    SF37KV_ECUDA = 2,        /* a CUDA call failed */
+    SF37KV_ENOMEM = 3,       /* device or host allocation failed */
+    SF37KV_EUNSUPPORTED = 4  /* valid but not implemented shape */
+};
+
+/* Cache element type = element size in bytes. */
+enum { SF37KV_F16 = 2, SF37KV_F32 = 4 };
+/* Query element type for prefill. */
+enum { SF37KV_Q_F32 = 0, SF37KV_Q_BF16 = 1 };
+/* Snapshot KV row formats. */
+enum { SF37KV_FMT_RAW_F32 = 0, SF37KV_FMT_I8_GROUPED = 1 };
+
+const char *sf37kv_last_error(void);
+const char *sf37kv_version(void);
+
+/* Library stream used by the drop-in entry points and by native calls given
+ * stream == NULL.  Default: the legacy default stream (as the reference). */
+int sf37kv_set_stream(void *stream);
+void *sf37kv_get_stream(void);
+
+/* One layer's cache.  k_cache/v_cache: [cap][kv_heads][head_dim] of dtype.
+ * Positions live in ring slot pos % cap.  sliding layers attend to the
+ * last `window` positions (sf37_cuda.cu:2752-2758). */
+typedef struct {
+    void *k_cache;
+    void *v_cache;
+    uint32_t cap;
+    uint32_t sliding;
+    uint32_t window;
+    uint32_t reserved;
+} sf37kv_cache;
+
+/* One layer of a decode step. */
+typedef struct {
+    sf37kv_cache cache;
+    uint32_t pos;          /* position of this token */
+    uint32_t reserved;
+    const float *q;        /* [q_heads][head_dim] */
+    const float *gate;     /* [q_heads] or NULL (no gate) */
+    float *out;            /* [q_heads][head_dim] */
+    const float *k_new;    /* [kv_heads*head_dim] row appended at pos, or NULL */
+    const float *v_new;
+} sf37kv_decode_layer;
+
+/* Decode step over n_layers independent layers: for each layer, append
+ * (k_new, v_new) at slot pos % cap (f32 -> f16 round-to-nearest-even for f16
+ * caches) when k_new is non-NULL, then GQA attention of the query at pos:
+ * out[h] = softmax(q[h] K^T / sqrt(head_dim)) V * sigmoid(gate[h]), with
+ * K/V head h / (q_heads/kv_heads) (sf37_cuda.cu:3079-3161 semantics).
+ * head_dim 128 and q_heads/kv_heads <= 16 use the fast kernels; other shapes
+ * use a generic kernel (head_dim <= 256). */
+int sf37kv_decode(const sf37kv_decode_layer *layers, uint32_t n_layers,
+                  uint32_t q_heads, uint32_t kv_heads, uint32_t head_dim,
+                  int dtype, void *stream);
+
+/* Append n_tok rows per layer: row t -> slot (pos0 + t) % cap
+ * (store_kv_cache_batch_kernel, sf37_cuda.cu:6355-6372). */
+typedef struct {
+    sf37kv_cache cache;
+    uint32_t pos0;
+    uint32_t n_tok;
+    const float *k;        /* [n_tok][kv_dim] */
+    const float *v;
+} sf37kv_append_layer;
+int sf37kv_append(const sf37kv_append_layer *layers, uint32_t n_layers,
+                  uint32_t kv_dim, int dtype, void *stream);
+
+/* Chunked prefill of one layer: the n_tok rows of the chunk must already be
+ * appended; token t is a causal query at pos0 + t over rows
+ * start_at(pos0+t) .. pos0+t (sf37_cuda.cu:3163-3317 semantics).
+ * q: [n_tok][q_heads][head_dim] of q_type; gate: [n_tok][q_heads] f32 or
+ * NULL; out: [n_tok][q_heads][head_dim] f32.  A sliding ring needs
+ * cap >= window + n_tok (sf37.c:3083-3091) for exact results. */
+int sf37kv_prefill(const sf37kv_cache *cache, const void *q, int q_type,
+                   const float *gate, float *out, uint32_t pos0, uint32_t n_tok,
+                   uint32_t q_heads, uint32_t kv_heads, uint32_t head_dim,
+                   int dtype, void *stream);
+
+/* ---- snapshot KV sections (bit-exact with the reference formats) ----
+ * Byte size of one encoded row. */
+uint64_t sf37kv_row_bytes(uint32_t kv_dim, int fmt, uint32_t group);
+
+/* One layer of a snapshot pack/unpack: rows first_pos .. first_pos+rows-1
+ * (ring slot % cap), written as K row then V row per position into
+ * dst + offset (sf37.c:6980-7010, 7298-7320). */
+typedef struct {
+    sf37kv_cache cache;
+    uint32_t first_pos;
+    uint32_t rows;
+    uint64_t offset;       /* byte offset of this layer's section in the buffer */
+} sf37kv_pack_layer;
+
+/* Gather/encode all layers into dst (device memory or device-mapped pinned
+ * host memory).  variant: see sf37_cuda_kv_pack_rows_i8g. */
+int sf37kv_pack(void *dst, const sf37kv_pack_layer *layers, uint32_t n_layers,
+                uint32_t kv_dim, int dtype, int fmt, uint32_t group, int variant,
+                void *stream);
+/* Decode/scatter src back into the caches (the inverse of sf37kv_pack). */
+int sf37kv_unpack(const void *src, const sf37kv_pack_layer *layers, uint32_t n_layers,
+                  uint32_t kv_dim, int dtype, int fmt, uint32_t group, void *stream);
+
+/* Pinned host memory for snapshot buffers (cudaHostAlloc, mapped). */
+void *sf37kv_host_alloc(uint64_t bytes);
+void sf37kv_host_free(void *p);
+
+/* Whole snapshot KV section to host memory: packs on the device into a
+ * staging buffer chunk by chunk and streams each chunk to host_dst with the
+ * copy engine on a side stream, overlapping pack and copy.  Synchronous:
+ * returns when host_dst holds the bytes.  host_dst should be pinned
+ * (sf37kv_host_alloc) for full link speed. */
+int sf37kv_pack_to_host(void *host_dst, const sf37kv_pack_layer *layers, uint32_t n_layers,
+                        uint32_t kv_dim, int dtype, int fmt, uint32_t group, int variant);
+int sf37kv_unpack_from_host(const void *host_src, const sf37kv_pack_layer *layers,
+                            uint32_t n_layers, uint32_t kv_dim, int dtype, int fmt,
+                            uint32_t group);
+
+/* Number of kernel launches this library has issued (process total). */
+uint64_t sf37kv_launch_count(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif

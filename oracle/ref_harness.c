@@ -1,0 +1,127 @@
+/*
+ * Test infrastructure only: a thin exporter around the reference's own CPU
+ * KV-cache code.  It compiles the reference translation unit sf37.c
+ * (found through -I$(REF_DIR)) with the reference Makefile flags and
+ * re-exports the static functions the KV hot path is built from, so that the
+ * oracle restatement and the CUDA library can be checked against the
+ * reference's real arithmetic.  Nothing in the product links this file.
+ *
+ * Re-exported (reference file:line):
+ *   kv_cache_push                      sf37.c:2054-2064
+ *   attention_decode                   sf37.c:2066-2101
+ *   gate loop after attention          sf37.c:2235-2239 (sf37_sigmoid, sf37_ops.c:9-16)
+ *   payload_encode_kv_row_i8_grouped   sf37.c:6633-6659
+ *   payload_decode_kv_row_i8_grouped   sf37.c:6661-6674
+ *   payload_encoded_kv_row_bytes       sf37.c:6628-6631
+ */
+#include "sf37.c"
+
+#include <pthread.h>
+
+/* One linear CPU layer cache, as sf37_layer_kv_cache (sf37.c:199-204). */
+uint64_t sf37ref_layer_cache_bytes(uint32_t cap) {
+    return (uint64_t)cap * SF37_KV_HEADS * SF37_HEAD_DIM * sizeof(float);
+}
+
+/* Push n rows (k, v each [n][1024] f32) into a cache of capacity cap that
+ * currently holds *n_live rows; on return *n_live is the new count. */
+void sf37ref_kv_cache_push_rows(float *k_cache, float *v_cache, uint32_t cap,
+                                uint32_t *n_live, const float *k, const float *v,
+                                uint32_t n) {
+    sf37_layer_kv_cache layer;
+    layer.k = k_cache;
+    layer.v = v_cache;
+    layer.n = *n_live;
+    layer.cap = cap;
+    const uint64_t row = (uint64_t)SF37_KV_HEADS * SF37_HEAD_DIM;
+    for (uint32_t i = 0; i < n; i++) kv_cache_push(&layer, k + i * row, v + i * row);
+    *n_live = layer.n;
+}
+
+/* attention_decode + the sigmoid gate of run_layer_decode.  gate may be NULL
+ * (no gating, as attention_decode alone). */
+void sf37ref_attention_decode(float *out, const float *q, const float *k_cache,
+                              const float *v_cache, uint32_t n_live, uint32_t cap,
+                              uint32_t q_heads, int sliding, const float *gate) {
+    sf37_layer_kv_cache layer;
+    layer.k = (float *)k_cache;
+    layer.v = (float *)v_cache;
+    layer.n = n_live;
+    layer.cap = cap;
+    attention_decode(out, q, &layer, q_heads, sliding != 0);
+    if (gate) {
+        for (uint32_t h = 0; h < q_heads; h++) {
+            const float g = sf37_sigmoid(gate[h]);
+            float *head = out + (uint64_t)h * SF37_HEAD_DIM;
+            for (uint32_t d = 0; d < SF37_HEAD_DIM; d++) head[d] *= g;
+        }
+    }
+}
+
+uint64_t sf37ref_payload_row_bytes(uint32_t elems, uint32_t group) {
+    return payload_encoded_kv_row_bytes(elems, group);
+}
+
+void sf37ref_payload_encode_rows(const float *src, uint32_t elems, uint32_t group,
+                                 uint64_t n_rows, uint8_t *dst) {
+    const uint64_t eb = payload_encoded_kv_row_bytes(elems, group);
+    for (uint64_t r = 0; r < n_rows; r++)
+        payload_encode_kv_row_i8_grouped(src + r * elems, elems, group, dst + r * eb);
+}
+
+void sf37ref_payload_decode_rows(const uint8_t *src, uint32_t elems, uint32_t group,
+                                 uint64_t n_rows, float *dst) {
+    const uint64_t eb = payload_encoded_kv_row_bytes(elems, group);
+    for (uint64_t r = 0; r < n_rows; r++)
+        payload_decode_kv_row_i8_grouped(src + r * eb, elems, group, dst + r * elems);
+}
+
+/* ---- multi-threaded driver for the timed CPU baseline ----
+ * The reference CPU path is single-threaded (one layer after another).  For
+ * the CPU baseline the independent layers of the synthetic stack are spread
+ * over worker threads; each layer still runs the reference's own
+ * kv_cache_push + attention_decode + gate. */
+typedef struct {
+    float **k, **v, **q, **out, **gate, **k_new, **v_new;
+    uint32_t *n_live, cap, q_heads;
+    const int *sliding;
+    uint32_t l0, l1;
+} sf37ref_job;
+
+static void *sf37ref_worker(void *arg) {
+    sf37ref_job *j = (sf37ref_job *)arg;
+    for (uint32_t l = j->l0; l < j->l1; l++) {
+        sf37ref_kv_cache_push_rows(j->k[l], j->v[l], j->cap, &j->n_live[l],
+                                   j->k_new[l], j->v_new[l], 1);
+        sf37ref_attention_decode(j->out[l], j->q[l], j->k[l], j->v[l], j->n_live[l],
+                                 j->cap, j->q_heads, j->sliding[l], j->gate[l]);
+    }
+    return NULL;
+}
+
+/* One decode step of n_layers independent layers on n_threads threads. */
+int sf37ref_decode_step_layers(float **k, float **v, uint32_t *n_live, uint32_t cap,
+                               float **k_new, float **v_new, float **q, float **gate,
+                               float **out, const int *sliding, uint32_t q_heads,
+                               uint32_t n_layers, uint32_t n_threads) {
+    if (n_threads == 0) n_threads = 1;
+    if (n_threads > n_layers) n_threads = n_layers;
+    pthread_t th[256];
+    sf37ref_job jobs[256];
+    if (n_threads > 256) n_threads = 256;
+    uint32_t per = (n_layers + n_threads - 1) / n_threads;
+    uint32_t started = 0;
+    for (uint32_t t = 0; t < n_threads; t++) {
+        sf37ref_job *j = &jobs[t];
+        j->k = k; j->v = v; j->q = q; j->out = out; j->gate = gate;
+        j->k_new = k_new; j->v_new = v_new; j->n_live = n_live; j->cap = cap;
+        j->q_heads = q_heads; j->sliding = sliding;
+        j->l0 = t * per;
+        j->l1 = j->l0 + per > n_layers ? n_layers : j->l0 + per;
+        if (j->l0 >= j->l1) break;
+        if (pthread_create(&th[t], NULL, sf37ref_worker, j) != 0) return 0;
+        started++;
+    }
+    for (uint32_t t = 0; t < started; t++) pthread_join(th[t], NULL);
+    return 1;
+}

@@ -1,0 +1,936 @@
+// GQA decode attention over ring-indexed KV caches: split-K flash-decoding.
+//
+// Semantics (reference sf37_cuda.cu:2384-3161): for query head h of KV head
+// kvh = h / G (G = q_heads / kv_heads), over logical rows [start, end) at ring
+// slot r % cap:  out[h] = softmax(q[h].K[r] / sqrt(d)) . V[r] * sigmoid(gate[h]).
+//
+// Work decomposition (all kernels): one CTA per (job, kv head, split), where
+// a job is one layer's query (decode) or one prefill token (fallback path)
+// and a split is a contiguous run of rows.  Every CTA serves all G query
+// heads of its KV head, so each K/V byte is read from HBM once per group.
+// Inside a CTA the warps take interleaved 16-row (f16) or 4/8-row (f32)
+// blocks, keep an online softmax state each, and merge through shared memory.
+// With more than one split per (job, kv head), each CTA writes a partial
+// (O, max, sum) to scratch; the last CTA to finish (atomic counter) merges
+// the partials and writes the output, so a whole multi-layer step is one
+// launch.  Scores are kept in the log2 domain (q pre-scaled by
+// log2(e)/sqrt(d)); a running max is only raised when a block's max exceeds
+// it by more than 8 (2^8 headroom), which removes almost all O rescaling.
+//
+// f16 caches (the throughput path, head_dim 128, G <= 16): QK^T and PV are
+// mma.sync m16n8k16 tiles fed straight from 128-bit global loads in
+// registers (no shared-memory staging: the dimension order inside a head is
+// permuted so each thread's loaded words already are its mma fragments).
+// The 16 M-rows of a tile hold 8 query heads twice: rows 0-7 carry the f16
+// "hi" part of q (and of P), rows 8-15 the f16 remainder "lo", so q.K and
+// P.V are computed to ~22 mantissa bits with fp32 accumulation at no extra
+// mma cost.  This is a bandwidth-bound gather; the tensor cores only keep the
+// FMA count out of the way.
+//
+// f32 caches (the reference-compatible path): CUDA-core fp32 kernel, lanes
+// over the head dimension, partial dot products of several rows x heads
+// reduced with a transposing butterfly (N values over 32 lanes in N-1
+// shuffles).
+//
+// Anything else (head_dim != 128, other G): a generic warp-per-head kernel.
+#include <cfloat>
+#include <cstdio>
+#include <cmath>
+
+#include "kv_internal.cuh"
+#include "../../include/sf37_cuda_kv.h"
+
+namespace sf37kv {
+
+extern unsigned long long g_launches;
+
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr uint32_t kMaxSplits = 256;
+constexpr float kRescaleSlack = 8.0f;
+
+struct JobDev {
+    const void *k;
+    const void *v;
+    const float *q;
+    const float *gate;
+    float *out;
+    uint32_t start, end, cap;
+    uint32_t split_rows, n_splits, cta_begin;
+};
+
+struct DecodeParams {
+    JobDev job[kMaxJobs];
+    uint32_t n_jobs, total_ctas;
+    uint32_t q_heads, kv_heads, group;
+    uint32_t part_stride;  // floats per CTA partial: G*128 O, then G (m, l) pairs
+    float *part;
+    uint32_t *counters;    // one per (job, kv head)
+    float qscale;          // log2(e) / sqrt(head_dim)
+};
+
+// ------------------------------------------------------------ helpers
+__device__ __forceinline__ uint32_t locate_job(const DecodeParams &P, uint32_t cta) {
+    uint32_t j = 0;
+    while (j + 1 < P.n_jobs && P.job[j + 1].cta_begin <= cta) j++;
+    return j;
+}
+
+__device__ __forceinline__ uint4 ld_stream16(const void *p) {
+    uint4 r;
+    asm("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+        : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+        : "l"(p));
+    return r;
+}
+
+__device__ __forceinline__ float4 ld_stream_f4(const void *p) {
+    uint4 r = ld_stream16(p);
+    return make_float4(__uint_as_float(r.x), __uint_as_float(r.y), __uint_as_float(r.z),
+                       __uint_as_float(r.w));
+}
+
+__device__ __forceinline__ uint32_t word_of(const uint4 &u, int w) {
+    return w == 0 ? u.x : (w == 1 ? u.y : (w == 2 ? u.z : u.w));
+}
+
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+    uint32_t r;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(sel));
+    return r;
+}
+
+__device__ __forceinline__ uint32_t h2_as_u32(__half2 h) { return *reinterpret_cast<uint32_t *>(&h); }
+
+__device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                         uint32_t a3, uint32_t b0, uint32_t b1) {
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+        "{%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// Slot of logical row base + x, given sb = base % cap.
+__device__ __forceinline__ uint32_t ring_slot(uint32_t sb, uint32_t x, uint32_t cap) {
+    uint32_t s = sb + x;
+    if (s >= cap) s -= cap;
+    if (s >= cap) s %= cap;  // only when cap < 16
+    return s;
+}
+
+// ------------------------------------------------------------ CTA epilogue
+// Shared memory used by the epilogue: per stream and head, O[128], m, l.
+//   Os[(stream * 16 + h) * 128 + d], Ms[stream*16 + h], Ls[stream*16 + h]
+// After the stream merge, the CTA's result is written either directly to the
+// output (single split) or to scratch followed by the last-CTA reduction.
+template <int NT>
+__device__ void finish_cta(const DecodeParams &P, const JobDev &J, uint32_t j, uint32_t kvh,
+                           uint32_t split, uint32_t cta, uint32_t n_streams,
+                           uint32_t heads_per_part, float *Os, float *Ms, float *Ls) {
+    const uint32_t G = P.group;
+    const uint32_t tid = threadIdx.x;
+    __syncthreads();
+    // Merge streams: thread handles elements (h, d) with stride NT.
+    const bool single = J.n_splits == 1;
+    float *part = P.part + (uint64_t)cta * P.part_stride;
+    for (uint32_t idx = tid; idx < G * 128u; idx += NT) {
+        const uint32_t h = idx >> 7, d = idx & 127u;
+        float M = -INFINITY;
+        for (uint32_t s = 0; s < n_streams; s++) M = fmaxf(M, Ms[s * 16u + h]);
+        float L = 0.f, O = 0.f;
+        if (M != -INFINITY) {
+            for (uint32_t s = 0; s < n_streams; s++) {
+                const float w = exp2f(Ms[s * 16u + h] - M);
+                L += Ls[s * 16u + h] * w;
+                O += Os[(s * 16u + h) * 128u + d] * w;
+            }
+        }
+        if (single) {
+            const uint32_t qh = kvh * G + h;
+            const float g = J.gate ? sigmoid_dev(J.gate[qh]) : 1.0f;
+            J.out[(uint64_t)qh * 128u + d] = L > 0.f ? O / L * g : 0.f;
+        } else {
+            part[h * 128u + d] = O;
+            if (d == 0) {
+                part[G * 128u + 2u * h] = M;
+                part[G * 128u + 2u * h + 1u] = L;
+            }
+        }
+    }
+    (void)heads_per_part;
+    if (single) return;
+
+    // Last-CTA election (threadFenceReduction pattern).
+    __shared__ uint32_t s_last;
+    __threadfence();
+    __syncthreads();
+    uint32_t *ctr = P.counters + (uint64_t)j * P.kv_heads + kvh;
+    if (tid == 0) s_last = atomicAdd(ctr, 1u) == J.n_splits - 1u;
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+
+    const uint32_t n = J.n_splits;
+    const uint32_t base = J.cta_begin + kvh * n;
+    const float *P0 = P.part + (uint64_t)base * P.part_stride;
+    // Step 1: per head, global max, weights w[s][h] (into Os), total sum.
+    float *W = Os;          // n * G floats (n <= kMaxSplits, G <= 16)
+    float *Mh = Ms;         // G floats
+    float *Lh = Ls;         // G floats
+    const uint32_t lane = tid & 31u, warp = tid >> 5;
+    for (uint32_t h = warp; h < G; h += NT / 32) {
+        float m = -INFINITY;
+        for (uint32_t s = lane; s < n; s += 32)
+            m = fmaxf(m, __ldcg(P0 + (uint64_t)s * P.part_stride + G * 128u + 2u * h));
+        for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        float l = 0.f;
+        for (uint32_t s = lane; s < n; s += 32) {
+            const float *ml = P0 + (uint64_t)s * P.part_stride + G * 128u + 2u * h;
+            const float w = m == -INFINITY ? 0.f : exp2f(__ldcg(ml) - m);
+            W[s * G + h] = w;
+            l += __ldcg(ml + 1) * w;
+        }
+        for (int o = 16; o; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
+        if (lane == 0) {
+            Mh[h] = m;
+            Lh[h] = l;
+        }
+    }
+    __syncthreads();
+    // Step 2: O = sum_s w[s][h] * O_s[h][d], four dims per thread.
+    for (uint32_t idx = tid; idx < G * 32u; idx += NT) {
+        const uint32_t h = idx >> 5, d4 = (idx & 31u) * 4u;
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        uint32_t s = 0;
+        for (; s + 4 <= n; s += 4) {
+            float4 x[4];
+#pragma unroll
+            for (int u = 0; u < 4; u++)
+                x[u] = __ldcg(reinterpret_cast<const float4 *>(
+                    P0 + (uint64_t)(s + u) * P.part_stride + h * 128u + d4));
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                const float w = W[(s + u) * G + h];
+                acc.x += x[u].x * w;
+                acc.y += x[u].y * w;
+                acc.z += x[u].z * w;
+                acc.w += x[u].w * w;
+            }
+        }
+        for (; s < n; s++) {
+            const float4 x = __ldcg(reinterpret_cast<const float4 *>(
+                P0 + (uint64_t)s * P.part_stride + h * 128u + d4));
+            const float w = W[s * G + h];
+            acc.x += x.x * w;
+            acc.y += x.y * w;
+            acc.z += x.z * w;
+            acc.w += x.w * w;
+        }
+        const uint32_t qh = kvh * G + h;
+        const float L = Lh[h];
+        const float g = J.gate ? sigmoid_dev(J.gate[qh]) : 1.0f;
+        const float f = L > 0.f ? g / L : 0.f;
+        float4 r;
+        r.x = L > 0.f ? acc.x / L * g : 0.f;
+        r.y = L > 0.f ? acc.y / L * g : 0.f;
+        r.z = L > 0.f ? acc.z / L * g : 0.f;
+        r.w = L > 0.f ? acc.w / L * g : 0.f;
+        (void)f;
+        *reinterpret_cast<float4 *>(J.out + (uint64_t)qh * 128u + d4) = r;
+    }
+    if (tid == 0) *ctr = 0u;  // ready for the next launch
+}
+
+// ------------------------------------------------------------ f16 kernel
+// NW warps; warp w handles M-tile (w % n_mt) (query heads 8*mt .. 8*mt+7 of
+// the group) and row stream (w / n_mt).  Thread (g = lane/4, t = lane%4).
+//
+// Register fragments (mma m16n8k16, A row-major 16x16, B col-major 16x8):
+//  * QK^T: B[k][n] = K[row b+8i+n][pi(k)], the head dimension permuted so
+//    that thread (g,t) holds 16-byte chunks t, t+4, t+8, t+12 of row b+8i+g;
+//    the 16 words of those chunks are, in order, the B registers of the 8
+//    k-steps.  A = q in the same permutation: row g = hi(q[head g]), row
+//    g+8 = lo(q[head g]).  S = C[row g] + C[row g+8].
+//  * PV: A = P from the S accumulators (FlashAttention-2 register reuse),
+//    rows g / g+8 = hi / lo of p.  B[k][n] = V[row b+k][sigma(n-tile, n)]:
+//    thread (g,t) loads rows b+2t, b+2t+1, b+2t+8, b+2t+9, chunks g and g+8,
+//    and interleaves the two rows of each B register with one PRMT.
+//    Output dim of (n-tile jt, column c) = jt<8 ? 8c+jt : 64+8c+jt-8.
+template <int NW>
+__global__ void __launch_bounds__(NW * 32, 3) decode_f16_kernel(const __grid_constant__ DecodeParams P) {
+    extern __shared__ __align__(16) float smem[];
+    float *Os = smem;                                  // [NW streams][16 heads][128]
+    float *Ms = Os + NW * 16 * 128;                    // 16*NW
+    float *Ls = Ms + 16 * NW;                          // 16*NW
+    uint4 *Qs = reinterpret_cast<uint4 *>(Ls + 16 * NW);  // [n_mt][8 kk][32 lanes]
+
+    const uint32_t cta = blockIdx.x;
+    const uint32_t j = locate_job(P, cta);
+    const JobDev &J = P.job[j];
+    const uint32_t local = cta - J.cta_begin;
+    const uint32_t kvh = local / J.n_splits, split = local - kvh * J.n_splits;
+    const uint32_t G = P.group;
+    const uint32_t n_mt = (G + 7u) >> 3;
+    const uint32_t n_streams = NW / n_mt;
+    const uint32_t lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;
+    const uint32_t g = lane >> 2, t = lane & 3u;
+    const uint32_t mt = warp % n_mt, stream = warp / n_mt;
+
+    // Q fragments -> shared memory (one warp per M-tile builds them).
+    if (warp < n_mt) {
+        const uint32_t hg = warp * 8u + g;
+        const bool valid = hg < G;
+        const float *qp = J.q + (uint64_t)(kvh * G + (valid ? hg : 0u)) * 128u;
+#pragma unroll
+        for (int kk = 0; kk < 8; kk++) {
+            uint32_t r[4];
+#pragma unroll
+            for (int half = 0; half < 2; half++) {
+                const int w = 2 * kk + half;
+                const uint32_t dim = (4u * (w >> 2) + t) * 8u + 2u * (w & 3);
+                float2 x = valid ? *reinterpret_cast<const float2 *>(qp + dim) : make_float2(0.f, 0.f);
+                x.x *= P.qscale;
+                x.y *= P.qscale;
+                const __half2 hi = __floats2half2_rn(x.x, x.y);
+                const float2 hf = __half22float2(hi);
+                const __half2 lo = __floats2half2_rn(x.x - hf.x, x.y - hf.y);
+                r[half * 2] = h2_as_u32(hi);
+                r[half * 2 + 1] = h2_as_u32(lo);
+            }
+            Qs[(warp * 8 + kk) * 32 + lane] = make_uint4(r[0], r[1], r[2], r[3]);
+        }
+    }
+    __syncthreads();
+
+    const uint32_t row0 = J.start + split * J.split_rows;
+    const uint32_t row1 = min(row0 + J.split_rows, J.end);
+    const uint32_t cap = J.cap;
+    const uint64_t row_bytes = (uint64_t)P.kv_heads * 256u;
+    const char *kbase = reinterpret_cast<const char *>(J.k) + kvh * 256u;
+    const char *vbase = reinterpret_cast<const char *>(J.v) + kvh * 256u;
+    const uint4 *qs = Qs + mt * 8 * 32 + lane;
+
+    float o[16][4];
+#pragma unroll
+    for (int i = 0; i < 16; i++) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+    float m_run = -INFINITY, l_run = 0.f;
+
+    const uint32_t bstep = n_streams * 16u;
+    uint32_t b = row0 + stream * 16u;
+    uint4 kr[2][4], vr[4][2];
+
+    auto load_k = [&](uint32_t bb) {
+        const uint32_t sb = bb % cap;
+#pragma unroll
+        for (int i = 0; i < 2; i++) {
+            const uint32_t r = bb + 8u * i + g;
+            const uint32_t slot = r < row1 ? ring_slot(sb, 8u * i + g, cap) : sb;
+            const char *p = kbase + (uint64_t)slot * row_bytes + t * 16u;
+#pragma unroll
+            for (int c = 0; c < 4; c++) kr[i][c] = ld_stream16(p + c * 64);
+        }
+    };
+    auto load_v = [&](uint32_t bb) {
+        const uint32_t sb = bb % cap;
+#pragma unroll
+        for (int x = 0; x < 4; x++) {
+            const uint32_t off = 2u * t + (x & 1) + (x >> 1) * 8u;
+            const uint32_t r = bb + off;
+            const uint32_t slot = r < row1 ? ring_slot(sb, off, cap) : sb;
+            const char *p = vbase + (uint64_t)slot * row_bytes + g * 16u;
+            vr[x][0] = ld_stream16(p);
+            vr[x][1] = ld_stream16(p + 128);
+        }
+    };
+
+    if (b < row1) {
+        load_k(b);
+        load_v(b);
+    }
+    for (; b < row1; b += bstep) {
+        // S = q K^T for rows b .. b+15 (two n-tiles of 8 keys).
+        float s[2][4];
+#pragma unroll
+        for (int i = 0; i < 2; i++) s[i][0] = s[i][1] = s[i][2] = s[i][3] = 0.f;
+#pragma unroll
+        for (int kk = 0; kk < 8; kk++) {
+            const uint4 a = qs[kk * 32];
+#pragma unroll
+            for (int i = 0; i < 2; i++) {
+                const uint4 &u = kr[i][kk >> 1];
+                const uint32_t b0 = (kk & 1) ? u.z : u.x;
+                const uint32_t b1 = (kk & 1) ? u.w : u.y;
+                mma16816(s[i], a.x, a.y, a.z, a.w, b0, b1);
+            }
+        }
+        const uint32_t nb = b + bstep;
+        if (nb < row1) load_k(nb);
+
+        // Online softmax (log2 domain) for head row g.
+        float sc[2][2];
+#pragma unroll
+        for (int i = 0; i < 2; i++)
+#pragma unroll
+            for (int e = 0; e < 2; e++) {
+                const uint32_t r = b + 8u * i + 2u * t + e;
+                sc[i][e] = r < row1 ? s[i][e] + s[i][e + 2] : -INFINITY;
+            }
+        float mx = fmaxf(fmaxf(sc[0][0], sc[0][1]), fmaxf(sc[1][0], sc[1][1]));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+        if (__any_sync(0xffffffffu, mx > m_run + kRescaleSlack)) {
+            const float m_new = fmaxf(m_run, mx);
+            const float alpha = fast_exp2(m_run - m_new);
+            l_run *= alpha;
+#pragma unroll
+            for (int i = 0; i < 16; i++) {
+                o[i][0] *= alpha;
+                o[i][1] *= alpha;
+                o[i][2] *= alpha;
+                o[i][3] *= alpha;
+            }
+            m_run = m_new;
+        }
+        float p[2][2];
+#pragma unroll
+        for (int i = 0; i < 2; i++)
+#pragma unroll
+            for (int e = 0; e < 2; e++) {
+                p[i][e] = fast_exp2(sc[i][e] - m_run);
+                l_run += p[i][e];
+            }
+        uint32_t pa[4];
+#pragma unroll
+        for (int i = 0; i < 2; i++) {
+            const __half2 hi = __floats2half2_rn(p[i][0], p[i][1]);
+            const float2 hf = __half22float2(hi);
+            const __half2 lo = __floats2half2_rn(p[i][0] - hf.x, p[i][1] - hf.y);
+            pa[2 * i] = h2_as_u32(hi);
+            pa[2 * i + 1] = h2_as_u32(lo);
+        }
+        // O += P V over 16 n-tiles of 8 (permuted) dims.
+#pragma unroll
+        for (int jt = 0; jt < 16; jt++) {
+            const int u = jt >> 3, e = jt & 7, w = e >> 1;
+            const uint32_t sel = (e & 1) ? 0x7632u : 0x5410u;
+            const uint32_t b0 = prmt(word_of(vr[0][u], w), word_of(vr[1][u], w), sel);
+            const uint32_t b1 = prmt(word_of(vr[2][u], w), word_of(vr[3][u], w), sel);
+            mma16816(o[jt], pa[0], pa[1], pa[2], pa[3], b0, b1);
+        }
+        if (nb < row1) load_v(nb);
+    }
+
+    // Per-warp state -> shared memory.
+    l_run += __shfl_xor_sync(0xffffffffu, l_run, 1);
+    l_run += __shfl_xor_sync(0xffffffffu, l_run, 2);
+    const uint32_t hrow = mt * 8u + g;
+    float *Ow = Os + (stream * 16u + hrow) * 128u;
+    if (hrow < G) {
+#pragma unroll
+        for (int jt = 0; jt < 16; jt++)
+#pragma unroll
+            for (int e = 0; e < 2; e++) {
+                const uint32_t c = 2u * t + e;
+                const uint32_t dim = jt < 8 ? 8u * c + jt : 64u + 8u * c + (jt - 8);
+                Ow[dim] = o[jt][e] + o[jt][e + 2];
+            }
+        if (t == 0) {
+            Ms[stream * 16u + hrow] = m_run;
+            Ls[stream * 16u + hrow] = l_run;
+        }
+    }
+    finish_cta<NW * 32>(P, J, j, kvh, split, cta, n_streams, 8, Os, Ms, Ls);
+}
+
+// ------------------------------------------------------------ f32 kernel
+// Warp = (part, stream): part p owns heads [p*GP, (p+1)*GP) of the group,
+// stream s takes row blocks s, s+n_streams, ...  Lane holds dims 4*lane..+3.
+template <int NW, int GP, int R>
+__global__ void __launch_bounds__(NW * 32) decode_f32_kernel(const __grid_constant__ DecodeParams P) {
+    extern __shared__ __align__(16) float smem[];
+    float *Os = smem;                          // 16 streams*16 heads*128 max
+    float *Ms = Os + NW * 16 * 128;
+    float *Ls = Ms + 16 * NW;
+    float *Sx = Ls + 16 * NW;                  // [NW][R*GP] scores / probabilities
+
+    constexpr int N = R * GP;  // partial dot products per lane per block
+    const uint32_t cta = blockIdx.x;
+    const uint32_t j = locate_job(P, cta);
+    const JobDev &J = P.job[j];
+    const uint32_t local = cta - J.cta_begin;
+    const uint32_t kvh = local / J.n_splits, split = local - kvh * J.n_splits;
+    const uint32_t G = P.group;
+    const uint32_t parts = G / GP;
+    const uint32_t n_streams = NW / parts;
+    const uint32_t lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;
+    const uint32_t part = warp % parts, stream = warp / parts;
+    float *sx = Sx + warp * N;
+
+    float4 q[GP];
+#pragma unroll
+    for (int h = 0; h < GP; h++) {
+        const float4 x = *reinterpret_cast<const float4 *>(
+            J.q + (uint64_t)(kvh * G + part * GP + h) * 128u + lane * 4u);
+        q[h] = make_float4(x.x * P.qscale, x.y * P.qscale, x.z * P.qscale, x.w * P.qscale);
+    }
+    float4 o[GP];
+    float m[GP], l[GP];
+#pragma unroll
+    for (int h = 0; h < GP; h++) {
+        o[h] = make_float4(0.f, 0.f, 0.f, 0.f);
+        m[h] = -INFINITY;
+        l[h] = 0.f;
+    }
+
+    const uint32_t row0 = J.start + split * J.split_rows;
+    const uint32_t row1 = min(row0 + J.split_rows, J.end);
+    const uint32_t cap = J.cap;
+    const uint64_t row_elems = (uint64_t)P.kv_heads * 128u;
+    const float *kb = reinterpret_cast<const float *>(J.k) + kvh * 128u + lane * 4u;
+    const float *vb = reinterpret_cast<const float *>(J.v) + kvh * 128u + lane * 4u;
+
+    for (uint32_t b = row0 + stream * R; b < row1; b += n_streams * R) {
+        const uint32_t sb = b % cap;
+        float4 kf[R], vf[R];
+#pragma unroll
+        for (int r = 0; r < R; r++) {
+            const uint32_t slot = b + r < row1 ? ring_slot(sb, r, cap) : sb;
+            kf[r] = ld_stream_f4(kb + slot * row_elems);
+            vf[r] = ld_stream_f4(vb + slot * row_elems);
+        }
+        float d[N];
+#pragma unroll
+        for (int r = 0; r < R; r++)
+#pragma unroll
+            for (int h = 0; h < GP; h++)
+                d[r * GP + h] = q[h].x * kf[r].x + q[h].y * kf[r].y + q[h].z * kf[r].z +
+                                q[h].w * kf[r].w;
+        // Transposing butterfly: after it, lane holds cnt values whose
+        // original indices are idx0 .. idx0+cnt-1.
+        int cnt = N;
+        uint32_t idx0 = 0;
+#pragma unroll
+        for (int msk = 16; msk >= 1; msk >>= 1) {
+            if ((cnt & 1) == 0) {
+                const int half = cnt >> 1;
+                const bool upper = (lane & msk) != 0;
+#pragma unroll
+                for (int i = 0; i < N / 2; i++) {
+                    if (i < half) {
+                        const float send = upper ? d[i] : d[i + half];
+                        const float keep = upper ? d[i + half] : d[i];
+                        d[i] = keep + __shfl_xor_sync(0xffffffffu, send, msk);
+                    }
+                }
+                if (upper) idx0 += half;
+                cnt = half;
+            } else {
+#pragma unroll
+                for (int i = 0; i < N; i++)
+                    if (i < cnt) d[i] += __shfl_xor_sync(0xffffffffu, d[i], msk);
+            }
+        }
+        // Own scores -> shared, then every lane reads all of them.
+#pragma unroll
+        for (int i = 0; i < N; i++)
+            if (i < cnt) sx[idx0 + i] = d[i];
+        __syncwarp();
+        float sc[N];
+#pragma unroll
+        for (int i = 0; i < N; i += 4) {
+            const float4 x = *reinterpret_cast<const float4 *>(sx + i);
+            sc[i] = x.x;
+            sc[i + 1] = x.y;
+            sc[i + 2] = x.z;
+            sc[i + 3] = x.w;
+        }
+        const uint32_t nvalid = row1 - b;
+#pragma unroll
+        for (int r = 0; r < R; r++)
+            if ((uint32_t)r >= nvalid)
+#pragma unroll
+                for (int h = 0; h < GP; h++) sc[r * GP + h] = -INFINITY;
+#pragma unroll
+        for (int h = 0; h < GP; h++) {
+            float bm = sc[h];
+#pragma unroll
+            for (int r = 1; r < R; r++) bm = fmaxf(bm, sc[r * GP + h]);
+            if (bm > m[h] + kRescaleSlack) {  // uniform across the warp
+                const float alpha = fast_exp2(m[h] - bm);
+                l[h] *= alpha;
+                o[h].x *= alpha;
+                o[h].y *= alpha;
+                o[h].z *= alpha;
+                o[h].w *= alpha;
+                m[h] = bm;
+            }
+        }
+        __syncwarp();
+        // Own probabilities -> shared, then every lane reads all of them.
+#pragma unroll
+        for (int i = 0; i < N; i++)
+            if (i < cnt) {
+                const uint32_t id = idx0 + i;
+                const uint32_t h = id % GP, r = id / GP;
+                float mh = m[0];
+#pragma unroll
+                for (int hh = 1; hh < GP; hh++)
+                    if (h == (uint32_t)hh) mh = m[hh];
+                sx[id] = r < nvalid ? fast_exp2(d[i] - mh) : 0.f;
+            }
+        __syncwarp();
+#pragma unroll
+        for (int i = 0; i < N; i += 4) {
+            const float4 x = *reinterpret_cast<const float4 *>(sx + i);
+            sc[i] = x.x;
+            sc[i + 1] = x.y;
+            sc[i + 2] = x.z;
+            sc[i + 3] = x.w;
+        }
+        __syncwarp();
+#pragma unroll
+        for (int r = 0; r < R; r++)
+#pragma unroll
+            for (int h = 0; h < GP; h++) {
+                const float pv = sc[r * GP + h];
+                l[h] += pv;
+                o[h].x += pv * vf[r].x;
+                o[h].y += pv * vf[r].y;
+                o[h].z += pv * vf[r].z;
+                o[h].w += pv * vf[r].w;
+            }
+    }
+#pragma unroll
+    for (int h = 0; h < GP; h++) {
+        const uint32_t hrow = part * GP + h;
+        *reinterpret_cast<float4 *>(Os + (stream * 16u + hrow) * 128u + lane * 4u) = o[h];
+        if (lane == 0) {
+            Ms[stream * 16u + hrow] = m[h];
+            Ls[stream * 16u + hrow] = l[h];
+        }
+    }
+    finish_cta<NW * 32>(P, J, j, kvh, split, cta, n_streams, GP, Os, Ms, Ls);
+}
+
+// ------------------------------------------------------------ generic kernel
+// Any head_dim <= 256 and any group: one warp per (job, query head), one
+// pass over the rows with an online softmax.  Lane holds dims lane + 32*i.
+struct GenericParams {
+    JobDev job[kMaxJobs];
+    uint32_t n_jobs, q_heads, kv_heads, head_dim;
+    float scale;
+};
+
+template <typename T>
+__device__ __forceinline__ float to_f(T x);
+template <>
+__device__ __forceinline__ float to_f<float>(float x) { return x; }
+template <>
+__device__ __forceinline__ float to_f<__half>(__half x) { return __half2float(x); }
+
+template <typename T>
+__global__ void __launch_bounds__(256) decode_generic_kernel(const __grid_constant__ GenericParams P) {
+    const uint32_t gw = blockIdx.x * 8u + (threadIdx.x >> 5);
+    const uint32_t lane = threadIdx.x & 31u;
+    const uint32_t jj = gw / P.q_heads;
+    if (jj >= P.n_jobs) return;
+    const uint32_t h = gw - jj * P.q_heads;
+    const JobDev &J = P.job[jj];
+    const uint32_t G = P.q_heads / P.kv_heads;
+    const uint32_t kvh = h / G;
+    const uint32_t hd = P.head_dim;
+    const uint64_t row = (uint64_t)P.kv_heads * hd;
+    const T *kc = reinterpret_cast<const T *>(J.k) + (uint64_t)kvh * hd;
+    const T *vc = reinterpret_cast<const T *>(J.v) + (uint64_t)kvh * hd;
+    float q[8], o[8];
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        const uint32_t d = lane + 32u * i;
+        q[i] = d < hd ? J.q[(uint64_t)h * hd + d] * P.scale : 0.f;
+        o[i] = 0.f;
+    }
+    float m = -INFINITY, l = 0.f;
+    for (uint32_t r = J.start; r < J.end; r++) {
+        const uint64_t slot = r % J.cap;
+        float dot = 0.f;
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            const uint32_t d = lane + 32u * i;
+            if (d < hd) dot += q[i] * to_f<T>(kc[slot * row + d]);
+        }
+        for (int msk = 16; msk; msk >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, msk);
+        const float mn = fmaxf(m, dot);
+        const float alpha = exp2f(m - mn), p = exp2f(dot - mn);
+        l = l * alpha + p;
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            const uint32_t d = lane + 32u * i;
+            o[i] = o[i] * alpha + (d < hd ? p * to_f<T>(vc[slot * row + d]) : 0.f);
+        }
+        m = mn;
+    }
+    const float g = J.gate ? sigmoid_dev(J.gate[h]) : 1.0f;
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        const uint32_t d = lane + 32u * i;
+        if (d < hd) J.out[(uint64_t)h * hd + d] = l > 0.f ? o[i] / l * g : 0.f;
+    }
+}
+
+// ------------------------------------------------------------ host side
+static int f32_gp(uint32_t G) {
+    switch (G) {
+        case 1: return 1;
+        case 2: return 2;
+        case 4: return 4;
+        case 8: return 8;
+        case 12: return 6;
+        case 16: return 8;
+        default: return 0;
+    }
+}
+
+constexpr int kNW = 4;  // warps per CTA of the fast kernels
+
+static size_t smem_f16() {
+    return (size_t)(kNW * 16 * 128 + 32 * kNW) * 4 + 2 * 8 * 32 * 16;
+}
+template <int GP, int R>
+static size_t smem_f32() {
+    return (size_t)(kNW * 16 * 128 + 32 * kNW + kNW * R * GP) * 4;
+}
+
+static int launch_generic(const AttnJob *jobs, uint32_t n, uint32_t q_heads, uint32_t kv_heads,
+                          uint32_t head_dim, int dtype, cudaStream_t stream) {
+    if (head_dim > 256)
+        return set_error(SF37KV_EUNSUPPORTED, "attention: head_dim %u > 256", head_dim);
+    for (uint32_t base = 0; base < n; base += kMaxJobs) {
+        GenericParams P;
+        P.n_jobs = 0;
+        P.q_heads = q_heads;
+        P.kv_heads = kv_heads;
+        P.head_dim = head_dim;
+        P.scale = kLog2e / sqrtf((float)head_dim);
+        for (uint32_t i = base; i < n && i < base + kMaxJobs; i++) {
+            const AttnJob &A = jobs[i];
+            JobDev &D = P.job[P.n_jobs++];
+            D = JobDev{A.k, A.v, A.q, A.gate, A.out, A.start, A.end, A.cap, 0, 1, 0};
+        }
+        const uint64_t warps = (uint64_t)P.n_jobs * q_heads;
+        const unsigned grid = (unsigned)((warps + 7) / 8);
+        if (dtype == SF37KV_F32) decode_generic_kernel<float><<<grid, 256, 0, stream>>>(P);
+        else decode_generic_kernel<__half><<<grid, 256, 0, stream>>>(P);
+        g_launches++;
+        if (int rc = check_cuda(cudaGetLastError(), "generic attention launch")) return rc;
+    }
+    return SF37KV_OK;
+}
+
+template <int GP, int R>
+static void launch_f32(const DecodeParams &P, unsigned grid, cudaStream_t stream) {
+    static bool attr = false;
+    const size_t sm = smem_f32<GP, R>();
+    if (!attr) {
+        cudaFuncSetAttribute(decode_f32_kernel<kNW, GP, R>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+        attr = true;
+    }
+    decode_f32_kernel<kNW, GP, R><<<grid, kNW * 32, sm, stream>>>(P);
+}
+
+int attention_jobs(const AttnJob *jobs, uint32_t n, uint32_t q_heads, uint32_t kv_heads,
+                   uint32_t head_dim, int dtype, cudaStream_t stream) {
+    if (dtype != SF37KV_F32 && dtype != SF37KV_F16)
+        return set_error(SF37KV_EINVAL, "attention: unknown cache dtype %d", dtype);
+    if (kv_heads == 0 || q_heads == 0 || q_heads % kv_heads != 0 || head_dim == 0)
+        return set_error(SF37KV_EINVAL, "attention: bad head configuration q=%u kv=%u d=%u",
+                         q_heads, kv_heads, head_dim);
+    for (uint32_t i = 0; i < n; i++) {
+        const AttnJob &A = jobs[i];
+        if (!A.k || !A.v || !A.q || !A.out || A.cap == 0 || A.end < A.start)
+            return set_error(SF37KV_EINVAL, "attention: job %u is invalid", i);
+    }
+    const uint32_t G = q_heads / kv_heads;
+    const bool fast = head_dim == 128 && G <= 16 && (dtype == SF37KV_F16 || f32_gp(G) != 0);
+    if (!fast) return launch_generic(jobs, n, q_heads, kv_heads, head_dim, dtype, stream);
+
+    const int sms = num_sms();
+    for (uint32_t base = 0; base < n; base += kMaxJobs) {
+        const uint32_t m = (n - base) < (uint32_t)kMaxJobs ? (n - base) : (uint32_t)kMaxJobs;
+        uint64_t total = 0;
+        for (uint32_t i = 0; i < m; i++) total += (uint64_t)(jobs[base + i].end - jobs[base + i].start);
+        total *= kv_heads;
+        // Aim for ~3 resident CTAs per SM, 2 waves; never below 128 rows.
+        const uint64_t target = (uint64_t)sms * 6;
+        uint64_t per = (total + target - 1) / target;
+        if (per < 128) per = 128;
+        DecodeParams P;
+        P.n_jobs = m;
+        P.q_heads = q_heads;
+        P.kv_heads = kv_heads;
+        P.group = G;
+        P.part_stride = (G * 130u + 3u) & ~3u;
+        P.qscale = kLog2e / sqrtf(128.0f);
+        uint32_t ctas = 0;
+        bool any_split = false;
+        for (uint32_t i = 0; i < m; i++) {
+            const AttnJob &A = jobs[base + i];
+            const uint32_t rows = A.end - A.start;
+            uint64_t ns = (rows + per - 1) / per;
+            if (ns < 1) ns = 1;
+            if (ns > kMaxSplits) ns = kMaxSplits;
+            uint32_t sr = (uint32_t)((rows + ns - 1) / ns);
+            sr = (sr + 15u) & ~15u;
+            if (sr == 0) sr = 16;
+            ns = (rows + sr - 1) / sr;
+            if (ns < 1) ns = 1;
+            if (ns > 1) any_split = true;
+            JobDev &D = P.job[i];
+            D = JobDev{A.k, A.v, A.q, A.gate, A.out, A.start, A.end, A.cap, sr, (uint32_t)ns, ctas};
+            if ((uint64_t)ctas + ns * kv_heads > 0x7fffffffull)
+                return set_error(SF37KV_EINVAL, "attention: grid too large");
+            ctas += (uint32_t)ns * kv_heads;
+        }
+        P.total_ctas = ctas;
+        Scratch S;
+        if (any_split) {
+            if (int rc = scratch_get((uint64_t)ctas * P.part_stride * 4u, (uint64_t)m * kv_heads, &S))
+                return rc;
+        }
+        P.part = S.part;
+        P.counters = S.counters;
+        if (dtype == SF37KV_F16) {
+            static bool attr = false;
+            if (!attr) {
+                cudaFuncSetAttribute(decode_f16_kernel<kNW>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)smem_f16());
+                attr = true;
+            }
+            decode_f16_kernel<kNW><<<ctas, kNW * 32, smem_f16(), stream>>>(P);
+        } else {
+            switch (G) {
+                case 1: launch_f32<1, 8>(P, ctas, stream); break;
+                case 2: launch_f32<2, 8>(P, ctas, stream); break;
+                case 4: launch_f32<4, 8>(P, ctas, stream); break;
+                case 8: launch_f32<8, 4>(P, ctas, stream); break;
+                case 12: launch_f32<6, 4>(P, ctas, stream); break;
+                default: launch_f32<8, 4>(P, ctas, stream); break;  // 16
+            }
+        }
+        g_launches++;
+        if (int rc = check_cuda(cudaGetLastError(), "attention launch")) return rc;
+    }
+    return SF37KV_OK;
+}
+
+}  // namespace sf37kv
+
+using namespace sf37kv;
+
+// ------------------------------------------------------------ native API
+extern "C" int sf37kv_decode(const sf37kv_decode_layer *layers, uint32_t n_layers, uint32_t q_heads,
+                             uint32_t kv_heads, uint32_t head_dim, int dtype, void *stream) {
+    if (!layers && n_layers) return set_error(SF37KV_EINVAL, "decode: layers is NULL");
+    cudaStream_t s = stream ? (cudaStream_t)stream : current_stream();
+    AppendJob aj[kMaxJobs];
+    AttnJob jobs[kMaxJobs];
+    for (uint32_t base = 0; base < n_layers; base += kMaxJobs) {
+        uint32_t na = 0, m = 0;
+        for (uint32_t i = base; i < n_layers && m < (uint32_t)kMaxJobs; i++, m++) {
+            const sf37kv_decode_layer &L = layers[i];
+            if (L.cache.cap == 0) return set_error(SF37KV_EINVAL, "decode: layer %u cap 0", i);
+            if (L.k_new || L.v_new) {
+                if (!L.k_new || !L.v_new)
+                    return set_error(SF37KV_EINVAL, "decode: layer %u has only one of k_new/v_new", i);
+                aj[na++] = AppendJob{L.cache.k_cache, L.cache.v_cache, L.k_new, L.v_new, L.pos, 1,
+                                     L.cache.cap};
+            }
+            jobs[m] = AttnJob{L.cache.k_cache, L.cache.v_cache, L.q, L.gate, L.out,
+                              start_at(L.pos, L.cache.cap, L.cache.sliding, L.cache.window),
+                              L.pos + 1u, L.cache.cap};
+        }
+        if (na)
+            if (int rc = append_jobs(aj, na, kv_heads * head_dim, dtype, s)) return rc;
+        if (int rc = attention_jobs(jobs, m, q_heads, kv_heads, head_dim, dtype, s)) return rc;
+    }
+    return SF37KV_OK;
+}
+
+// ------------------------------------------------------------ drop-in API
+static int dropin_fail(const char *what) {
+    fprintf(stderr, "sf37: %s failed: %s\n", what, sf37kv_last_error());
+    return 0;
+}
+
+extern "C" int sf37_cuda_attention_decode_heads(sf37_cuda_tensor *out_heads, const sf37_cuda_tensor *q,
+                                                const sf37_cuda_tensor *k_cache,
+                                                const sf37_cuda_tensor *v_cache,
+                                                const sf37_cuda_tensor *head_gate, uint32_t n_cache,
+                                                uint32_t cache_cap, uint32_t q_heads,
+                                                uint32_t kv_heads, uint32_t head_dim, int sliding,
+                                                uint32_t window) {
+    // Validation as sf37_cuda.cu:3015-3024.
+    if (!out_heads || !q || !k_cache || !v_cache || !head_gate || kv_heads == 0 ||
+        q_heads % kv_heads != 0 || n_cache > cache_cap)
+        return 0;
+    const uint64_t q_dim = (uint64_t)q_heads * head_dim, kv_dim = (uint64_t)kv_heads * head_dim;
+    if (out_heads->bytes < q_dim * 4 || q->bytes < q_dim * 4 ||
+        k_cache->bytes < (uint64_t)cache_cap * kv_dim * 4 ||
+        v_cache->bytes < (uint64_t)cache_cap * kv_dim * 4 || head_gate->bytes < (uint64_t)q_heads * 4)
+        return 0;
+    uint32_t start = 0;
+    if (sliding && n_cache > window) start = n_cache - window;
+    AttnJob job{k_cache->ptr, v_cache->ptr, (const float *)q->ptr, (const float *)head_gate->ptr,
+                (float *)out_heads->ptr, start, n_cache, cache_cap};
+    if (attention_jobs(&job, 1, q_heads, kv_heads, head_dim, SF37KV_F32, current_stream()))
+        return dropin_fail("attention_decode_heads");
+    return 1;
+}
+
+extern "C" int sf37_cuda_attention_decode_heads_at(sf37_cuda_tensor *out_heads, const sf37_cuda_tensor *q,
+                                                   const sf37_cuda_tensor *k_cache,
+                                                   const sf37_cuda_tensor *v_cache,
+                                                   const sf37_cuda_tensor *head_gate, uint32_t pos,
+                                                   uint32_t cache_cap, uint32_t q_heads,
+                                                   uint32_t kv_heads, uint32_t head_dim, int sliding,
+                                                   uint32_t window) {
+    // Validation as sf37_cuda.cu:3091-3103.
+    if (!out_heads || !q || !k_cache || !v_cache || !head_gate || cache_cap == 0 ||
+        kv_heads == 0 || q_heads % kv_heads != 0 || head_dim == 0)
+        return 0;
+    const uint64_t q_dim = (uint64_t)q_heads * head_dim, kv_dim = (uint64_t)kv_heads * head_dim;
+    if (out_heads->bytes < q_dim * 4 || q->bytes < q_dim * 4 ||
+        k_cache->bytes < (uint64_t)cache_cap * kv_dim * 4 ||
+        v_cache->bytes < (uint64_t)cache_cap * kv_dim * 4 || head_gate->bytes < (uint64_t)q_heads * 4)
+        return 0;
+    AttnJob job{k_cache->ptr, v_cache->ptr, (const float *)q->ptr, (const float *)head_gate->ptr,
+                (float *)out_heads->ptr, start_at(pos, cache_cap, sliding, window), pos + 1u, cache_cap};
+    if (attention_jobs(&job, 1, q_heads, kv_heads, head_dim, SF37KV_F32, current_stream()))
+        return dropin_fail("attention_decode_heads_at");
+    return 1;
+}
+
+__global__ static void gqa_single_token_kernel(float *out, const float *v, const float *gate,
+                                               uint32_t q_heads, uint32_t kv_heads, uint32_t hd) {
+    const uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (uint64_t)q_heads * hd) return;
+    const uint32_t h = (uint32_t)(i / hd), d = (uint32_t)(i - (uint64_t)h * hd);
+    const uint32_t kvh = h / (q_heads / kv_heads);
+    out[i] = v[(uint64_t)kvh * hd + d] * sigmoid_dev(gate[h]);
+}
+
+// sf37_cuda.cu:2333-2367.
+extern "C" int sf37_cuda_gqa_single_token_heads(sf37_cuda_tensor *out_heads, const sf37_cuda_tensor *v,
+                                                const sf37_cuda_tensor *head_gate, uint32_t q_heads,
+                                                uint32_t kv_heads, uint32_t head_dim) {
+    if (!out_heads || !v || !head_gate || kv_heads == 0 || q_heads % kv_heads != 0) return 0;
+    const uint64_t q_dim = (uint64_t)q_heads * head_dim, kv_dim = (uint64_t)kv_heads * head_dim;
+    if (out_heads->bytes < q_dim * 4 || v->bytes < kv_dim * 4 || head_gate->bytes < (uint64_t)q_heads * 4)
+        return 0;
+    if (q_dim == 0) return 1;
+    gqa_single_token_kernel<<<(unsigned)((q_dim + 255) / 256), 256, 0, current_stream()>>>(
+        (float *)out_heads->ptr, (const float *)v->ptr, (const float *)head_gate->ptr, q_heads,
+        kv_heads, head_dim);
+    g_launches++;
+    if (check_cuda(cudaGetLastError(), "gqa single-token launch")) return dropin_fail("gqa_single_token_heads");
+    return 1;
+}

@@ -1,0 +1,466 @@
+// Snapshot KV sections: gather (+ int8-grouped encode) and the inverse
+// scatter (+ decode), bit-exact with the reference's CUDA-backend formats:
+//
+//   raw snapshot  (sf37_session_save_snapshot, sf37.c:7298-7320): per
+//     position r of a layer, the K row then the V row as f32;
+//   disk payload  (sf37_session_save_payload, sf37.c:6980-7010): the same
+//     rows, each encoded by payload_encode_kv_row_i8_grouped
+//     (sf37.c:6633-6659): per group of `group` elements one f32 scale, then
+//     all int8 values.
+//
+// Position r lives in ring slot (first_pos + r) % cap.  One CTA per encoded
+// row; a thread handles 8 consecutive elements (one 16-byte f16 load or two
+// f32 loads), so a 64-element group is 8 lanes and its max is 3 shuffles.
+// These kernels are HBM- (device buffer) or link- (mapped host buffer) bound.
+#include <cstdio>
+#include <cstring>
+
+#include "kv_internal.cuh"
+#include "../../include/sf37_cuda_kv.h"
+
+namespace sf37kv {
+
+extern unsigned long long g_launches;
+
+struct PackJob {
+    const void *k, *v;  // caches (unpack writes through them)
+    uint32_t cap, first_pos, rows;
+    uint64_t offset;    // byte offset of the layer section in the buffer
+    uint32_t row_begin; // prefix sum of rows*2 (encoded rows)
+};
+
+struct PackParams {
+    PackJob job[kMaxJobs];
+    uint32_t n_jobs;
+    uint32_t kv_dim, group, groups;
+    uint64_t row_bytes;
+    int variant;
+};
+
+__device__ __forceinline__ uint32_t locate(const PackParams &P, uint32_t row) {
+    uint32_t j = 0;
+    while (j + 1 < P.n_jobs && P.job[j + 1].row_begin <= row) j++;
+    return j;
+}
+
+// Loads 8 consecutive cache elements as f32.
+template <typename T>
+__device__ __forceinline__ void load8(const T *p, float (&x)[8]);
+template <>
+__device__ __forceinline__ void load8<float>(const float *p, float (&x)[8]) {
+    const float4 a = __ldcs(reinterpret_cast<const float4 *>(p));
+    const float4 b = __ldcs(reinterpret_cast<const float4 *>(p) + 1);
+    x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w;
+    x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
+}
+template <>
+__device__ __forceinline__ void load8<__half>(const __half *p, float (&x)[8]) {
+    const uint4 u = __ldcs(reinterpret_cast<const uint4 *>(p));
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(&w[i]));
+        x[2 * i] = f.x;
+        x[2 * i + 1] = f.y;
+    }
+}
+
+template <typename T>
+__device__ __forceinline__ void store8(T *p, const float (&x)[8]);
+template <>
+__device__ __forceinline__ void store8<float>(float *p, const float (&x)[8]) {
+    reinterpret_cast<float4 *>(p)[0] = make_float4(x[0], x[1], x[2], x[3]);
+    reinterpret_cast<float4 *>(p)[1] = make_float4(x[4], x[5], x[6], x[7]);
+}
+template <>
+__device__ __forceinline__ void store8<__half>(__half *p, const float (&x)[8]) {
+    uint32_t w[4];
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const __half2 h = __floats2half2_rn(x[2 * i], x[2 * i + 1]);
+        w[i] = *reinterpret_cast<const uint32_t *>(&h);
+    }
+    *reinterpret_cast<uint4 *>(p) = make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+// Stores n bytes (n = 8) with the widest stores the address allows.
+__device__ __forceinline__ void store_bytes8(uint8_t *dst, uint32_t lo, uint32_t hi) {
+    const uintptr_t a = (uintptr_t)dst;
+    if ((a & 7u) == 0) {
+        *reinterpret_cast<uint2 *>(dst) = make_uint2(lo, hi);
+    } else if ((a & 3u) == 0) {
+        reinterpret_cast<uint32_t *>(dst)[0] = lo;
+        reinterpret_cast<uint32_t *>(dst)[1] = hi;
+    } else {
+#pragma unroll
+        for (int i = 0; i < 4; i++) dst[i] = (uint8_t)(lo >> (8 * i));
+#pragma unroll
+        for (int i = 0; i < 4; i++) dst[4 + i] = (uint8_t)(hi >> (8 * i));
+    }
+}
+
+// Row r of the job's section: K row (kv = 0) or V row (kv = 1) at ring slot.
+template <typename T, int FMT>
+__global__ void __launch_bounds__(128) pack_kernel(uint8_t *dst, const __grid_constant__ PackParams P) {
+    const uint32_t row = blockIdx.x;
+    const uint32_t j = locate(P, row);
+    const PackJob &J = P.job[j];
+    const uint32_t local = row - J.row_begin;
+    const uint32_t r = local >> 1, kv = local & 1u;
+    const uint64_t slot = (uint64_t)((J.first_pos + r) % J.cap);
+    const T *src = reinterpret_cast<const T *>(kv ? J.v : J.k) + slot * P.kv_dim;
+    uint8_t *out = dst + J.offset + (uint64_t)local * P.row_bytes;
+    const uint32_t tpg = P.group >> 3;  // threads per group
+    for (uint32_t e0 = threadIdx.x * 8u; e0 < P.kv_dim; e0 += blockDim.x * 8u) {
+        float x[8];
+        load8<T>(src + e0, x);
+        if (FMT == SF37KV_FMT_RAW_F32) {
+            uint8_t *o = out + (uint64_t)e0 * 4u;
+            if (((uintptr_t)o & 15u) == 0) {
+                reinterpret_cast<float4 *>(o)[0] = make_float4(x[0], x[1], x[2], x[3]);
+                reinterpret_cast<float4 *>(o)[1] = make_float4(x[4], x[5], x[6], x[7]);
+            } else {
+                for (int i = 0; i < 8; i += 2)
+                    store_bytes8(o + 4 * i, __float_as_uint(x[i]), __float_as_uint(x[i + 1]));
+            }
+        } else {
+            // payload_encode_kv_row_i8_grouped: max |x| over finite values.
+            float m = 0.f;
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+                const float a = fabsf(x[i]);
+                if (isfinite(a) && a > m) m = a;
+            }
+            // Groups are whole and lane-aligned, so a lane's partners are active.
+            const unsigned act = __activemask();
+            for (uint32_t s = 1; s < tpg; s <<= 1) m = fmaxf(m, __shfl_xor_sync(act, m, s));
+            float scale, inv;
+            if (m > 0.f) {
+                if (P.variant == 1) {
+                    // -ffast-math form: m * (1/127), x * (1/scale), IEEE-rounded.
+                    scale = __fmul_rn(m, 1.0f / 127.0f);
+                    inv = __frcp_rn(scale);
+                } else {
+                    scale = __fdiv_rn(m, 127.0f);
+                    inv = 0.f;
+                }
+            } else {
+                scale = 1.0f;
+                inv = 1.0f;
+            }
+            const uint32_t grp = e0 / P.group;
+            if ((threadIdx.x & (tpg - 1u)) == 0) {
+                uint8_t *so = out + (uint64_t)grp * 4u;
+                const uint32_t u = __float_as_uint(scale);
+                if (((uintptr_t)so & 3u) == 0) *reinterpret_cast<uint32_t *>(so) = u;
+                else
+                    for (int i = 0; i < 4; i++) so[i] = (uint8_t)(u >> (8 * i));
+            }
+            uint32_t q[8];
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+                float v = isfinite(x[i]) ? x[i] : 0.f;
+                const float y = (P.variant == 1 || m <= 0.f) ? __fmul_rn(v, inv) : __fdiv_rn(v, scale);
+                int qi = __float2int_rn(y);
+                qi = qi > 127 ? 127 : (qi < -127 ? -127 : qi);
+                q[i] = (uint32_t)(qi & 0xff);
+            }
+            const uint32_t lo = q[0] | (q[1] << 8) | (q[2] << 16) | (q[3] << 24);
+            const uint32_t hi = q[4] | (q[5] << 8) | (q[6] << 16) | (q[7] << 24);
+            store_bytes8(out + (uint64_t)P.groups * 4u + e0, lo, hi);
+        }
+    }
+}
+
+template <typename T, int FMT>
+__global__ void __launch_bounds__(128) unpack_kernel(const uint8_t *src, const __grid_constant__ PackParams P) {
+    const uint32_t row = blockIdx.x;
+    const uint32_t j = locate(P, row);
+    const PackJob &J = P.job[j];
+    const uint32_t local = row - J.row_begin;
+    const uint32_t r = local >> 1, kv = local & 1u;
+    const uint64_t slot = (uint64_t)((J.first_pos + r) % J.cap);
+    T *dst = const_cast<T *>(reinterpret_cast<const T *>(kv ? J.v : J.k)) + slot * P.kv_dim;
+    const uint8_t *in = src + J.offset + (uint64_t)local * P.row_bytes;
+    for (uint32_t e0 = threadIdx.x * 8u; e0 < P.kv_dim; e0 += blockDim.x * 8u) {
+        float x[8];
+        if (FMT == SF37KV_FMT_RAW_F32) {
+            const uint8_t *p = in + (uint64_t)e0 * 4u;
+            if (((uintptr_t)p & 15u) == 0) {
+                const float4 a = __ldcs(reinterpret_cast<const float4 *>(p));
+                const float4 b = __ldcs(reinterpret_cast<const float4 *>(p) + 1);
+                x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w;
+                x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
+            } else {
+                for (int i = 0; i < 8; i++) {
+                    uint32_t u = 0;
+                    for (int bb = 0; bb < 4; bb++) u |= (uint32_t)p[4 * i + bb] << (8 * bb);
+                    x[i] = __uint_as_float(u);
+                }
+            }
+        } else {
+            // payload_decode_kv_row_i8_grouped (sf37.c:6661-6674): q * scale.
+            const uint32_t grp = e0 / P.group;
+            const uint8_t *sp = in + (uint64_t)grp * 4u;
+            uint32_t su = 0;
+            for (int bb = 0; bb < 4; bb++) su |= (uint32_t)sp[bb] << (8 * bb);
+            const float scale = __uint_as_float(su);
+            const uint8_t *qp = in + (uint64_t)P.groups * 4u + e0;
+#pragma unroll
+            for (int i = 0; i < 8; i++) x[i] = __fmul_rn((float)(int8_t)qp[i], scale);
+        }
+        store8<T>(dst + e0, x);
+    }
+}
+
+static uint64_t row_bytes_of(uint32_t kv_dim, int fmt, uint32_t group) {
+    if (fmt == SF37KV_FMT_RAW_F32) return (uint64_t)kv_dim * 4u;
+    const uint64_t groups = (kv_dim + group - 1u) / group;
+    return groups * 4u + kv_dim;
+}
+
+static int validate(uint32_t kv_dim, int dtype, int fmt, uint32_t group) {
+    if (dtype != SF37KV_F32 && dtype != SF37KV_F16)
+        return set_error(SF37KV_EINVAL, "pack: unknown cache dtype %d", dtype);
+    if (fmt != SF37KV_FMT_RAW_F32 && fmt != SF37KV_FMT_I8_GROUPED)
+        return set_error(SF37KV_EINVAL, "pack: unknown format %d", fmt);
+    if (kv_dim == 0 || kv_dim % 8u)
+        return set_error(SF37KV_EUNSUPPORTED, "pack: kv_dim %u is not a multiple of 8", kv_dim);
+    if (fmt == SF37KV_FMT_I8_GROUPED &&
+        (group < 8 || group > 256 || (group & (group - 1u)) || kv_dim % group))
+        return set_error(SF37KV_EUNSUPPORTED,
+                         "pack: group %u must be a power of two in [8, 256] dividing kv_dim", group);
+    return SF37KV_OK;
+}
+
+// Launches pack (dir = 0) or unpack (dir = 1) over the layers.
+static int launch_layers(void *buf, const sf37kv_pack_layer *layers, uint32_t n, uint32_t kv_dim,
+                         int dtype, int fmt, uint32_t group, int variant, int dir,
+                         cudaStream_t stream) {
+    if (int rc = validate(kv_dim, dtype, fmt, group)) return rc;
+    if (!buf && n) return set_error(SF37KV_EINVAL, "pack: buffer is NULL");
+    const uint64_t rb = row_bytes_of(kv_dim, fmt, group);
+    for (uint32_t base = 0; base < n; base += kMaxJobs) {
+        PackParams P;
+        P.n_jobs = 0;
+        P.kv_dim = kv_dim;
+        P.group = fmt == SF37KV_FMT_I8_GROUPED ? group : 8;
+        P.groups = fmt == SF37KV_FMT_I8_GROUPED ? kv_dim / group : 0;
+        P.row_bytes = rb;
+        P.variant = variant;
+        uint64_t rows = 0;
+        for (uint32_t i = base; i < n && i < base + kMaxJobs; i++) {
+            const sf37kv_pack_layer &L = layers[i];
+            if (!L.cache.k_cache || !L.cache.v_cache || L.cache.cap == 0)
+                return set_error(SF37KV_EINVAL, "pack: layer %u has a null cache or cap 0", i);
+            if (L.rows > L.cache.cap)
+                return set_error(SF37KV_EINVAL, "pack: layer %u rows %u exceed cap %u", i, L.rows,
+                                 L.cache.cap);
+            if ((((uintptr_t)L.cache.k_cache | (uintptr_t)L.cache.v_cache) & 15u) != 0)
+                return set_error(SF37KV_EINVAL, "pack: layer %u caches must be 16-byte aligned", i);
+            if (L.rows == 0) continue;
+            PackJob &J = P.job[P.n_jobs++];
+            J = PackJob{L.cache.k_cache, L.cache.v_cache, L.cache.cap, L.first_pos, L.rows,
+                        L.offset, (uint32_t)rows};
+            rows += 2ull * L.rows;
+            if (rows > 0x7fffffffull) return set_error(SF37KV_EINVAL, "pack: too many rows");
+        }
+        if (P.n_jobs == 0) continue;
+        const unsigned grid = (unsigned)rows;
+        const unsigned threads = kv_dim / 8u < 128u ? ((kv_dim / 8u + 31u) & ~31u) : 128u;
+        uint8_t *b = (uint8_t *)buf;
+#define SF37_PACK_LAUNCH(T, F)                                                         \
+    do {                                                                               \
+        if (dir == 0) pack_kernel<T, F><<<grid, threads, 0, stream>>>(b, P);          \
+        else unpack_kernel<T, F><<<grid, threads, 0, stream>>>(b, P);                 \
+    } while (0)
+        if (dtype == SF37KV_F32) {
+            if (fmt == SF37KV_FMT_RAW_F32) SF37_PACK_LAUNCH(float, SF37KV_FMT_RAW_F32);
+            else SF37_PACK_LAUNCH(float, SF37KV_FMT_I8_GROUPED);
+        } else {
+            if (fmt == SF37KV_FMT_RAW_F32) SF37_PACK_LAUNCH(__half, SF37KV_FMT_RAW_F32);
+            else SF37_PACK_LAUNCH(__half, SF37KV_FMT_I8_GROUPED);
+        }
+#undef SF37_PACK_LAUNCH
+        g_launches++;
+        if (int rc = check_cuda(cudaGetLastError(), dir == 0 ? "pack launch" : "unpack launch"))
+            return rc;
+    }
+    return SF37KV_OK;
+}
+
+// ---------------------------------------------------------------- host staging
+// Two device staging buffers and a copy stream, created on first use and
+// kept for the process (freed by sf37_cuda_cleanup via staging_release()).
+constexpr uint64_t kStageBytes = 64ull << 20;
+static void *g_stage[2] = {nullptr, nullptr};
+static cudaStream_t g_copy_stream = nullptr, g_work_stream = nullptr;
+static cudaEvent_t g_ev_packed[2], g_ev_copied[2], g_ev_start;
+
+static int staging_init() {
+    if (g_stage[0]) return SF37KV_OK;
+    for (int i = 0; i < 2; i++)
+        if (int rc = check_cuda(cudaMalloc(&g_stage[i], kStageBytes), "staging alloc")) return rc;
+    if (int rc = check_cuda(cudaStreamCreateWithFlags(&g_copy_stream, cudaStreamNonBlocking), "stream"))
+        return rc;
+    if (int rc = check_cuda(cudaStreamCreateWithFlags(&g_work_stream, cudaStreamNonBlocking), "stream"))
+        return rc;
+    for (int i = 0; i < 2; i++) {
+        cudaEventCreateWithFlags(&g_ev_packed[i], cudaEventDisableTiming);
+        cudaEventCreateWithFlags(&g_ev_copied[i], cudaEventDisableTiming);
+    }
+    cudaEventCreateWithFlags(&g_ev_start, cudaEventDisableTiming);
+    return check_cuda(cudaGetLastError(), "staging events");
+}
+
+// Splits each layer's section into chunks of at most kStageBytes and runs
+// pack -> D2H (dir 0) or H2D -> unpack (dir 1) with double buffering.
+static int host_pipeline(void *host, const sf37kv_pack_layer *layers, uint32_t n, uint32_t kv_dim,
+                         int dtype, int fmt, uint32_t group, int variant, int dir) {
+    if (int rc = validate(kv_dim, dtype, fmt, group)) return rc;
+    if (!host && n) return set_error(SF37KV_EINVAL, "pack: host buffer is NULL");
+    if (int rc = staging_init()) return rc;
+    const uint64_t rb = row_bytes_of(kv_dim, fmt, group);
+    const uint64_t chunk_rows = kStageBytes / (2 * rb);
+    if (chunk_rows == 0) return set_error(SF37KV_EUNSUPPORTED, "pack: row larger than staging");
+    // Order after everything already queued on the library stream.
+    cudaEventRecord(g_ev_start, current_stream());
+    cudaStreamWaitEvent(g_work_stream, g_ev_start, 0);
+    cudaStreamWaitEvent(g_copy_stream, g_ev_start, 0);
+    int buf = 0;
+    bool used[2] = {false, false};
+    for (uint32_t i = 0; i < n; i++) {
+        const sf37kv_pack_layer &L = layers[i];
+        for (uint64_t r0 = 0; r0 < L.rows; r0 += chunk_rows) {
+            const uint32_t nr = (uint32_t)((L.rows - r0) < chunk_rows ? (L.rows - r0) : chunk_rows);
+            sf37kv_pack_layer c = L;
+            c.first_pos = L.first_pos + (uint32_t)r0;
+            c.rows = nr;
+            c.offset = 0;
+            const uint64_t bytes = 2ull * nr * rb;
+            uint8_t *h = (uint8_t *)host + L.offset + 2ull * r0 * rb;
+            if (dir == 0) {
+                if (used[buf]) cudaStreamWaitEvent(g_work_stream, g_ev_copied[buf], 0);
+                if (int rc = launch_layers(g_stage[buf], &c, 1, kv_dim, dtype, fmt, group, variant, 0,
+                                           g_work_stream))
+                    return rc;
+                cudaEventRecord(g_ev_packed[buf], g_work_stream);
+                cudaStreamWaitEvent(g_copy_stream, g_ev_packed[buf], 0);
+                if (int rc = check_cuda(cudaMemcpyAsync(h, g_stage[buf], bytes, cudaMemcpyDeviceToHost,
+                                                        g_copy_stream), "pack D2H"))
+                    return rc;
+                cudaEventRecord(g_ev_copied[buf], g_copy_stream);
+            } else {
+                if (used[buf]) cudaStreamWaitEvent(g_copy_stream, g_ev_packed[buf], 0);
+                if (int rc = check_cuda(cudaMemcpyAsync(g_stage[buf], h, bytes, cudaMemcpyHostToDevice,
+                                                        g_copy_stream), "unpack H2D"))
+                    return rc;
+                cudaEventRecord(g_ev_copied[buf], g_copy_stream);
+                cudaStreamWaitEvent(g_work_stream, g_ev_copied[buf], 0);
+                if (int rc = launch_layers(g_stage[buf], &c, 1, kv_dim, dtype, fmt, group, variant, 1,
+                                           g_work_stream))
+                    return rc;
+                cudaEventRecord(g_ev_packed[buf], g_work_stream);
+            }
+            used[buf] = true;
+            buf ^= 1;
+        }
+    }
+    if (int rc = check_cuda(cudaStreamSynchronize(g_copy_stream), "pack copy sync")) return rc;
+    if (int rc = check_cuda(cudaStreamSynchronize(g_work_stream), "pack work sync")) return rc;
+    // Later work on the library stream must see restored caches.
+    return SF37KV_OK;
+}
+
+void staging_release() {
+    for (int i = 0; i < 2; i++)
+        if (g_stage[i]) {
+            cudaFree(g_stage[i]);
+            g_stage[i] = nullptr;
+        }
+}
+
+}  // namespace sf37kv
+
+using namespace sf37kv;
+
+extern "C" uint64_t sf37kv_row_bytes(uint32_t kv_dim, int fmt, uint32_t group) {
+    return row_bytes_of(kv_dim, fmt, group);
+}
+
+extern "C" int sf37kv_pack(void *dst, const sf37kv_pack_layer *layers, uint32_t n_layers,
+                           uint32_t kv_dim, int dtype, int fmt, uint32_t group, int variant,
+                           void *stream) {
+    return launch_layers(dst, layers, n_layers, kv_dim, dtype, fmt, group, variant, 0,
+                         stream ? (cudaStream_t)stream : current_stream());
+}
+
+extern "C" int sf37kv_unpack(const void *src, const sf37kv_pack_layer *layers, uint32_t n_layers,
+                             uint32_t kv_dim, int dtype, int fmt, uint32_t group, void *stream) {
+    return launch_layers(const_cast<void *>(src), layers, n_layers, kv_dim, dtype, fmt, group, 1, 1,
+                         stream ? (cudaStream_t)stream : current_stream());
+}
+
+extern "C" int sf37kv_pack_to_host(void *host_dst, const sf37kv_pack_layer *layers, uint32_t n_layers,
+                                   uint32_t kv_dim, int dtype, int fmt, uint32_t group, int variant) {
+    return host_pipeline(host_dst, layers, n_layers, kv_dim, dtype, fmt, group, variant, 0);
+}
+
+extern "C" int sf37kv_unpack_from_host(const void *host_src, const sf37kv_pack_layer *layers,
+                                       uint32_t n_layers, uint32_t kv_dim, int dtype, int fmt,
+                                       uint32_t group) {
+    return host_pipeline(const_cast<void *>(host_src), layers, n_layers, kv_dim, dtype, fmt, group, 1,
+                         1);
+}
+
+// ---------------------------------------------------------------- drop-in
+static int dropin_pack(void *host, const sf37_cuda_tensor *k, const sf37_cuda_tensor *v,
+                       uint32_t first_pos, uint32_t rows, uint32_t cap, uint32_t kv_dim, int fmt,
+                       uint32_t group, int variant, int dir, const char *what) {
+    if (!host || !k || !v || cap == 0 || kv_dim == 0 || rows > cap) return 0;
+    const uint64_t need = (uint64_t)cap * kv_dim * 4u;
+    if (k->bytes < need || v->bytes < need) return 0;
+    sf37kv_pack_layer L;
+    memset(&L, 0, sizeof(L));
+    L.cache.k_cache = k->ptr;
+    L.cache.v_cache = v->ptr;
+    L.cache.cap = cap;
+    L.first_pos = first_pos;
+    L.rows = rows;
+    L.offset = 0;
+    if (host_pipeline(host, &L, 1, kv_dim, SF37KV_F32, fmt, group, variant, dir)) {
+        fprintf(stderr, "sf37: %s failed: %s\n", what, sf37kv_last_error());
+        return 0;
+    }
+    return 1;
+}
+
+extern "C" int sf37_cuda_kv_pack_rows_f32(void *host_dst, const sf37_cuda_tensor *k_cache,
+                                          const sf37_cuda_tensor *v_cache, uint32_t first_pos,
+                                          uint32_t rows, uint32_t cache_cap, uint32_t kv_dim) {
+    return dropin_pack(host_dst, k_cache, v_cache, first_pos, rows, cache_cap, kv_dim,
+                       SF37KV_FMT_RAW_F32, 64, 1, 0, "kv pack f32");
+}
+
+extern "C" int sf37_cuda_kv_unpack_rows_f32(const void *host_src, sf37_cuda_tensor *k_cache,
+                                            sf37_cuda_tensor *v_cache, uint32_t first_pos,
+                                            uint32_t rows, uint32_t cache_cap, uint32_t kv_dim) {
+    return dropin_pack(const_cast<void *>(host_src), k_cache, v_cache, first_pos, rows, cache_cap,
+                       kv_dim, SF37KV_FMT_RAW_F32, 64, 1, 1, "kv unpack f32");
+}
+
+extern "C" int sf37_cuda_kv_pack_rows_i8g(void *host_dst, const sf37_cuda_tensor *k_cache,
+                                          const sf37_cuda_tensor *v_cache, uint32_t first_pos,
+                                          uint32_t rows, uint32_t cache_cap, uint32_t kv_dim,
+                                          uint32_t group, int variant) {
+    return dropin_pack(host_dst, k_cache, v_cache, first_pos, rows, cache_cap, kv_dim,
+                       SF37KV_FMT_I8_GROUPED, group, variant, 0, "kv pack i8g");
+}
+
+extern "C" int sf37_cuda_kv_unpack_rows_i8g(const void *host_src, sf37_cuda_tensor *k_cache,
+                                            sf37_cuda_tensor *v_cache, uint32_t first_pos,
+                                            uint32_t rows, uint32_t cache_cap, uint32_t kv_dim,
+                                            uint32_t group) {
+    return dropin_pack(const_cast<void *>(host_src), k_cache, v_cache, first_pos, rows, cache_cap,
+                       kv_dim, SF37KV_FMT_I8_GROUPED, group, 1, 1, "kv unpack i8g");
+}

@@ -1,0 +1,71 @@
+"""Generates the golden fixtures in this directory from the REFERENCE's own
+CPU code (oracle/_ref/libsf37ref.so, compiled from the reference sources with
+its Makefile flags by `make -C oracle ref`).  Run in the development
+container where the reference tree exists:
+
+    python tests/golden/make_golden.py
+
+Fixtures (all inputs are regenerable from the seeds in sf37_b200.synth):
+  payload_rows.npz  16 N(0,1)*3 rows + the reference self-test pattern row +
+                    a zero row, and their int8-grouped encodings (group 64)
+  cfg1_decode.npz   BASELINE config 1 (2048 f16-valued rows + 1 appended
+                    fp32 row, 64 Q / 8 KV heads, d 128): attention_decode
+                    output without and with the sigmoid gate
+  sliding_decode.npz 96 Q heads (group 12), 600 rows, sliding window 512
+  kv_push.npz       kv_cache_push of 6 rows into a capacity-4 linear cache
+"""
+import os
+import sys
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+sys.path.insert(0, ROOT)
+import oracle  # noqa: E402
+from sf37_b200 import synth  # noqa: E402
+
+OUT = os.path.dirname(os.path.abspath(__file__))
+
+
+def main():
+    assert oracle.ref_available(), "build oracle/_ref first: make -C oracle ref"
+    # payload rows
+    rows = synth.normal(101, (16, 1024)) * np.float32(3.0)
+    pat = ((np.arange(1024) % 97).astype(np.int32) - 48).astype(np.float32) / np.float32(13.0)
+    rows = np.vstack([rows, pat[None], np.zeros((1, 1024), np.float32)]).astype(np.float32)
+    enc = oracle.ref_payload_encode_rows(rows)
+    dec = oracle.ref_payload_decode_rows(enc, 1024)
+    np.savez_compressed(os.path.join(OUT, "payload_rows.npz"), rows=rows, enc=enc, dec=dec)
+
+    # config 1
+    k, v, k_new, v_new, q, gate = synth.cfg1_inputs(0)
+    cap = 2049
+    kc = np.zeros((cap, 1024), np.float32)
+    vc = np.zeros((cap, 1024), np.float32)
+    n = oracle.ref_kv_cache_push(kc, vc, cap, 0, k.astype(np.float32), v.astype(np.float32))
+    n = oracle.ref_kv_cache_push(kc, vc, cap, n, k_new[None], v_new[None])
+    out_nogate = oracle.ref_attention_decode(q, kc, vc, n, cap, 64, 0, None)
+    out_gate = oracle.ref_attention_decode(q, kc, vc, n, cap, 64, 0, gate)
+    np.savez_compressed(os.path.join(OUT, "cfg1_decode.npz"), out_nogate=out_nogate,
+                        out_gate=out_gate, n_live=n)
+
+    # sliding layer of the real model: 96 query heads, window 512
+    ks = synth.normal(201, (600, 1024))
+    vs = synth.normal(202, (600, 1024))
+    qs = synth.normal(203, (96, 128))
+    gs = synth.normal(204, (96,))
+    out_s = oracle.ref_attention_decode(qs, ks, vs, 600, 600, 96, 1, gs)
+    np.savez_compressed(os.path.join(OUT, "sliding_decode.npz"), out=out_s)
+
+    # kv_cache_push wrap behaviour (memmove when full)
+    kp = synth.normal(301, (6, 1024))
+    vp = synth.normal(302, (6, 1024))
+    kc4 = np.zeros((4, 1024), np.float32)
+    vc4 = np.zeros((4, 1024), np.float32)
+    n4 = oracle.ref_kv_cache_push(kc4, vc4, 4, 0, kp, vp)
+    np.savez_compressed(os.path.join(OUT, "kv_push.npz"), k=kc4, v=vc4, n=n4)
+    print("golden fixtures written to", OUT)
+
+
+if __name__ == "__main__":
+    main()

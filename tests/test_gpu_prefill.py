@@ -1,0 +1,51 @@
+"""GPU parity: chunked-prefill attention (sf37_cuda.cu:3163-3317) vs the
+oracle (cpu_attention_prefill_ref, tests/test_sf37_cuda_ops.cu:859-905)."""
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from sf37_b200 import kv, synth
+from tests.gpu_util import dev, f16_cache, host
+from tests.helpers import assert_close
+
+pytestmark = pytest.mark.gpu
+
+
+def test_reference_prefill_case():
+    # tests/test_sf37_cuda_ops.cu:1112-1150: n_tok 3, pos0 2, cap 8, 8/2 heads, tol 6e-5
+    n_tok, pos0, qh, kvh, hd, cap = 3, 2, 8, 2, 128, 8
+    qd, kd = qh * hd, kvh * hd
+    q = (((np.arange(n_tok * qd) % 37) - 18) * 0.006).astype(np.float32).reshape(n_tok, qd)
+    k = (((np.arange(n_tok * kd) % 31) - 15) * 0.005).astype(np.float32).reshape(n_tok, kd)
+    v = (((np.arange(n_tok * kd) % 29) - 14) * 0.007).astype(np.float32).reshape(n_tok, kd)
+    g = (((np.arange(n_tok * qh) % 11) - 5) * 0.09).astype(np.float32).reshape(n_tok, qh)
+    kc = (((np.arange(cap * kd) % 23) - 11) * 0.004).astype(np.float32).reshape(cap, kd)
+    vc = (((np.arange(cap * kd) % 19) - 9) * 0.008).astype(np.float32).reshape(cap, kd)
+    dkc, dvc = dev(kc), dev(vc)
+    out = torch.empty(n_tok, qd, device="cuda")
+    assert kv.store_kv_cache_batch(dkc, dvc, dev(k), dev(v), pos0, n_tok, cap, kd)
+    assert kv.attention_prefill_heads(out, dev(q), dkc, dvc, dev(g), pos0, n_tok, cap, qh, kvh, hd, 0, 512)
+    oracle.store_kv_rows(kc, vc, k, v, pos0, n_tok, cap, kd)
+    want = oracle.attention_prefill(q, kc, vc, g, pos0, n_tok, cap, qh, kvh, hd)
+    assert_close(host(out).reshape(n_tok, qh, hd), want, atol=6e-5, rtol=0)
+
+
+@pytest.mark.parametrize("qtype", ["f32", "bf16"])
+@pytest.mark.parametrize("pos0,n_tok,cap,sliding", [(0, 64, 64, 0), (300, 130, 1024, 0),
+                                                    (1000, 200, 768, 1), (5, 1, 16, 0)])
+def test_native_prefill_f16(qtype, pos0, n_tok, cap, sliding):
+    qh, kvh, hd = 64, 8, 128
+    kd = kvh * hd
+    kc, kref = f16_cache(synth.normal(11 + pos0, (cap, kd)))
+    vc, vref = f16_cache(synth.normal(12 + pos0, (cap, kd)))
+    qf = synth.normal(13 + pos0, (n_tok, qh, hd))
+    tq = dev(qf)
+    if qtype == "bf16":
+        tq = tq.to(torch.bfloat16)
+        qf = tq.float().cpu().numpy()
+    g = synth.normal(14, (n_tok, qh))
+    out = torch.empty(n_tok, qh, hd, device="cuda")
+    kv.prefill(kc, vc, cap, tq, dev(g), out, pos0, n_tok, qh, kvh, hd, kv.F16, sliding=sliding)
+    want = oracle.attention_prefill(qf, kref, vref, g, pos0, n_tok, cap, qh, kvh, hd, sliding, 512)
+    assert_close(host(out), want)

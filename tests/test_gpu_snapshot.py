@@ -1,0 +1,120 @@
+"""GPU parity: snapshot KV pack/restore, bit-exact with the reference
+formats (raw f32 rows, sf37.c:7298-7320; int8-grouped payload rows,
+sf37.c:6980-7010 with payload_encode_kv_row_i8_grouped 6633-6659)."""
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from sf37_b200 import kv, synth
+from tests.gpu_util import dev, f16_cache, host
+
+pytestmark = pytest.mark.gpu
+
+
+def _layers(dtype, specs, kd=1024, scale=1.0):
+    out = []
+    for i, (cap, first, rows) in enumerate(specs):
+        kf = synth.normal(900 + i, (cap, kd)) * np.float32(scale)
+        vf = synth.normal(950 + i, (cap, kd)) * np.float32(scale)
+        if dtype == kv.F16:
+            kc, _ = f16_cache(kf)
+            vc, _ = f16_cache(vf)
+            hk, hv = oracle.f32_to_f16_bits(kf), oracle.f32_to_f16_bits(vf)
+        else:
+            kc, vc, hk, hv = dev(kf), dev(vf), kf, vf
+        out.append(dict(k_cache=kc, v_cache=vc, cap=cap, first_pos=first, rows=rows, hk=hk, hv=hv))
+    return out
+
+
+SPECS = [(64, 0, 64), (512, 70000 - 512, 512), (100, 37, 80), (8, 3, 0), (300, 1000, 1)]
+
+
+@pytest.mark.parametrize("dtype", [kv.F32, kv.F16])
+@pytest.mark.parametrize("fmt", [kv.FMT_RAW, kv.FMT_I8G])
+def test_pack_bit_exact(dtype, fmt):
+    Ls = _layers(dtype, SPECS)
+    arr, total = kv.pack_layers_desc(Ls, 1024, fmt)
+    buf = torch.empty(total, dtype=torch.uint8, device="cuda")
+    kv.pack(buf, arr, 1024, dtype, fmt)
+    got = host(buf)
+    want = np.concatenate([oracle.pack_layer(L["hk"], L["hv"], L["first_pos"], L["rows"], L["cap"], 1024,
+                                             fmt) for L in Ls])
+    assert np.array_equal(got, want)
+    if fmt == kv.FMT_I8G and oracle.ref_available():
+        # the same rows through the reference's own compiled encoder
+        rows = np.concatenate([oracle.f16_bits_to_f32(np.stack([L["hk"][(L["first_pos"] + r) % L["cap"]],
+                                                                L["hv"][(L["first_pos"] + r) % L["cap"]]]))
+                               if dtype == kv.F16 else
+                               np.stack([L["hk"][(L["first_pos"] + r) % L["cap"]],
+                                         L["hv"][(L["first_pos"] + r) % L["cap"]]])
+                               for L in Ls for r in range(L["rows"])])
+        assert np.array_equal(got.reshape(-1, 1088), oracle.ref_payload_encode_rows(rows))
+
+
+@pytest.mark.parametrize("dtype", [kv.F32, kv.F16])
+@pytest.mark.parametrize("fmt", [kv.FMT_RAW, kv.FMT_I8G])
+def test_unpack_inverse(dtype, fmt):
+    Ls = _layers(dtype, SPECS)
+    arr, total = kv.pack_layers_desc(Ls, 1024, fmt)
+    src = np.frombuffer(synth.splitmix64(5, (total + 7) // 8).tobytes()[:total], np.uint8).copy()
+    if fmt == kv.FMT_RAW:
+        # finite f32 values
+        src = (synth.normal(6, (total // 4,))).view(np.uint8).copy()
+    else:
+        rb = 1088
+        rows = synth.normal(7, (total // rb, 1024))
+        src = oracle.payload_encode_rows(rows).reshape(-1)
+    kv.unpack(dev(src), arr, 1024, dtype, fmt)
+    torch.cuda.synchronize()
+    for L in Ls:
+        hk, hv = L["hk"].copy(), L["hv"].copy()
+        off = arr[Ls.index(L)].offset
+        sec = src[off: off + 2 * L["rows"] * kv.row_bytes(1024, fmt)]
+        oracle.unpack_layer(sec, hk, hv, L["first_pos"], L["rows"], L["cap"], 1024, fmt)
+        gk = L["k_cache"].cpu()
+        gv = L["v_cache"].cpu()
+        if dtype == kv.F16:
+            gk = gk.view(torch.int16).numpy().view(np.uint16)
+            gv = gv.view(torch.int16).numpy().view(np.uint16)
+        else:
+            gk, gv = gk.numpy(), gv.numpy()
+        assert np.array_equal(gk, hk) and np.array_equal(gv, hv)
+
+
+@pytest.mark.parametrize("fmt", [kv.FMT_RAW, kv.FMT_I8G])
+def test_pack_to_host_roundtrip(fmt):
+    Ls = _layers(kv.F16, [(5000, 123, 5000), (512, 9000, 512)])
+    arr, total = kv.pack_layers_desc(Ls, 1024, fmt)
+    hbuf = np.empty(total, np.uint8)
+    kv.pack_to_host(hbuf.ctypes.data, arr, 1024, kv.F16, fmt)
+    want = np.concatenate([oracle.pack_layer(L["hk"], L["hv"], L["first_pos"], L["rows"], L["cap"], 1024,
+                                             fmt) for L in Ls])
+    assert np.array_equal(hbuf, want)
+    if fmt == kv.FMT_RAW:
+        # restore into zeroed caches reproduces the f16 caches exactly
+        for L in Ls:
+            L["k_cache"].zero_()
+            L["v_cache"].zero_()
+        kv.unpack_from_host(hbuf.ctypes.data, arr, 1024, kv.F16, fmt)
+        for L in Ls:
+            assert np.array_equal(L["k_cache"].cpu().view(torch.int16).numpy().view(np.uint16), L["hk"])
+
+
+@pytest.mark.parametrize("fmt", [kv.FMT_RAW, kv.FMT_I8G])
+def test_dropin_pack_rows(fmt):
+    cap, first, rows = 520, 600, 500
+    kf = synth.normal(41, (cap, 1024))
+    vf = synth.normal(42, (cap, 1024))
+    dk, dv = dev(kf), dev(vf)
+    rb = kv.row_bytes(1024, fmt)
+    hbuf = np.empty(2 * rows * rb, np.uint8)
+    assert kv.kv_pack_rows(hbuf, dk, dv, first, rows, cap, 1024, fmt)
+    assert np.array_equal(hbuf, oracle.pack_layer(kf, vf, first, rows, cap, 1024, fmt))
+    dk.zero_()
+    dv.zero_()
+    assert kv.kv_unpack_rows(hbuf, dk, dv, first, rows, cap, 1024, fmt)
+    hk = np.zeros_like(kf)
+    hv = np.zeros_like(vf)
+    oracle.unpack_layer(hbuf, hk, hv, first, rows, cap, 1024, fmt)
+    assert np.array_equal(host(dk), hk) and np.array_equal(host(dv), hv)
