@@ -29,7 +29,8 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 METRIC = "decode-attn KV-read GB/s (% of 8 TB/s) and tokens/s at 32K ctx, 1/2/4/8 B200"
-LAYERS, QH, KVH, HD, CTX = 48, 64, 8, 128, 32768
+QH, KVH, HD, CTX = 64, 8, 128, 32768
+LAYERS = 48  # --layers overrides (profiling runs use a small stack)
 
 
 def _peaks():
@@ -267,12 +268,13 @@ def run_ours(args, rank, world):
     barrier()
     n0 = kv.launch_count()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(dev.index) as clk:
-        ev0.record(stream)
-        for i in range(warm, warm + steps):
-            step(i)
-        ev1.record(stream)
-        barrier()
+    clk = ClockSampler(dev.index).__enter__()
+    time.sleep(0.3)  # let nvidia-smi start before the timed region
+    ev0.record(stream)
+    for i in range(warm, warm + steps):
+        step(i)
+    ev1.record(stream)
+    barrier()
     launches = kv.launch_count() - n0
     ms = ev0.elapsed_time(ev1) / steps
     if world > 1:
@@ -283,20 +285,29 @@ def run_ours(args, rank, world):
     kv_bytes_step = LAYERS * rows_mean * KVH * HD * 2 * 2  # whole job, f16 K+V
     tok_s = 1000.0 / ms
 
+    if args.quick:  # profiling runs: the timed steps only
+        clk.__exit__()
+        if rank == 0:
+            print(json.dumps({"quick": True, "layers": LAYERS, "ms_per_step": ms, "value": tok_s,
+                              "gpu_launches": launches}), flush=True)
+        return
+
     # Roofline leg: the attention kernel alone (no append), one launch per
     # call, CUDA events on the launching stream around each launch.
     att_desc = descs(CTX + warm + steps - 1, with_append=False)
     for _ in range(3):
         kv.decode(att_desc, qh_l, kvh_l, HD, kv.F16, stream)
     torch.cuda.synchronize(dev)
+    # at least ~0.5 s of launches so the clock samples cover the kernel
+    n_roof = max(steps, int(500.0 / max(ms, 0.05)))
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-           for _ in range(steps)]
+           for _ in range(n_roof)]
     for a, b in evs:
         a.record(stream)
         kv.decode(att_desc, qh_l, kvh_l, HD, kv.F16, stream)
         b.record(stream)
     torch.cuda.synchronize(dev)
-    att_ms = sum(a.elapsed_time(b) for a, b in evs) / steps
+    att_ms = sum(a.elapsed_time(b) for a, b in evs) / len(evs)
     rows_att = CTX + warm + steps
     att_bytes = LAYERS * (rows_att * kd * 2 * 2 + qh_l * HD * 4 * 2 + qh_l * 4)
     peak, peak_kind = _peaks()
@@ -344,6 +355,7 @@ def run_ours(args, rank, world):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_ms = float(t.item())
 
+    clk.__exit__()
     if rank != 0:
         return
     cpu = cpu_baseline(CTX + 1) if world == 1 and not args.no_cpu else None
@@ -383,7 +395,13 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
+    ap.add_argument("--quick", action="store_true",
+                    help="timed steps only (no roofline/e2e/cpu legs): for profiler runs")
+    ap.add_argument("--layers", type=int, default=48,
+                    help="layers in the synthetic stack (48 = BASELINE config 2)")
     args = ap.parse_args()
+    global LAYERS
+    LAYERS = args.layers
     if args.warmup < 3:
         args.warmup = 3
     world = int(os.environ.get("WORLD_SIZE", "1"))

@@ -47,6 +47,9 @@ __global__ void __launch_bounds__(256) append_kernel(const __grid_constant__ App
     while (j + 1 < P.n_jobs && P.row_begin[j + 1] <= row) j++;
     const AppendJob &J = P.job[j];
     const uint32_t t = row - P.row_begin[j];
+    // With n_tok > cap several tokens share a slot; the last one wins, as in
+    // a sequential append (kv_cache_push order).  Earlier ones write nothing.
+    if ((uint64_t)t + J.cap < J.n_tok) return;
     const uint64_t slot = (uint64_t)((J.pos0 + t) % J.cap);
     const uint32_t kv_dim = P.kv_dim;
     T *kc = reinterpret_cast<T *>(J.k_cache) + slot * kv_dim;

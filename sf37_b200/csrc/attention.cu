@@ -35,6 +35,7 @@
 // Anything else (head_dim != 128, other G): a generic warp-per-head kernel.
 #include <cfloat>
 #include <cstdio>
+#include <cstdlib>
 #include <cmath>
 
 #include "kv_internal.cuh"
@@ -255,8 +256,8 @@ __device__ void finish_cta(const DecodeParams &P, const JobDev &J, uint32_t j, u
 //    thread (g,t) loads rows b+2t, b+2t+1, b+2t+8, b+2t+9, chunks g and g+8,
 //    and interleaves the two rows of each B register with one PRMT.
 //    Output dim of (n-tile jt, column c) = jt<8 ? 8c+jt : 64+8c+jt-8.
-template <int NW>
-__global__ void __launch_bounds__(NW * 32, 3) decode_f16_kernel(const __grid_constant__ DecodeParams P) {
+template <int NW, int MINB>
+__global__ void __launch_bounds__(NW * 32, MINB) decode_f16_kernel(const __grid_constant__ DecodeParams P) {
     extern __shared__ __align__(16) float smem[];
     float *Os = smem;                                  // [NW streams][16 heads][128]
     float *Ms = Os + NW * 16 * 128;                    // 16*NW
@@ -759,10 +760,12 @@ int attention_jobs(const AttnJob *jobs, uint32_t n, uint32_t q_heads, uint32_t k
         uint64_t total = 0;
         for (uint32_t i = 0; i < m; i++) total += (uint64_t)(jobs[base + i].end - jobs[base + i].start);
         total *= kv_heads;
-        // Aim for ~3 resident CTAs per SM, 2 waves; never below 128 rows.
-        const uint64_t target = (uint64_t)sms * 6;
+        // Rows per CTA: about 8 waves of resident CTAs for big batches (keeps
+        // the last partial wave small), at least 256 rows per CTA.
+        const uint64_t target = (uint64_t)sms * 3 * 8;
         uint64_t per = (total + target - 1) / target;
-        if (per < 128) per = 128;
+        if (per < 256) per = 256;
+        if (const char *e = getenv("SF37KV_SPLIT_ROWS")) per = strtoull(e, nullptr, 10) ? strtoull(e, nullptr, 10) : per;
         DecodeParams P;
         P.n_jobs = m;
         P.q_heads = q_heads;
@@ -799,13 +802,17 @@ int attention_jobs(const AttnJob *jobs, uint32_t n, uint32_t q_heads, uint32_t k
         P.part = S.part;
         P.counters = S.counters;
         if (dtype == SF37KV_F16) {
-            static bool attr = false;
-            if (!attr) {
-                cudaFuncSetAttribute(decode_f16_kernel<kNW>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+            static int minb = -1;
+            if (minb < 0) {
+                const char *e = getenv("SF37KV_DECODE_MINB");
+                minb = (e && atoi(e) == 2) ? 2 : 3;
+                cudaFuncSetAttribute(decode_f16_kernel<kNW, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      (int)smem_f16());
-                attr = true;
+                cudaFuncSetAttribute(decode_f16_kernel<kNW, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)smem_f16());
             }
-            decode_f16_kernel<kNW><<<ctas, kNW * 32, smem_f16(), stream>>>(P);
+            if (minb == 2) decode_f16_kernel<kNW, 2><<<ctas, kNW * 32, smem_f16(), stream>>>(P);
+            else decode_f16_kernel<kNW, 3><<<ctas, kNW * 32, smem_f16(), stream>>>(P);
         } else {
             switch (G) {
                 case 1: launch_f32<1, 8>(P, ctas, stream); break;
