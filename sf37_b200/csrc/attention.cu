@@ -36,6 +36,7 @@
 #include <cfloat>
 #include <cstdio>
 #include <cstdlib>
+#include <cstring>
 #include <cmath>
 
 #include "kv_internal.cuh"
@@ -442,6 +443,223 @@ __global__ void __launch_bounds__(NW * 32, MINB) decode_f16_kernel(const __grid_
     finish_cta<NW * 32>(P, J, j, kvh, split, cta, n_streams, 8, Os, Ms, Ls);
 }
 
+// ------------------------------------------------------------ f16 kernel, cp.async pipeline
+// Same math and register fragments as decode_f16_kernel, but K/V blocks are
+// staged through a per-warp ring of S shared-memory stages filled with
+// 16-byte cp.async copies, so S-1 blocks (8 KB each) per warp are in flight
+// without holding registers.  Warps never wait on each other inside the
+// loop (per-warp cp.async groups + __syncwarp).
+//
+// Stage layout: K tile then V tile, each [16 rows][16 chunks of 16 B]; chunk
+// ch of row r sits at slot ch ^ swz(r), swz(r) = ((r&1)<<2) ^ (((r>>1)&3)<<1),
+// which makes both fragment read patterns (K: rows g/g+8, chunks 4c+t; V:
+// rows 2t+{0,1,8,9}, chunks g/g+8) bank-conflict free for 128-bit loads.
+__device__ __forceinline__ uint32_t swz(uint32_t r) { return ((r & 1u) << 2) ^ (((r >> 1) & 3u) << 1); }
+
+__device__ __forceinline__ void cp_async16(uint32_t smem_addr, const void *gptr) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr), "l"(gptr));
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N)); }
+
+__device__ __forceinline__ uint4 lds128(uint32_t addr) {
+    uint4 r;
+    asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "r"(addr));
+    return r;
+}
+
+template <int NW, int S>
+__global__ void __launch_bounds__(NW * 32, 1) decode_f16_pipe_kernel(const __grid_constant__ DecodeParams P) {
+    extern __shared__ __align__(128) uint8_t smem_raw[];
+    constexpr uint32_t kStage = 8192;  // 16 rows x 256 B for K, then V
+    uint4 *Qs = reinterpret_cast<uint4 *>(smem_raw + NW * S * kStage);  // [n_mt][8 kk][32 lanes]
+    // Epilogue arrays alias the stage buffers once the loop is done.
+    float *Os = reinterpret_cast<float *>(smem_raw);
+    float *Ms = Os + NW * 16 * 128;
+    float *Ls = Ms + 16 * NW;
+
+    const uint32_t cta = blockIdx.x;
+    const uint32_t j = locate_job(P, cta);
+    const JobDev &J = P.job[j];
+    const uint32_t local = cta - J.cta_begin;
+    const uint32_t kvh = local / J.n_splits, split = local - kvh * J.n_splits;
+    const uint32_t G = P.group;
+    const uint32_t n_mt = (G + 7u) >> 3;
+    const uint32_t n_streams = NW / n_mt;
+    const uint32_t lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;
+    const uint32_t g = lane >> 2, t = lane & 3u;
+    const uint32_t mt = warp % n_mt, stream = warp / n_mt;
+
+    if (warp < n_mt) {
+        const uint32_t hg = warp * 8u + g;
+        const bool valid = hg < G;
+        const float *qp = J.q + (uint64_t)(kvh * G + (valid ? hg : 0u)) * 128u;
+#pragma unroll
+        for (int kk = 0; kk < 8; kk++) {
+            uint32_t r[4];
+#pragma unroll
+            for (int half = 0; half < 2; half++) {
+                const int w = 2 * kk + half;
+                const uint32_t dim = (4u * (w >> 2) + t) * 8u + 2u * (w & 3);
+                float2 x = valid ? *reinterpret_cast<const float2 *>(qp + dim) : make_float2(0.f, 0.f);
+                x.x *= P.qscale;
+                x.y *= P.qscale;
+                const __half2 hi = __floats2half2_rn(x.x, x.y);
+                const float2 hf = __half22float2(hi);
+                const __half2 lo = __floats2half2_rn(x.x - hf.x, x.y - hf.y);
+                r[half * 2] = h2_as_u32(hi);
+                r[half * 2 + 1] = h2_as_u32(lo);
+            }
+            Qs[(warp * 8 + kk) * 32 + lane] = make_uint4(r[0], r[1], r[2], r[3]);
+        }
+    }
+    __syncthreads();
+
+    const uint32_t row0 = J.start + split * J.split_rows;
+    const uint32_t row1 = min(row0 + J.split_rows, J.end);
+    const uint32_t cap = J.cap;
+    const uint64_t row_bytes = (uint64_t)P.kv_heads * 256u;
+    const char *kbase = reinterpret_cast<const char *>(J.k) + kvh * 256u;
+    const char *vbase = reinterpret_cast<const char *>(J.v) + kvh * 256u;
+    const uint32_t qs_addr = (uint32_t)__cvta_generic_to_shared(Qs + mt * 8 * 32 + lane);
+    const uint32_t wbuf = (uint32_t)__cvta_generic_to_shared(smem_raw) + warp * S * kStage;
+
+    const uint32_t bstep = n_streams * 16u;
+    const uint32_t b_first = row0 + stream * 16u;
+    const uint32_t nblk = b_first < row1 ? (row1 - b_first + bstep - 1) / bstep : 0u;
+
+    // Copy block `it` (rows b_first + it*bstep ...) into stage it % S.
+    // Lane copies chunks c = lane + 32*i (i < 8) of K and of V: row c>>4, chunk c&15.
+    auto issue = [&](uint32_t it) {
+        if (it < nblk) {
+            const uint32_t bb = b_first + it * bstep;
+            const uint32_t sb = bb % cap;
+            const uint32_t st = wbuf + (it % S) * kStage;
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+                const uint32_t c = lane + 32u * i;
+                const uint32_t r = c >> 4, ch = c & 15u;
+                const uint32_t slot = bb + r < row1 ? ring_slot(sb, r, cap) : sb;
+                const uint64_t go = (uint64_t)slot * row_bytes + ch * 16u;
+                const uint32_t so = r * 256u + ((ch ^ swz(r)) * 16u);
+                cp_async16(st + so, kbase + go);
+                cp_async16(st + 4096u + so, vbase + go);
+            }
+        }
+        cp_async_commit();
+    };
+
+    float o[16][4];
+#pragma unroll
+    for (int i = 0; i < 16; i++) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+    float m_run = -INFINITY, l_run = 0.f;
+
+#pragma unroll
+    for (int s = 0; s < S - 1; s++) issue(s);
+
+    for (uint32_t it = 0; it < nblk; it++) {
+        cp_async_wait<S - 2>();
+        __syncwarp();
+        issue(it + S - 1);
+        const uint32_t b = b_first + it * bstep;
+        const uint32_t st = wbuf + (it % S) * kStage;
+
+        // S = q K^T for rows b .. b+15.
+        float s[2][4];
+#pragma unroll
+        for (int i = 0; i < 2; i++) s[i][0] = s[i][1] = s[i][2] = s[i][3] = 0.f;
+#pragma unroll
+        for (int c = 0; c < 4; c++) {
+            const uint4 a0 = lds128(qs_addr + (2 * c) * 512);
+            const uint4 a1 = lds128(qs_addr + (2 * c + 1) * 512);
+#pragma unroll
+            for (int i = 0; i < 2; i++) {
+                const uint32_t r = 8u * i + g;
+                const uint4 u = lds128(st + r * 256u + (((4u * c + t) ^ swz(r)) * 16u));
+                mma16816(s[i], a0.x, a0.y, a0.z, a0.w, u.x, u.y);
+                mma16816(s[i], a1.x, a1.y, a1.z, a1.w, u.z, u.w);
+            }
+        }
+
+        float sc[2][2];
+#pragma unroll
+        for (int i = 0; i < 2; i++)
+#pragma unroll
+            for (int e = 0; e < 2; e++) {
+                const uint32_t r = b + 8u * i + 2u * t + e;
+                sc[i][e] = r < row1 ? s[i][e] + s[i][e + 2] : -INFINITY;
+            }
+        float mx = fmaxf(fmaxf(sc[0][0], sc[0][1]), fmaxf(sc[1][0], sc[1][1]));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+        if (__any_sync(0xffffffffu, mx > m_run + kRescaleSlack)) {
+            const float m_new = fmaxf(m_run, mx);
+            const float alpha = fast_exp2(m_run - m_new);
+            l_run *= alpha;
+#pragma unroll
+            for (int i = 0; i < 16; i++) {
+                o[i][0] *= alpha;
+                o[i][1] *= alpha;
+                o[i][2] *= alpha;
+                o[i][3] *= alpha;
+            }
+            m_run = m_new;
+        }
+        uint32_t pa[4];
+#pragma unroll
+        for (int i = 0; i < 2; i++) {
+            const float p0 = fast_exp2(sc[i][0] - m_run), p1 = fast_exp2(sc[i][1] - m_run);
+            l_run += p0 + p1;
+            const __half2 hi = __floats2half2_rn(p0, p1);
+            const float2 hf = __half22float2(hi);
+            const __half2 lo = __floats2half2_rn(p0 - hf.x, p1 - hf.y);
+            pa[2 * i] = h2_as_u32(hi);
+            pa[2 * i + 1] = h2_as_u32(lo);
+        }
+        // V fragments: rows 2t, 2t+1, 2t+8, 2t+9; chunks g and g+8.
+        uint4 vr[4][2];
+#pragma unroll
+        for (int x = 0; x < 4; x++) {
+            const uint32_t r = 2u * t + (x & 1) + (x >> 1) * 8u;
+            const uint32_t base = st + 4096u + r * 256u;
+            vr[x][0] = lds128(base + ((g ^ swz(r)) * 16u));
+            vr[x][1] = lds128(base + (((g + 8u) ^ swz(r)) * 16u));
+        }
+#pragma unroll
+        for (int jt = 0; jt < 16; jt++) {
+            const int u = jt >> 3, e = jt & 7, w = e >> 1;
+            const uint32_t sel = (e & 1) ? 0x7632u : 0x5410u;
+            const uint32_t b0 = prmt(word_of(vr[0][u], w), word_of(vr[1][u], w), sel);
+            const uint32_t b1 = prmt(word_of(vr[2][u], w), word_of(vr[3][u], w), sel);
+            mma16816(o[jt], pa[0], pa[1], pa[2], pa[3], b0, b1);
+        }
+        __syncwarp();
+    }
+    cp_async_wait<0>();
+    __syncthreads();  // stage buffers become the epilogue arrays
+
+    l_run += __shfl_xor_sync(0xffffffffu, l_run, 1);
+    l_run += __shfl_xor_sync(0xffffffffu, l_run, 2);
+    const uint32_t hrow = mt * 8u + g;
+    float *Ow = Os + (stream * 16u + hrow) * 128u;
+    if (hrow < G) {
+#pragma unroll
+        for (int jt = 0; jt < 16; jt++)
+#pragma unroll
+            for (int e = 0; e < 2; e++) {
+                const uint32_t c = 2u * t + e;
+                const uint32_t dim = jt < 8 ? 8u * c + jt : 64u + 8u * c + (jt - 8);
+                Ow[dim] = o[jt][e] + o[jt][e + 2];
+            }
+        if (t == 0) {
+            Ms[stream * 16u + hrow] = m_run;
+            Ls[stream * 16u + hrow] = l_run;
+        }
+    }
+    finish_cta<NW * 32>(P, J, j, kvh, split, cta, n_streams, 8, Os, Ms, Ls);
+}
+
 // ------------------------------------------------------------ f32 kernel
 // Warp = (part, stream): part p owns heads [p*GP, (p+1)*GP) of the group,
 // stream s takes row blocks s, s+n_streams, ...  Lane holds dims 4*lane..+3.
@@ -695,6 +913,7 @@ constexpr int kNW = 4;  // warps per CTA of the fast kernels
 static size_t smem_f16() {
     return (size_t)(kNW * 16 * 128 + 32 * kNW) * 4 + 2 * 8 * 32 * 16;
 }
+static size_t smem_pipe(int nw, int stages) { return (size_t)nw * stages * 8192 + 2 * 8 * 32 * 16; }
 template <int GP, int R>
 static size_t smem_f32() {
     return (size_t)(kNW * 16 * 128 + 32 * kNW + kNW * R * GP) * 4;
@@ -782,8 +1001,8 @@ int attention_jobs(const AttnJob *jobs, uint32_t n, uint32_t q_heads, uint32_t k
             if (ns < 1) ns = 1;
             if (ns > kMaxSplits) ns = kMaxSplits;
             uint32_t sr = (uint32_t)((rows + ns - 1) / ns);
-            sr = (sr + 15u) & ~15u;
-            if (sr == 0) sr = 16;
+            sr = (sr + 127u) & ~127u;
+            if (sr == 0) sr = 128;
             ns = (rows + sr - 1) / sr;
             if (ns < 1) ns = 1;
             if (ns > 1) any_split = true;
@@ -802,17 +1021,30 @@ int attention_jobs(const AttnJob *jobs, uint32_t n, uint32_t q_heads, uint32_t k
         P.part = S.part;
         P.counters = S.counters;
         if (dtype == SF37KV_F16) {
-            static int minb = -1;
-            if (minb < 0) {
-                const char *e = getenv("SF37KV_DECODE_MINB");
-                minb = (e && atoi(e) == 2) ? 2 : 3;
+            // SF37KV_DECODE_KERNEL selects a variant for tuning runs:
+            // pipe4 (default: 4 warps x 3 cp.async stages, two CTAs per SM),
+            // pipe8 (8 warps x 3 stages, one CTA per SM), reg2 / reg3 (register
+            // prefetch, 2 or 3 CTAs per SM).  Measured on B200 (48 layers, 32K
+            // rows): pipe4 6.25 TB/s, pipe8 5.97, reg2 5.09.
+            static int variant = -1;
+            if (variant < 0) {
+                const char *e = getenv("SF37KV_DECODE_KERNEL");
+                variant = !e ? 1 : !strcmp(e, "pipe8") ? 0 : !strcmp(e, "reg2") ? 2 : !strcmp(e, "reg3") ? 3 : 1;
                 cudaFuncSetAttribute(decode_f16_kernel<kNW, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      (int)smem_f16());
                 cudaFuncSetAttribute(decode_f16_kernel<kNW, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      (int)smem_f16());
+                cudaFuncSetAttribute(decode_f16_pipe_kernel<8, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)smem_pipe(8, 3));
+                cudaFuncSetAttribute(decode_f16_pipe_kernel<4, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)smem_pipe(4, 3));
             }
-            if (minb == 2) decode_f16_kernel<kNW, 2><<<ctas, kNW * 32, smem_f16(), stream>>>(P);
-            else decode_f16_kernel<kNW, 3><<<ctas, kNW * 32, smem_f16(), stream>>>(P);
+            switch (variant) {
+                case 1: decode_f16_pipe_kernel<4, 3><<<ctas, 128, smem_pipe(4, 3), stream>>>(P); break;
+                case 2: decode_f16_kernel<kNW, 2><<<ctas, kNW * 32, smem_f16(), stream>>>(P); break;
+                case 3: decode_f16_kernel<kNW, 3><<<ctas, kNW * 32, smem_f16(), stream>>>(P); break;
+                default: decode_f16_pipe_kernel<8, 3><<<ctas, 256, smem_pipe(8, 3), stream>>>(P); break;
+            }
         } else {
             switch (G) {
                 case 1: launch_f32<1, 8>(P, ctas, stream); break;

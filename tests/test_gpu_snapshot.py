@@ -57,7 +57,6 @@ def test_pack_bit_exact(dtype, fmt):
 def test_unpack_inverse(dtype, fmt):
     Ls = _layers(dtype, SPECS)
     arr, total = kv.pack_layers_desc(Ls, 1024, fmt)
-    src = np.frombuffer(synth.splitmix64(5, (total + 7) // 8).tobytes()[:total], np.uint8).copy()
     if fmt == kv.FMT_RAW:
         # finite f32 values
         src = (synth.normal(6, (total // 4,))).view(np.uint8).copy()
@@ -67,9 +66,9 @@ def test_unpack_inverse(dtype, fmt):
         src = oracle.payload_encode_rows(rows).reshape(-1)
     kv.unpack(dev(src), arr, 1024, dtype, fmt)
     torch.cuda.synchronize()
-    for L in Ls:
+    for i, L in enumerate(Ls):
         hk, hv = L["hk"].copy(), L["hv"].copy()
-        off = arr[Ls.index(L)].offset
+        off = arr[i].offset
         sec = src[off: off + 2 * L["rows"] * kv.row_bytes(1024, fmt)]
         oracle.unpack_layer(sec, hk, hv, L["first_pos"], L["rows"], L["cap"], 1024, fmt)
         gk = L["k_cache"].cpu()
