@@ -312,7 +312,7 @@ def run_ours(args, rank, world):
     att_bytes = LAYERS * (rows_att * kd * 2 * 2 + qh_l * HD * 4 * 2 + qh_l * 4)
     peak, peak_kind = _peaks()
     achieved = att_bytes / (att_ms * 1e-3) / 1e9
-    traffic = _traffic_from_profiles("decode_f16_cfg2.md")
+    traffic = _traffic_from_profiles("decode_f16_pipe_cfg2.md") if LAYERS == 48 else None
 
     # End-to-end leg through the C ABI with host buffers: pinned host inputs
     # (q, gate, new K/V rows) copied in, outputs copied out, every step.
@@ -374,7 +374,7 @@ def run_ours(args, rank, world):
                    "l2": "no flush needed: 6.4 GB of KV per step >> 126 MB L2"},
         "kv_read_GBps": kv_bytes_step / (ms * 1e-3) / 1e9,
         "kv_read_frac_of_8TBps": kv_bytes_step / (ms * 1e-3) / 8e12,
-        "roofline": {"bound": "hbm", "kernel": "decode_f16_kernel", "achieved": achieved,
+        "roofline": {"bound": "hbm", "kernel": "decode_f16_pipe_kernel", "achieved": achieved,
                      "peak": peak, "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / peak,
                      "traffic": traffic, "launch_ms": att_ms,
                      "algorithmic_bytes_per_launch": att_bytes},
