@@ -84,6 +84,25 @@ int sf37kv_decode(const sf37kv_decode_layer *layers, uint32_t n_layers,
                   uint32_t q_heads, uint32_t kv_heads, uint32_t head_dim,
                   int dtype, void *stream);
 
+/* Allocation-free variant of sf37kv_decode(); no counterpart in the
+ * reference.  For callers that cannot call cudaMalloc while decoding (an
+ * engine whose memory pool owns the whole device, allocations frozen after
+ * start-up, or a loop that cannot afford the device synchronization of a
+ * first-use allocation): the split-K partials and counters live in a fixed
+ * device array of SF37KV_NOALLOC_SCRATCH_BYTES compiled into the library,
+ * which every GPU that loads the library holds until exit.  Same arguments
+ * and results as sf37kv_decode(), with these limits: head_dim 128,
+ * q_heads/kv_heads <= 16 (f32 caches: 1, 2, 4, 8, 12 or 16), at most 64
+ * layers per call, layers x kv_heads <= 4096; other sizes are rejected with
+ * SF37KV_EINVAL / SF37KV_EUNSUPPORTED and nothing is launched.  The first
+ * call on a device looks up the array's address (make it before any stream
+ * capture).  All calls share the array: calls that overlap on the GPU race,
+ * so serialize them. */
+#define SF37KV_NOALLOC_SCRATCH_BYTES (8u * 1024u * 1024u + 16384u)
+int sf37kv_decode_noalloc(const sf37kv_decode_layer *layers, uint32_t n_layers,
+                          uint32_t q_heads, uint32_t kv_heads, uint32_t head_dim,
+                          int dtype, void *stream);
+
 /* Append n_tok rows per layer: row t -> slot (pos0 + t) % cap
  * (store_kv_cache_batch_kernel, sf37_cuda.cu:6355-6372). */
 typedef struct {

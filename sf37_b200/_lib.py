@@ -70,6 +70,8 @@ SIGNATURES = {
     "sf37kv_set_stream": (c_int, [c_vp]),
     "sf37kv_get_stream": (c_vp, []),
     "sf37kv_decode": (c_int, [ctypes.POINTER(DecodeLayer), c_u32, c_u32, c_u32, c_u32, c_int, c_vp]),
+    "sf37kv_decode_noalloc": (c_int, [ctypes.POINTER(DecodeLayer), c_u32, c_u32, c_u32, c_u32, c_int,
+                                      c_vp]),
     "sf37kv_append": (c_int, [ctypes.POINTER(AppendLayer), c_u32, c_u32, c_int, c_vp]),
     "sf37kv_prefill": (c_int, [ctypes.POINTER(Cache), c_vp, c_int, c_vp, c_vp, c_u32, c_u32,
                                c_u32, c_u32, c_u32, c_int, c_vp]),

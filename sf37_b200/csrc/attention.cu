@@ -1173,3 +1173,106 @@ extern "C" int sf37_cuda_gqa_single_token_heads(sf37_cuda_tensor *out_heads, con
     if (check_cuda(cudaGetLastError(), "gqa single-token launch")) return dropin_fail("gqa_single_token_heads");
     return 1;
 }
+
+// ------------------------------------------------------------ caller-provided scratch
+// Split-K decode launch whose partials and counters live in memory the
+// caller provides (the allocation-free entry point, decode_noalloc.cu).  It
+// plans like attention_jobs but raises the rows per CTA until the partials
+// fit in part_bytes, and never allocates.  Only the fast kernels (head_dim
+// 128, group <= 16) are reachable here; other shapes are rejected.
+namespace sf37kv {
+
+int attention_jobs_prealloc(const AttnJob *jobs, uint32_t n, uint32_t q_heads, uint32_t kv_heads,
+                            uint32_t head_dim, int dtype, cudaStream_t stream, float *part,
+                            uint64_t part_bytes, uint32_t *counters, uint64_t n_counters) {
+    if (dtype != SF37KV_F32 && dtype != SF37KV_F16)
+        return set_error(SF37KV_EINVAL, "decode_noalloc: unknown cache dtype %d", dtype);
+    if (kv_heads == 0 || q_heads == 0 || q_heads % kv_heads != 0)
+        return set_error(SF37KV_EINVAL, "decode_noalloc: bad head configuration q=%u kv=%u", q_heads,
+                         kv_heads);
+    const uint32_t G = q_heads / kv_heads;
+    if (head_dim != 128 || G > 16 || (dtype == SF37KV_F32 && f32_gp(G) == 0))
+        return set_error(SF37KV_EUNSUPPORTED,
+                         "decode_noalloc: needs head_dim 128 and q_heads/kv_heads in {1,2,4,8,12,16} "
+                         "(f32) or <= 16 (f16); got head_dim %u, group %u",
+                         head_dim, G);
+    if (n > (uint32_t)kMaxJobs)
+        return set_error(SF37KV_EINVAL, "decode_noalloc: %u layers exceed the maximum of %d per call", n,
+                         kMaxJobs);
+    if ((uint64_t)n * kv_heads > n_counters)
+        return set_error(SF37KV_EINVAL,
+                         "decode_noalloc: layers x kv_heads = %llu exceeds the %llu split counters",
+                         (unsigned long long)n * kv_heads, (unsigned long long)n_counters);
+    for (uint32_t i = 0; i < n; i++) {
+        const AttnJob &A = jobs[i];
+        if (!A.k || !A.v || !A.q || !A.out || A.cap == 0 || A.end < A.start)
+            return set_error(SF37KV_EINVAL, "decode_noalloc: layer %u is invalid", i);
+    }
+    if (n == 0) return SF37KV_OK;
+    const uint32_t stride = (G * 130u + 3u) & ~3u;
+    const uint64_t cap_parts = part_bytes / ((uint64_t)stride * 4u);
+    uint64_t total = 0;
+    uint32_t max_rows = 0;
+    for (uint32_t i = 0; i < n; i++) {
+        total += (uint64_t)(jobs[i].end - jobs[i].start);
+        if (jobs[i].end - jobs[i].start > max_rows) max_rows = jobs[i].end - jobs[i].start;
+    }
+    total *= kv_heads;
+    const uint64_t target = (uint64_t)num_sms() * 3 * 8;
+    uint64_t per = (total + target - 1) / target;
+    if (per < 256) per = 256;
+    DecodeParams P;
+    for (;;) {
+        P.n_jobs = n;
+        P.q_heads = q_heads;
+        P.kv_heads = kv_heads;
+        P.group = G;
+        P.part_stride = stride;
+        P.qscale = kLog2e / sqrtf(128.0f);
+        uint32_t ctas = 0;
+        bool any_split = false;
+        for (uint32_t i = 0; i < n; i++) {
+            const AttnJob &A = jobs[i];
+            const uint32_t rows = A.end - A.start;
+            uint64_t ns = (rows + per - 1) / per;
+            if (ns < 1) ns = 1;
+            if (ns > kMaxSplits) ns = kMaxSplits;
+            uint32_t sr = (uint32_t)((rows + ns - 1) / ns);
+            sr = (sr + 127u) & ~127u;
+            if (sr == 0) sr = 128;
+            ns = (rows + sr - 1) / sr;
+            if (ns < 1) ns = 1;
+            if (ns > 1) any_split = true;
+            P.job[i] = JobDev{A.k, A.v, A.q, A.gate, A.out, A.start, A.end, A.cap, sr, (uint32_t)ns, ctas};
+            ctas += (uint32_t)ns * kv_heads;
+        }
+        P.total_ctas = ctas;
+        if (!any_split || ctas <= cap_parts) break;
+        if (per >= max_rows) break;  // cannot happen: one split per layer uses no partials
+        per *= 2;
+    }
+    P.part = part;
+    P.counters = counters;
+    // Counters must start at zero; clear the ones this launch uses.
+    if (int rc = check_cuda(cudaMemsetAsync(counters, 0, (size_t)n * kv_heads * 4u, stream),
+                            "decode_noalloc counter clear"))
+        return rc;
+    if (dtype == SF37KV_F16) {
+        cudaFuncSetAttribute(decode_f16_pipe_kernel<4, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)smem_pipe(4, 3));
+        decode_f16_pipe_kernel<4, 3><<<P.total_ctas, 128, smem_pipe(4, 3), stream>>>(P);
+    } else {
+        switch (G) {
+            case 1: launch_f32<1, 8>(P, P.total_ctas, stream); break;
+            case 2: launch_f32<2, 8>(P, P.total_ctas, stream); break;
+            case 4: launch_f32<4, 8>(P, P.total_ctas, stream); break;
+            case 8: launch_f32<8, 4>(P, P.total_ctas, stream); break;
+            case 12: launch_f32<6, 4>(P, P.total_ctas, stream); break;
+            default: launch_f32<8, 4>(P, P.total_ctas, stream); break;
+        }
+    }
+    g_launches++;
+    return check_cuda(cudaGetLastError(), "decode_noalloc launch");
+}
+
+}  // namespace sf37kv

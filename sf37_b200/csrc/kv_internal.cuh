@@ -60,6 +60,12 @@ struct AttnJob {
 int attention_jobs(const AttnJob *jobs, uint32_t n, uint32_t q_heads, uint32_t kv_heads,
                    uint32_t head_dim, int dtype, cudaStream_t stream);
 
+// The same split-K decode with caller-provided partials and counters; never
+// allocates (see decode_noalloc.cu).
+int attention_jobs_prealloc(const AttnJob *jobs, uint32_t n, uint32_t q_heads, uint32_t kv_heads,
+                            uint32_t head_dim, int dtype, cudaStream_t stream, float *part,
+                            uint64_t part_bytes, uint32_t *counters, uint64_t n_counters);
+
 // Logical start row of the query at position pos (sf37_cuda.cu:2752-2758).
 static inline uint32_t start_at(uint32_t pos, uint32_t cap, int sliding, uint32_t window) {
     const uint32_t have = pos + 1u;
