@@ -1,0 +1,63 @@
+"""GPU, 2 ranks over NCCL (needs >= 2 GPUs): KV-head-sharded decode through
+the C ABI plus the output all-gather equals the oracle on the full heads."""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = [pytest.mark.gpu,
+              pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
+                                 reason="needs 2 GPUs")]
+
+
+def _worker(rank, world, port, result):
+    import torch.distributed as dist
+    from sf37_b200 import kv, synth
+    from sf37_b200.shard import ShardPlan, gather_outputs
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world)
+    plan = ShardPlan(world, rank)
+    layers, cap, pos = 4, 5000, 4999
+    descs, outs = [], torch.empty(layers, plan.q_local, 128, device="cuda")
+    for l in range(layers):
+        k = torch.from_numpy(synth.normal(10 + l, (cap, 1024))).cuda()
+        v = torch.from_numpy(synth.normal(20 + l, (cap, 1024))).cuda()
+        q = torch.from_numpy(synth.normal(30 + l, (64, 128))).cuda()
+        a, b = plan.q_range
+        descs.append(dict(k_cache=plan.slice_rows(k).half().contiguous(),
+                          v_cache=plan.slice_rows(v).half().contiguous(), cap=cap, pos=pos,
+                          q=plan.slice_q(q).contiguous(), out=outs[l]))
+    kv.decode(descs, plan.q_local, plan.kv_local, 128, kv.F16)
+    full = gather_outputs(outs, plan)
+    if rank == 0:
+        result.put(full.cpu().numpy())
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_sharded_decode_2gpu():
+    import oracle
+    from sf37_b200 import synth
+    from tests.helpers import assert_close
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    ps = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    got = q.get(timeout=300)
+    for p in ps:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    for l in range(4):
+        k = oracle.f16_bits_to_f32(oracle.f32_to_f16_bits(synth.normal(10 + l, (5000, 1024))))
+        v = oracle.f16_bits_to_f32(oracle.f32_to_f16_bits(synth.normal(20 + l, (5000, 1024))))
+        want = oracle.attention_decode_at(synth.normal(30 + l, (64, 128)), k, v, None, 4999, 5000, 64, 8, 128)
+        assert_close(got[l], want)
