@@ -388,6 +388,82 @@ def run_ours(args, rank, world):
     print(json.dumps(line), flush=True)
 
 
+def run_prefill(args, rank, world):
+    """per layer, append an 8192-token chunk onto a
+    24576-token f16 prefix and run causal chunk attention (bf16 queries,
+    64 Q / 8 KV heads, d 128); one step = all layers.  Tensor-core bound."""
+    import torch
+    from sf37_b200 import kv
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(dev)
+    kvh_l, qh_l = KVH // world, QH // world
+    kd = kvh_l * HD
+    prefix, chunk, cap = 24576, 8192, 32768
+    g = torch.Generator(device=dev)
+    g.manual_seed(99 + rank)
+    kc = [torch.randn(cap, kd, device=dev, generator=g).half() for _ in range(LAYERS)]
+    vc = [torch.randn(cap, kd, device=dev, generator=g).half() for _ in range(LAYERS)]
+    kn = torch.randn(chunk, kd, device=dev, generator=g)
+    vn = torch.randn(chunk, kd, device=dev, generator=g)
+    q = torch.randn(chunk, qh_l, HD, device=dev, generator=g).to(torch.bfloat16)
+    gate = torch.randn(chunk, qh_l, device=dev, generator=g)
+    out = torch.empty(chunk, qh_l, HD, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        for l in range(LAYERS):
+            kv.append([dict(k_cache=kc[l], v_cache=vc[l], cap=cap, pos0=prefix, n_tok=chunk, k=kn, v=vn)],
+                      kd, kv.F16, stream)
+            kv.prefill(kc[l], vc[l], cap, q, gate, out, prefix, chunk, qh_l, kvh_l, HD, kv.F16,
+                       stream=stream)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    n0 = kv.launch_count()
+    clk = ClockSampler(dev.index).__enter__()
+    time.sleep(0.3)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    ms = e0.elapsed_time(e1) / args.steps
+    launches = kv.launch_count() - n0
+    # attention kernel alone, CUDA events per launch
+    evs = []
+    for _ in range(min(LAYERS, 16)):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        kv.prefill(kc[0], vc[0], cap, q, gate, out, prefix, chunk, qh_l, kvh_l, HD, kv.F16, stream=stream)
+        b.record(stream)
+        evs.append((a, b))
+    torch.cuda.synchronize(dev)
+    clk.__exit__()
+    att_ms = sum(a.elapsed_time(b) for a, b in evs) / len(evs)
+    pairs = chunk * prefix + chunk * (chunk + 1) // 2
+    flops_layer = 4.0 * HD * pairs * qh_l
+    if rank != 0:
+        return
+    peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json"))) \
+        if os.path.exists(os.path.join(ROOT, "MEASURED_PEAKS.json")) else {}
+    peak = float(peaks.get("bf16_tflops_sustained", 1400.0))
+    ach = flops_layer / (att_ms * 1e-3) / 1e12
+    print(json.dumps({
+        "metric": "prefill tokens/s (config 4: 8192-token chunk on a 24576-token prefix, 48 layers)",
+        "value": chunk * world / (ms * 1e-3) / world, "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f16 K/V, bf16 q, f32 accumulate",
+        "data": "synthetic N(0,1), torch seeded CUDA generator",
+        "config": {"workload": "cfg4 chunked prefill", "layers": LAYERS, "prefix": prefix, "chunk": chunk},
+        "roofline": {"bound": "tensor", "kernel": "prefill_mma_kernel", "achieved": ach,
+                     "peak": peak, "peak_kind": "measured sustained" if peaks else "fallback",
+                     "unit": "TFLOP/s", "frac": ach / peak, "launch_ms": att_ms,
+                     "algorithmic_flops_per_launch": flops_layer},
+        "gpu_launches": launches, "clocks": clk.summary()}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -395,6 +471,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
+    ap.add_argument("--workload", default="decode", choices=["decode", "prefill"],
+                    help="decode = BASELINE config 2 (default); prefill = config 4")
     ap.add_argument("--quick", action="store_true",
                     help="timed steps only (no roofline/e2e/cpu legs): for profiler runs")
     ap.add_argument("--layers", type=int, default=48,
@@ -414,7 +492,10 @@ def main():
         import torch.distributed as dist
         torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
         dist.init_process_group("nccl")
-    run_ours(args, rank, world)
+    if args.workload == "prefill":
+        run_prefill(args, rank, world)
+    else:
+        run_ours(args, rank, world)
     if world > 1:
         import torch.distributed as dist
         dist.barrier()

@@ -164,6 +164,12 @@ int sf37kv_unpack_from_host(const void *host_src, const sf37kv_pack_layer *layer
                             uint32_t n_layers, uint32_t kv_dim, int dtype, int fmt,
                             uint32_t group);
 
+/* Synchronizes the device and returns the library's device error flag: 1
+ * when a kernel's bounded wait gave up (the kernel then stopped early and
+ * its output is invalid), 0 otherwise, -1 if it cannot be read.  clear != 0
+ * resets the flag. */
+int sf37kv_device_error(int clear);
+
 /* Number of kernel launches this library has issued (process total). */
 uint64_t sf37kv_launch_count(void);
 

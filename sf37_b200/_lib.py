@@ -87,6 +87,7 @@ SIGNATURES = {
     "sf37kv_unpack_from_host": (c_int, [c_vp, ctypes.POINTER(PackLayer), c_u32, c_u32, c_int,
                                         c_int, c_u32]),
     "sf37kv_launch_count": (c_u64, []),
+    "sf37kv_device_error": (c_int, [c_int]),
 }
 
 _lib = None

@@ -25,6 +25,7 @@ int set_error(int code, const char *fmt, ...);
 int check_cuda(cudaError_t err, const char *what);
 
 cudaStream_t current_stream();
+int *device_error_flag();
 int num_sms();
 
 // ---------------------------------------------------------------- scratch

@@ -7,6 +7,8 @@
 // tensor-core tile kernel for f16 caches lives in prefill_tc.cu and is used
 // when its shape conditions hold.
 #include <cstdio>
+#include <cstdlib>
+#include <cstring>
 
 #include "kv_internal.cuh"
 #include "../../include/sf37_cuda_kv.h"
@@ -15,6 +17,8 @@ namespace sf37kv {
 
 extern unsigned long long g_launches;
 
+int prefill_tc05(const sf37kv_cache *cache, const void *q, const float *gate, float *out, uint32_t pos0,
+                 uint32_t n_tok, uint32_t q_heads, uint32_t kv_heads, cudaStream_t stream, bool *handled);
 int prefill_tc(const sf37kv_cache *cache, const void *q, int q_type, const float *gate, float *out,
                uint32_t pos0, uint32_t n_tok, uint32_t q_heads, uint32_t kv_heads,
                cudaStream_t stream, bool *handled);
@@ -61,6 +65,12 @@ extern "C" int sf37kv_prefill(const sf37kv_cache *cache, const void *q, int q_ty
     cudaStream_t s = stream ? (cudaStream_t)stream : current_stream();
     if (dtype == SF37KV_F16 && head_dim == 128) {
         bool handled = false;
+        // SF37KV_PREFILL=mma selects the mma.sync kernel; default tcgen05.
+        const char *e = getenv("SF37KV_PREFILL");
+        if (q_type == SF37KV_Q_BF16 && !(e && !strcmp(e, "mma")))
+            if (int rc = prefill_tc05(cache, q, gate, out, pos0, n_tok, q_heads, kv_heads, s, &handled))
+                return rc;
+        if (!handled)
         if (int rc = prefill_tc(cache, q, q_type, gate, out, pos0, n_tok, q_heads, kv_heads, s, &handled))
             return rc;
         if (handled) return SF37KV_OK;

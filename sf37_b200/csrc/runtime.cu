@@ -80,6 +80,19 @@ int scratch_get(uint64_t part_bytes, uint64_t n_counters, Scratch *out) {
     return SF37KV_OK;
 }
 
+// One device int that kernels set when a bounded wait gives up.
+static int *g_err_flag = nullptr;
+int *device_error_flag() {
+    if (!g_err_flag) {
+        if (cudaMalloc(&g_err_flag, sizeof(int)) != cudaSuccess ||
+            cudaMemset(g_err_flag, 0, sizeof(int)) != cudaSuccess) {
+            (void)cudaGetLastError();
+            g_err_flag = nullptr;
+        }
+    }
+    return g_err_flag;
+}
+
 void scratch_release() {
     if (g_scratch.part) cudaFree(g_scratch.part);
     if (g_scratch.counters) cudaFree(g_scratch.counters);
@@ -101,6 +114,18 @@ int sf37kv_set_stream(void *stream) {
 }
 void *sf37kv_get_stream(void) { return (void *)g_stream; }
 uint64_t sf37kv_launch_count(void) { return g_launches; }
+
+int sf37kv_device_error(int clear) {
+    int *f = device_error_flag();
+    if (!f) return -1;
+    int v = 0;
+    if (cudaDeviceSynchronize() != cudaSuccess || cudaMemcpy(&v, f, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) {
+        (void)cudaGetLastError();
+        return -1;
+    }
+    if (clear && v) cudaMemset(f, 0, sizeof(int));
+    return v;
+}
 
 void *sf37kv_host_alloc(uint64_t bytes) {
     void *p = nullptr;

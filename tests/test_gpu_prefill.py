@@ -49,3 +49,28 @@ def test_native_prefill_f16(qtype, pos0, n_tok, cap, sliding):
     kv.prefill(kc, vc, cap, tq, dev(g), out, pos0, n_tok, qh, kvh, hd, kv.F16, sliding=sliding)
     want = oracle.attention_prefill(qf, kref, vref, g, pos0, n_tok, cap, qh, kvh, hd, sliding, 512)
     assert_close(host(out), want)
+
+
+@pytest.mark.parametrize("G,pos0,n_tok,cap,sliding", [(8, 2000, 300, 2400, 1), (8, 3000, 1000, 4096, 0),
+                                                      (12, 700, 257, 1024, 1), (4, 0, 33, 64, 0),
+                                                      (16, 90, 70, 256, 0)])
+def test_tensor_core_prefill_bf16(G, pos0, n_tok, cap, sliding):
+    kvh = 4 if G > 8 else 8
+    qh, hd = G * kvh, 128
+    kd = kvh * hd
+    kc, kref = f16_cache(synth.normal(51 + G, (cap, kd)))
+    vc, vref = f16_cache(synth.normal(52 + G, (cap, kd)))
+    tq = dev(synth.normal(53, (n_tok, qh, hd))).to(torch.bfloat16)
+    qf = tq.float().cpu().numpy()
+    g = synth.normal(54, (n_tok, qh))
+    out = torch.empty(n_tok, qh, hd, device="cuda")
+    kv.prefill(kc, vc, cap, tq, dev(g), out, pos0, n_tok, qh, kvh, hd, kv.F16, sliding=sliding)
+    got = host(out)
+    from sf37_b200 import _lib
+    assert _lib.lib().sf37kv_device_error(1) == 0, "a bounded wait in the prefill kernel gave up"
+    # all tokens for small chunks; a sampled prefix + suffix otherwise
+    spans = [(0, n_tok)] if n_tok <= 300 else [(0, 40), (n_tok - 40, n_tok)]
+    for a, b in spans:
+        want = oracle.attention_prefill(qf, kref, vref, g, pos0, n_tok, cap, qh, kvh, hd, sliding, 512,
+                                        t0=a, t1=b)
+        assert_close(got[a:b], want[a:b], what=f"tokens {a}..{b}")
