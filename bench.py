@@ -457,7 +457,7 @@ def run_prefill(args, rank, world):
         "scaling": "strong", "vs_baseline": None, "dtype": "f16 K/V, bf16 q, f32 accumulate",
         "data": "synthetic N(0,1), torch seeded CUDA generator",
         "config": {"workload": "cfg4 chunked prefill", "layers": LAYERS, "prefix": prefix, "chunk": chunk},
-        "roofline": {"bound": "tensor", "kernel": "prefill_mma_kernel", "achieved": ach,
+        "roofline": {"bound": "tensor", "kernel": "prefill_tc05_kernel", "achieved": ach,
                      "peak": peak, "peak_kind": "measured sustained" if peaks else "fallback",
                      "unit": "TFLOP/s", "frac": ach / peak, "launch_ms": att_ms,
                      "algorithmic_flops_per_launch": flops_layer},
