@@ -224,16 +224,23 @@ def run_ours(args, rank, world):
     qh_l = QH // world
     kd = kvh_l * HD
     steps, warm = args.steps, args.warmup
-    cap = CTX + warm + steps + 8
+    wl = args.workload
+    ctx = {"decode": CTX, "long": 131072, "hybrid": 65536}[wl]
+    full_cap = ctx + warm + steps + 16
+    # hybrid (config 3): layers il % 4 != 0 are sliding-window layers with a
+    # 512-row ring (cache indexed modulo 512); the others are full layers.
+    sliding = [wl == "hybrid" and (l % 4) != 0 for l in range(LAYERS)]
+    caps = [512 if sliding[l] else full_cap for l in range(LAYERS)]
     g = torch.Generator(device=dev)
     g.manual_seed(1234 + rank)
     stream = torch.cuda.current_stream(dev)
 
-    # Caches: KV rows 0..CTX-1 filled with N(0,1) (f16 RNE); every step appends one row.
+    # Caches: KV rows of positions < ctx filled with N(0,1) (f16 RNE); every
+    # step appends one row at the next position.
     kc, vc = [], []
-    for _ in range(LAYERS):
-        k = torch.empty(cap, kd, dtype=torch.float16, device=dev)
-        v = torch.empty(cap, kd, dtype=torch.float16, device=dev)
+    for l in range(LAYERS):
+        k = torch.empty(caps[l], kd, dtype=torch.float16, device=dev)
+        v = torch.empty(caps[l], kd, dtype=torch.float16, device=dev)
         k.normal_(generator=g)
         v.normal_(generator=g)
         kc.append(k)
@@ -247,11 +254,12 @@ def run_ours(args, rank, world):
 
     def descs(pos, with_append=True):
         return kv.decode_layers_desc([
-            dict(k_cache=kc[l], v_cache=vc[l], cap=cap, pos=pos, q=q[l], gate=gate[l], out=out[l],
+            dict(k_cache=kc[l], v_cache=vc[l], cap=caps[l], sliding=sliding[l], window=512, pos=pos,
+                 q=q[l], gate=gate[l], out=out[l],
                  k_new=kn[l] if with_append else None, v_new=vn[l] if with_append else None)
             for l in range(LAYERS)])
 
-    all_desc = [descs(CTX + i) for i in range(warm + steps)]
+    all_desc = [descs(ctx + i) for i in range(warm + steps)]
 
     def step(i):
         kv.decode(all_desc[i], qh_l, kvh_l, HD, kv.F16, stream)
@@ -281,8 +289,10 @@ def run_ours(args, rank, world):
         t = torch.tensor([ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
-    rows_mean = CTX + 1 + warm + (steps - 1) / 2.0
-    kv_bytes_step = LAYERS * rows_mean * KVH * HD * 2 * 2  # whole job, f16 K+V
+    def rows_at(pos, l):
+        return min(pos + 1, 512) if sliding[l] else pos + 1
+    kv_bytes_step = sum(rows_at(ctx + i, l) for i in range(warm, warm + steps) for l in range(LAYERS)) \
+        * KVH * HD * 2 * 2 / steps  # whole job, f16 K+V
     tok_s = 1000.0 / ms
 
     if args.quick:  # profiling runs: the timed steps only
@@ -294,7 +304,7 @@ def run_ours(args, rank, world):
 
     # Roofline leg: the attention kernel alone (no append), one launch per
     # call, CUDA events on the launching stream around each launch.
-    att_desc = descs(CTX + warm + steps - 1, with_append=False)
+    att_desc = descs(ctx + warm + steps - 1, with_append=False)
     for _ in range(3):
         kv.decode(att_desc, qh_l, kvh_l, HD, kv.F16, stream)
     torch.cuda.synchronize(dev)
@@ -308,11 +318,11 @@ def run_ours(args, rank, world):
         b.record(stream)
     torch.cuda.synchronize(dev)
     att_ms = sum(a.elapsed_time(b) for a, b in evs) / len(evs)
-    rows_att = CTX + warm + steps
-    att_bytes = LAYERS * (rows_att * kd * 2 * 2 + qh_l * HD * 4 * 2 + qh_l * 4)
+    att_bytes = sum(rows_at(ctx + warm + steps - 1, l) * kd * 2 * 2 + qh_l * HD * 4 * 2 + qh_l * 4
+                    for l in range(LAYERS))
     peak, peak_kind = _peaks()
     achieved = att_bytes / (att_ms * 1e-3) / 1e9
-    traffic = _traffic_from_profiles("decode_f16_pipe_cfg2.md") if LAYERS == 48 else None
+    traffic = _traffic_from_profiles("decode_f16_pipe_cfg2.md") if (LAYERS == 48 and wl == "decode") else None
 
     # End-to-end leg through the C ABI with host buffers: pinned host inputs
     # (q, gate, new K/V rows) copied in, outputs copied out, every step.
@@ -326,7 +336,7 @@ def run_ours(args, rank, world):
         t_.normal_()
     h2d = sum(t_.numel() * t_.element_size() for t_ in (h_q, h_gate, h_kn, h_vn))
     d2h = h_out.numel() * h_out.element_size()
-    e2e_desc = [descs(CTX + warm + steps + (i % 4)) for i in range(4)]
+    e2e_desc = [descs(ctx + warm + steps + (i % 4)) for i in range(4)]
 
     def e2e_step(i):
         q.copy_(h_q, non_blocking=True)
@@ -358,7 +368,7 @@ def run_ours(args, rank, world):
     clk.__exit__()
     if rank != 0:
         return
-    cpu = cpu_baseline(CTX + 1) if world == 1 and not args.no_cpu else None
+    cpu = cpu_baseline(CTX + 1) if (world == 1 and not args.no_cpu and wl == "decode") else None
     clocks = clk.summary()
     line = {
         "metric": METRIC, "value": tok_s, "unit": "tokens/s", "n_gpus": world, "steps": steps,
@@ -366,9 +376,13 @@ def run_ours(args, rank, world):
         "vs_baseline": None, "dtype": "f16",
         "data": "synthetic: N(0,1) f16 K/V caches and fp32 q/gate/new rows from torch's seeded CUDA "
                 "generator",
-        "config": {"workload": "cfg2: 48-layer decode step (append + GQA attention) at 32768 cached "
-                               "tokens, 64 Q / 8 KV heads, d 128, batch 1",
-                   "layers": LAYERS, "ctx": CTX, "q_heads": QH, "kv_heads": KVH, "head_dim": HD,
+        "config": {"workload": {"decode": "cfg2: 48-layer decode step (append + GQA attention) at 32768 "
+                                          "cached tokens, 64 Q / 8 KV heads, d 128, batch 1",
+                                "long": "cfg5a: 48-layer decode step at 131072 cached tokens, KV heads "
+                                        "sharded across GPUs",
+                                "hybrid": "cfg3: 48 layers, 12 full (il%4==0) + 36 sliding (window 512, "
+                                          "512-row ring), decode after a 65536-token prefix"}[wl],
+                   "layers": LAYERS, "ctx": ctx, "q_heads": QH, "kv_heads": KVH, "head_dim": HD,
                    "kv_heads_per_gpu": kvh_l,
                    "parallelism": f"kv-head shard x{world}" + (" + NCCL all-gather" if world > 1 else ""),
                    "l2": "no flush needed: 6.4 GB of KV per step >> 126 MB L2"},
@@ -386,6 +400,73 @@ def run_ours(args, rank, world):
     if cpu:
         line["cpu_baseline"] = cpu
     print(json.dumps(line), flush=True)
+
+
+def run_snapshot(args, rank, world):
+    """BASELINE config 5b: pack the 32768-token prefix of 48 f16 layers into
+    pinned host memory in both reference formats (raw f32 rows, int8-grouped
+    payload rows), then restore it.  Reports the device-side pack kernel
+    bandwidth (to a device buffer, HBM-bound) and the end-to-end host rates
+    (sf37kv_pack_to_host / sf37kv_unpack_from_host, link-bound)."""
+    import ctypes
+    import torch
+    from sf37_b200 import _lib, kv
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(dev)
+    kd = (KVH // world) * HD
+    rows = 32768
+    g = torch.Generator(device=dev)
+    g.manual_seed(7 + rank)
+    layers = []
+    for _ in range(LAYERS):
+        k = torch.empty(rows, kd, dtype=torch.float16, device=dev).normal_(generator=g)
+        v = torch.empty(rows, kd, dtype=torch.float16, device=dev).normal_(generator=g)
+        layers.append(dict(k_cache=k, v_cache=v, cap=rows, first_pos=0, rows=rows))
+    res = {}
+    stream = torch.cuda.current_stream(dev)
+    for fmt, name in ((kv.FMT_RAW, "raw_f32"), (kv.FMT_I8G, "i8_grouped")):
+        arr, total = kv.pack_layers_desc(layers, kd, fmt)
+        dbuf = torch.empty(total, dtype=torch.uint8, device=dev)
+        for _ in range(args.warmup):
+            kv.pack(dbuf, arr, kd, kv.F16, fmt, stream=stream)
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            kv.pack(dbuf, arr, kd, kv.F16, fmt, stream=stream)
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        ms = e0.elapsed_time(e1) / args.steps
+        kv_read = LAYERS * rows * kd * 2 * 2
+        del dbuf
+        host = _lib.lib().sf37kv_host_alloc(total)
+        assert host, _lib.last_error()
+        kv.pack_to_host(host, arr, kd, kv.F16, fmt)  # warm (page-in)
+        t0 = time.perf_counter()
+        kv.pack_to_host(host, arr, kd, kv.F16, fmt)
+        t_pack = time.perf_counter() - t0
+        t0 = time.perf_counter()
+        kv.unpack_from_host(host, arr, kd, kv.F16, fmt)
+        t_unpack = time.perf_counter() - t0
+        _lib.lib().sf37kv_host_free(host)
+        res[name] = {"bytes": total, "device_pack_ms": ms,
+                     "device_pack_GBps": (kv_read + total) / (ms * 1e-3) / 1e9,
+                     "host_pack_s": t_pack, "host_pack_GBps": total / t_pack / 1e9,
+                     "host_restore_s": t_unpack, "host_restore_GBps": total / t_unpack / 1e9}
+    if rank != 0:
+        return
+    peak, kind = _peaks()
+    r = res["raw_f32"]
+    print(json.dumps({
+        "metric": "snapshot pack GB/s (config 5b: 32768-token prefix x 48 layers to pinned host)",
+        "value": r["host_pack_GBps"], "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "f16 cache -> f32 rows / int8-grouped rows", "data": "synthetic N(0,1)",
+        "config": {"workload": "cfg5b snapshot pack/restore", "layers": LAYERS, "rows": rows},
+        "formats": res,
+        "roofline": {"bound": "hbm", "kernel": "pack_kernel (raw, device buffer)",
+                     "achieved": r["device_pack_GBps"], "peak": peak, "peak_kind": kind, "unit": "GB/s",
+                     "frac": r["device_pack_GBps"] / peak}}), flush=True)
 
 
 def run_prefill(args, rank, world):
@@ -471,8 +552,10 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
-    ap.add_argument("--workload", default="decode", choices=["decode", "prefill"],
-                    help="decode = BASELINE config 2 (default); prefill = config 4")
+    ap.add_argument("--workload", default="decode",
+                    choices=["decode", "prefill", "hybrid", "long", "snapshot"],
+                    help="decode = BASELINE config 2 (default); hybrid = config 3; prefill = config 4; "
+                         "long = config 5a; snapshot = config 5b")
     ap.add_argument("--quick", action="store_true",
                     help="timed steps only (no roofline/e2e/cpu legs): for profiler runs")
     ap.add_argument("--layers", type=int, default=48,
@@ -494,6 +577,8 @@ def main():
         dist.init_process_group("nccl")
     if args.workload == "prefill":
         run_prefill(args, rank, world)
+    elif args.workload == "snapshot":
+        run_snapshot(args, rank, world)
     else:
         run_ours(args, rank, world)
     if world > 1:
