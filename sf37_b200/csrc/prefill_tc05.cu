@@ -23,7 +23,7 @@
 //              (A = P from TMEM, V MN-major in smem); accumulators S_A, S_B,
 //              O_A, O_B fill the 512 TMEM columns; tcgen05.commit -> mbarrier;
 //   warp 17    one thread issues TMA tile loads (cp.async.bulk.tensor.2d,
-//              no multicast) of K and V tiles, each double-buffered, into
+//              single-CTA destination) of K and V tiles, each double-buffered, into
 //              128B-swizzled shared memory as soon as the MMAs release them.
 // Shared-memory operand tiles are two 64-column halves [rows][128 B] with
 // 16-byte chunk c of row r at c ^ (r & 7) (the TMA 128B swizzle); UMMA
