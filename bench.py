@@ -181,6 +181,60 @@ def cpu_baseline(rows):
             "kv_read_GBps": sample_layers * rows * KVH * HD * 2 * 4 / dt / 1e9}
 
 
+def reference_gpu_leg(dev, steps):
+    """Config 2 with fp32 caches, one call per layer through the reference's
+    own entry point sf37_cuda_attention_decode_heads_at: (a) the reference's
+    CUDA kernels (oracle/_ref/libsf37ref_cuda.so, sm_100a build of its
+    sources), (b) this library's drop-in of the same symbol.  Tokens/s of the
+    48 per-layer calls per step (attention only, fp32 KV = 12.9 GB)."""
+    import torch
+    import oracle
+    from sf37_b200 import kv
+    if not oracle.ref_cuda_available():
+        return None
+    R = oracle.ref_cuda()
+    cap = CTX + 1
+    kf = torch.empty(cap, KVH * HD, device=dev)
+    layers = []
+    for _ in range(LAYERS):
+        k = torch.empty(cap, KVH * HD, device=dev).normal_()
+        v = torch.empty(cap, KVH * HD, device=dev).normal_()
+        layers.append((k, v))
+    del kf
+    q = torch.randn(QH, HD, device=dev)
+    gate = torch.randn(QH, device=dev)
+    out = torch.empty(QH, HD, device=dev)
+
+    def rt(t):
+        return oracle.ref_tensor(t.data_ptr(), t.numel() * t.element_size())
+
+    def run(which, n):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        for rep in range(2):
+            torch.cuda.synchronize(dev)
+            e0.record()
+            for _ in range(n):
+                for k, v in layers:
+                    if which == "ref":
+                        R.sf37_cuda_attention_decode_heads_at(rt(out), rt(q), rt(k), rt(v), rt(gate), CTX, cap,
+                                                              QH, KVH, HD, 0, 512)
+                    else:
+                        kv.attention_decode_heads_at(out, q, k, v, gate, CTX, cap, QH, KVH, HD, 0, 512)
+            e1.record()
+            torch.cuda.synchronize(dev)
+        return e0.elapsed_time(e1) / n
+
+    n = max(2, min(steps, 5))
+    ms_ref = run("ref", n)
+    ms_ours = run("ours", n)
+    b = LAYERS * cap * KVH * HD * 4 * 2
+    del layers
+    torch.cuda.empty_cache()
+    return {"what": "cfg2 attention, fp32 caches, 48 per-layer calls of sf37_cuda_attention_decode_heads_at",
+            "reference_kernels": {"tokens_per_s": 1000.0 / ms_ref, "kv_read_GBps": b / (ms_ref * 1e-3) / 1e9},
+            "dropin_f32": {"tokens_per_s": 1000.0 / ms_ours, "kv_read_GBps": b / (ms_ours * 1e-3) / 1e9}}
+
+
 def run_reference(args, rank, world):
     """--impl reference: the reference's own CPU implementation of the path."""
     if rank != 0:
@@ -365,6 +419,9 @@ def run_ours(args, rank, world):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_ms = float(t.item())
 
+    ref_gpu = None
+    if world == 1 and wl == "decode" and not args.no_ref_gpu:
+        ref_gpu = reference_gpu_leg(dev, steps)
     clk.__exit__()
     if rank != 0:
         return
@@ -399,6 +456,8 @@ def run_ours(args, rank, world):
     }
     if cpu:
         line["cpu_baseline"] = cpu
+    if ref_gpu:
+        line["reference_gpu"] = ref_gpu
     print(json.dumps(line), flush=True)
 
 
@@ -552,6 +611,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
+    ap.add_argument("--no-ref-gpu", action="store_true", help="skip the reference CUDA kernels leg")
     ap.add_argument("--workload", default="decode",
                     choices=["decode", "prefill", "hybrid", "long", "snapshot"],
                     help="decode = BASELINE config 2 (default); hybrid = config 3; prefill = config 4; "

@@ -37,6 +37,8 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+
+#include <cuda_bf16.h>
 #include <cmath>
 
 #include "kv_internal.cuh"
@@ -660,6 +662,215 @@ __global__ void __launch_bounds__(NW * 32, 1) decode_f16_pipe_kernel(const __gri
     finish_cta<NW * 32>(P, J, j, kvh, split, cta, n_streams, 8, Os, Ms, Ls);
 }
 
+// ------------------------------------------------------------ f32 kernel, tensor cores
+// fp32 caches on the same per-warp cp.async pipeline and mma.sync tiles as
+// the f16 kernel.  Every fp32 operand x is split into bf16 hi = rn(x) and
+// lo = rn(x - hi) (16 significant bits, full fp32 range); S = q.K uses the
+// M-row trick for q (rows 0-7 hi, 8-15 lo) against K_hi and then K_lo, and
+// O = P.V likewise against V_hi and V_lo: four products, fp32 accumulate.
+// Stage: K then V, 16 rows x 512 B each; 16-byte chunk ch of row r at slot
+// ch ^ swz32(r), swz32(r) = ((r >> 1) & 3) ^ ((r & 1) << 2) (conflict free for
+// both fragment patterns).  Dimension order inside a head: k-step kk, thread
+// t holds dims 16kk + 4t .. +3 (one chunk); for PV, thread g holds dims
+// 16g .. 16g+15 and n-tile jt is dim 16g + jt.
+__device__ __forceinline__ uint32_t swz32(uint32_t r) { return ((r >> 1) & 3u) ^ ((r & 1u) << 2); }
+
+__device__ __forceinline__ void mma_bf16(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1) {
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+// (hi, lo) bf16 pairs of two floats: hi packs rn(a), rn(b); lo the residuals.
+__device__ __forceinline__ void split2(float a, float b, uint32_t &hi, uint32_t &lo) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    const float2 hf = __bfloat1622float2(h);
+    const __nv_bfloat162 l = __floats2bfloat162_rn(a - hf.x, b - hf.y);
+    hi = *reinterpret_cast<const uint32_t *>(&h);
+    lo = *reinterpret_cast<const uint32_t *>(&l);
+}
+
+template <int NW, int S>
+__global__ void __launch_bounds__(NW * 32, 1) decode_f32_pipe_kernel(const __grid_constant__ DecodeParams P) {
+    extern __shared__ __align__(128) uint8_t smem_raw[];
+    constexpr uint32_t kStage = 16384;  // 16 rows x 512 B for K, then V
+    uint4 *Qs = reinterpret_cast<uint4 *>(smem_raw + NW * S * kStage);  // [n_mt][8 kk][32 lanes]
+    float *Os = reinterpret_cast<float *>(smem_raw);
+    float *Ms = Os + NW * 16 * 128;
+    float *Ls = Ms + 16 * NW;
+
+    const uint32_t cta = blockIdx.x;
+    const uint32_t j = locate_job(P, cta);
+    const JobDev &J = P.job[j];
+    const uint32_t local = cta - J.cta_begin;
+    const uint32_t kvh = local / J.n_splits, split = local - kvh * J.n_splits;
+    const uint32_t G = P.group;
+    const uint32_t n_mt = (G + 7u) >> 3;
+    const uint32_t n_streams = NW / n_mt;
+    const uint32_t lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;
+    const uint32_t g = lane >> 2, t = lane & 3u;
+    const uint32_t mt = warp % n_mt, stream = warp / n_mt;
+
+    if (warp < n_mt) {
+        const uint32_t hg = warp * 8u + g;
+        const bool valid = hg < G;
+        const float *qp = J.q + (uint64_t)(kvh * G + (valid ? hg : 0u)) * 128u;
+#pragma unroll
+        for (int kk = 0; kk < 8; kk++) {
+            const float4 x = valid ? *reinterpret_cast<const float4 *>(qp + 16 * kk + 4 * t)
+                                   : make_float4(0.f, 0.f, 0.f, 0.f);
+            uint32_t r0, r1, r2, r3;
+            split2(x.x * P.qscale, x.y * P.qscale, r0, r1);
+            split2(x.z * P.qscale, x.w * P.qscale, r2, r3);
+            Qs[(warp * 8 + kk) * 32 + lane] = make_uint4(r0, r1, r2, r3);
+        }
+    }
+    __syncthreads();
+
+    const uint32_t row0 = J.start + split * J.split_rows;
+    const uint32_t row1 = min(row0 + J.split_rows, J.end);
+    const uint32_t cap = J.cap;
+    const uint64_t row_bytes = (uint64_t)P.kv_heads * 512u;
+    const char *kbase = reinterpret_cast<const char *>(J.k) + kvh * 512u;
+    const char *vbase = reinterpret_cast<const char *>(J.v) + kvh * 512u;
+    const uint32_t qs_addr = (uint32_t)__cvta_generic_to_shared(Qs + mt * 8 * 32 + lane);
+    const uint32_t wbuf = (uint32_t)__cvta_generic_to_shared(smem_raw) + warp * S * kStage;
+
+    const uint32_t bstep = n_streams * 16u;
+    const uint32_t b_first = row0 + stream * 16u;
+    const uint32_t nblk = b_first < row1 ? (row1 - b_first + bstep - 1) / bstep : 0u;
+
+    auto issue = [&](uint32_t it) {
+        if (it < nblk) {
+            const uint32_t bb = b_first + it * bstep;
+            const uint32_t sb = bb % cap;
+            const uint32_t st = wbuf + (it % S) * kStage;
+#pragma unroll
+            for (int i = 0; i < 16; i++) {
+                const uint32_t c = lane + 32u * i;
+                const uint32_t r = c >> 5, ch = c & 31u;
+                const uint32_t slot = bb + r < row1 ? ring_slot(sb, r, cap) : sb;
+                const uint64_t go = (uint64_t)slot * row_bytes + ch * 16u;
+                const uint32_t so = r * 512u + ((ch ^ swz32(r)) * 16u);
+                cp_async16(st + so, kbase + go);
+                cp_async16(st + 8192u + so, vbase + go);
+            }
+        }
+        cp_async_commit();
+    };
+
+    float o[16][4];
+#pragma unroll
+    for (int i = 0; i < 16; i++) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+    float m_run = -INFINITY, l_run = 0.f;
+
+#pragma unroll
+    for (int s = 0; s < S - 1; s++) issue(s);
+
+    for (uint32_t it = 0; it < nblk; it++) {
+        cp_async_wait<S - 2>();
+        __syncwarp();
+        issue(it + S - 1);
+        const uint32_t b = b_first + it * bstep;
+        const uint32_t st = wbuf + (it % S) * kStage;
+
+        float s[2][4];
+#pragma unroll
+        for (int i = 0; i < 2; i++) s[i][0] = s[i][1] = s[i][2] = s[i][3] = 0.f;
+#pragma unroll
+        for (int kk = 0; kk < 8; kk++) {
+            const uint4 a = lds128(qs_addr + kk * 512);
+#pragma unroll
+            for (int i = 0; i < 2; i++) {
+                const uint32_t r = 8u * i + g;
+                const uint4 u = lds128(st + r * 512u + (((4u * kk + t) ^ swz32(r)) * 16u));
+                uint32_t h0, l0, h1, l1;
+                split2(__uint_as_float(u.x), __uint_as_float(u.y), h0, l0);
+                split2(__uint_as_float(u.z), __uint_as_float(u.w), h1, l1);
+                mma_bf16(s[i], a.x, a.y, a.z, a.w, h0, h1);
+                mma_bf16(s[i], a.x, a.y, a.z, a.w, l0, l1);
+            }
+        }
+
+        float sc[2][2];
+#pragma unroll
+        for (int i = 0; i < 2; i++)
+#pragma unroll
+            for (int e = 0; e < 2; e++) {
+                const uint32_t r = b + 8u * i + 2u * t + e;
+                sc[i][e] = r < row1 ? s[i][e] + s[i][e + 2] : -INFINITY;
+            }
+        float mx = fmaxf(fmaxf(sc[0][0], sc[0][1]), fmaxf(sc[1][0], sc[1][1]));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+        if (__any_sync(0xffffffffu, mx > m_run + kRescaleSlack)) {
+            const float m_new = fmaxf(m_run, mx);
+            const float alpha = fast_exp2(m_run - m_new);
+            l_run *= alpha;
+#pragma unroll
+            for (int i = 0; i < 16; i++) {
+                o[i][0] *= alpha;
+                o[i][1] *= alpha;
+                o[i][2] *= alpha;
+                o[i][3] *= alpha;
+            }
+            m_run = m_new;
+        }
+        uint32_t pa[4];
+#pragma unroll
+        for (int i = 0; i < 2; i++) {
+            const float p0 = fast_exp2(sc[i][0] - m_run), p1 = fast_exp2(sc[i][1] - m_run);
+            l_run += p0 + p1;
+            split2(p0, p1, pa[2 * i], pa[2 * i + 1]);
+        }
+        // V: rows 2t, 2t+1, 2t+8, 2t+9; dims 16g .. 16g+15 (chunks 4g .. 4g+3).
+#pragma unroll
+        for (int c4 = 0; c4 < 4; c4++) {
+            float4 vv[4];
+#pragma unroll
+            for (int x = 0; x < 4; x++) {
+                const uint32_t r = 2u * t + (x & 1) + (x >> 1) * 8u;
+                const uint4 u = lds128(st + 8192u + r * 512u + (((4u * g + c4) ^ swz32(r)) * 16u));
+                vv[x] = make_float4(__uint_as_float(u.x), __uint_as_float(u.y), __uint_as_float(u.z),
+                                    __uint_as_float(u.w));
+            }
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+                const int jt = c4 * 4 + e;
+                const float a0 = e == 0 ? vv[0].x : e == 1 ? vv[0].y : e == 2 ? vv[0].z : vv[0].w;
+                const float a1 = e == 0 ? vv[1].x : e == 1 ? vv[1].y : e == 2 ? vv[1].z : vv[1].w;
+                const float a2 = e == 0 ? vv[2].x : e == 1 ? vv[2].y : e == 2 ? vv[2].z : vv[2].w;
+                const float a3 = e == 0 ? vv[3].x : e == 1 ? vv[3].y : e == 2 ? vv[3].z : vv[3].w;
+                uint32_t h0, l0, h1, l1;
+                split2(a0, a1, h0, l0);
+                split2(a2, a3, h1, l1);
+                mma_bf16(o[jt], pa[0], pa[1], pa[2], pa[3], h0, h1);
+                mma_bf16(o[jt], pa[0], pa[1], pa[2], pa[3], l0, l1);
+            }
+        }
+        __syncwarp();
+    }
+    cp_async_wait<0>();
+    __syncthreads();
+
+    l_run += __shfl_xor_sync(0xffffffffu, l_run, 1);
+    l_run += __shfl_xor_sync(0xffffffffu, l_run, 2);
+    const uint32_t hrow = mt * 8u + g;
+    float *Ow = Os + (stream * 16u + hrow) * 128u;
+    if (hrow < G) {
+#pragma unroll
+        for (int jt = 0; jt < 16; jt++)
+#pragma unroll
+            for (int e = 0; e < 2; e++) Ow[16u * (2u * t + e) + jt] = o[jt][e] + o[jt][e + 2];
+        if (t == 0) {
+            Ms[stream * 16u + hrow] = m_run;
+            Ls[stream * 16u + hrow] = l_run;
+        }
+    }
+    finish_cta<NW * 32>(P, J, j, kvh, split, cta, n_streams, 8, Os, Ms, Ls);
+}
+
 // ------------------------------------------------------------ f32 kernel
 // Warp = (part, stream): part p owns heads [p*GP, (p+1)*GP) of the group,
 // stream s takes row blocks s, s+n_streams, ...  Lane holds dims 4*lane..+3.
@@ -914,6 +1125,7 @@ static size_t smem_f16() {
     return (size_t)(kNW * 16 * 128 + 32 * kNW) * 4 + 2 * 8 * 32 * 16;
 }
 static size_t smem_pipe(int nw, int stages) { return (size_t)nw * stages * 8192 + 2 * 8 * 32 * 16; }
+static size_t smem_pipe32(int nw, int stages) { return (size_t)nw * stages * 16384 + 2 * 8 * 32 * 16; }
 template <int GP, int R>
 static size_t smem_f32() {
     return (size_t)(kNW * 16 * 128 + 32 * kNW + kNW * R * GP) * 4;
@@ -970,7 +1182,8 @@ int attention_jobs(const AttnJob *jobs, uint32_t n, uint32_t q_heads, uint32_t k
             return set_error(SF37KV_EINVAL, "attention: job %u is invalid", i);
     }
     const uint32_t G = q_heads / kv_heads;
-    const bool fast = head_dim == 128 && G <= 16 && (dtype == SF37KV_F16 || f32_gp(G) != 0);
+    const bool fast = head_dim == 128 && G <= 16 &&
+                      (dtype == SF37KV_F16 || f32_gp(G) != 0 || !getenv("SF37KV_DECODE_F32"));
     if (!fast) return launch_generic(jobs, n, q_heads, kv_heads, head_dim, dtype, stream);
 
     const int sms = num_sms();
@@ -1046,13 +1259,25 @@ int attention_jobs(const AttnJob *jobs, uint32_t n, uint32_t q_heads, uint32_t k
                 default: decode_f16_pipe_kernel<8, 3><<<ctas, 256, smem_pipe(8, 3), stream>>>(P); break;
             }
         } else {
-            switch (G) {
-                case 1: launch_f32<1, 8>(P, ctas, stream); break;
-                case 2: launch_f32<2, 8>(P, ctas, stream); break;
-                case 4: launch_f32<4, 8>(P, ctas, stream); break;
-                case 8: launch_f32<8, 4>(P, ctas, stream); break;
-                case 12: launch_f32<6, 4>(P, ctas, stream); break;
-                default: launch_f32<8, 4>(P, ctas, stream); break;  // 16
+            // SF37KV_DECODE_F32=cuda selects the CUDA-core fp32 kernel (comparison runs).
+            static int f32_cuda = -1;
+            if (f32_cuda < 0) {
+                const char *e = getenv("SF37KV_DECODE_F32");
+                f32_cuda = (e && !strcmp(e, "cuda")) ? 1 : 0;
+                cudaFuncSetAttribute(decode_f32_pipe_kernel<4, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)smem_pipe32(4, 3));
+            }
+            if (!f32_cuda) {
+                decode_f32_pipe_kernel<4, 3><<<ctas, 128, smem_pipe32(4, 3), stream>>>(P);
+            } else {
+                switch (G) {
+                    case 1: launch_f32<1, 8>(P, ctas, stream); break;
+                    case 2: launch_f32<2, 8>(P, ctas, stream); break;
+                    case 4: launch_f32<4, 8>(P, ctas, stream); break;
+                    case 8: launch_f32<8, 4>(P, ctas, stream); break;
+                    case 12: launch_f32<6, 4>(P, ctas, stream); break;
+                    default: launch_f32<8, 4>(P, ctas, stream); break;  // 16
+                }
             }
         }
         g_launches++;
