@@ -36,6 +36,7 @@
 #include <cfloat>
 #include <cstdio>
 #include <cstdlib>
+#include <algorithm>
 #include <cstring>
 
 #include <cuda_bf16.h>
@@ -205,14 +206,14 @@ __device__ void finish_cta(const DecodeParams &P, const JobDev &J, uint32_t j, u
         const uint32_t h = idx >> 5, d4 = (idx & 31u) * 4u;
         float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
         uint32_t s = 0;
-        for (; s + 4 <= n; s += 4) {
-            float4 x[4];
+        for (; s + 8 <= n; s += 8) {
+            float4 x[8];
 #pragma unroll
-            for (int u = 0; u < 4; u++)
+            for (int u = 0; u < 8; u++)
                 x[u] = __ldcg(reinterpret_cast<const float4 *>(
                     P0 + (uint64_t)(s + u) * P.part_stride + h * 128u + d4));
 #pragma unroll
-            for (int u = 0; u < 4; u++) {
+            for (int u = 0; u < 8; u++) {
                 const float w = W[(s + u) * G + h];
                 acc.x += x[u].x * w;
                 acc.y += x[u].y * w;
@@ -1192,11 +1193,28 @@ int attention_jobs(const AttnJob *jobs, uint32_t n, uint32_t q_heads, uint32_t k
         uint64_t total = 0;
         for (uint32_t i = 0; i < m; i++) total += (uint64_t)(jobs[base + i].end - jobs[base + i].start);
         total *= kv_heads;
-        // Rows per CTA: about 8 waves of resident CTAs for big batches (keeps
-        // the last partial wave small), at least 256 rows per CTA.
-        const uint64_t target = (uint64_t)sms * 3 * 8;
-        uint64_t per = (total + target - 1) / target;
-        if (per < 256) per = 256;
+        // Rows per CTA.  Big batches (e.g. 48 layers x 32K rows): about 8
+        // waves of resident CTAs, which keeps the last partial wave small.
+        // Small launches (one layer): a single wave, so each (layer, KV head)
+        // has few splits and its last CTA merges few partials.
+        const uint64_t occ = dtype == SF37KV_F16 ? 2 : 1;  // resident CTAs per SM
+        uint64_t per = (total + (uint64_t)sms * 24 - 1) / ((uint64_t)sms * 24);
+        if (per < 2048) {
+            const uint64_t slots = (uint64_t)sms * occ;
+            per = (total + slots - 1) / slots;
+            // round so that ceil(rows / per) CTAs of a job stay within the wave
+            per = ((per + 127) / 128) * 128;
+            if (per < 128) per = 128;
+            const uint64_t ctas1 = (uint64_t)m * kv_heads;
+            if (ctas1 <= slots) {
+                // per-job split count from the wave size (jobs of similar length)
+                const uint64_t ns = slots / ctas1;
+                uint64_t longest = 0;
+                for (uint32_t i = 0; i < m; i++) longest = std::max<uint64_t>(longest, jobs[base + i].end - jobs[base + i].start);
+                const uint64_t per2 = ((longest + ns - 1) / ns + 127) / 128 * 128;
+                if (per2 > per) per = per2;
+            }
+        }
         if (const char *e = getenv("SF37KV_SPLIT_ROWS")) per = strtoull(e, nullptr, 10) ? strtoull(e, nullptr, 10) : per;
         DecodeParams P;
         P.n_jobs = m;
