@@ -223,6 +223,10 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map
             P.trace[(slot) * 16 + (j)] = clock64();                                                 \
     } while (0)
 
+// POLY: one in POLY exp2 evaluations of a row uses the FMA polynomial
+// (exp2_fma), the others the MUFU unit (0 = MUFU only); balances the MUFU
+// and issue limits of the softmax warps.
+template <int POLY>
 __global__ void __launch_bounds__(576, 1) prefill_tc05_kernel(const __grid_constant__ Tc05Params P) {
     using namespace tc05;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -482,7 +486,8 @@ __global__ void __launch_bounds__(576, 1) prefill_tc05_kernel(const __grid_const
 #pragma unroll
                     for (int i = 0; i < 16; i++) {
                         const float p0 = fast_exp2(fmaf(v[2 * i], qs, -mu));
-                        const float p1 = exp2_fma(fmaf(v[2 * i + 1], qs, -mu));
+                        const float y1 = fmaf(v[2 * i + 1], qs, -mu);
+                        const float p1 = (POLY > 0 && (i % POLY) == 0) ? exp2_fma(y1) : fast_exp2(y1);
                         la += p0;
                         lb += p1;
                         w[q2][i] = pack_h2(p0, p1);
@@ -496,7 +501,7 @@ __global__ void __launch_bounds__(576, 1) prefill_tc05_kernel(const __grid_const
                         const bool ok1 = kp + 1u >= s_row && kp + 1u <= p_row && kp + 1u < kend;
                         const float x0 = ok0 ? fmaf(v[2 * i], qs, -mu) : -INFINITY;
                         const float x1 = ok1 ? fmaf(v[2 * i + 1], qs, -mu) : -INFINITY;
-                        const float p0 = fast_exp2(x0), p1 = exp2_fma(x1);
+                        const float p0 = fast_exp2(x0), p1 = (POLY > 0 && (i % POLY) == 0) ? exp2_fma(x1) : fast_exp2(x1);
                         la += p0;
                         lb += p1;
                         w[q2][i] = pack_h2(p0, p1);
@@ -611,7 +616,16 @@ int prefill_tc05(const sf37kv_cache *cache, const void *q, const float *gate, fl
         P.dbg = e ? (uint32_t)atoi(e) : 0u;
     }
     const size_t sm = 6 * tc05::kTile + 1024;
-    cudaFuncSetAttribute(prefill_tc05_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+    static int poly = -1;
+    if (poly < 0) {
+        const char *e = getenv("SF37KV_TC05_POLY");
+        poly = e ? atoi(e) : 0;
+        cudaFuncSetAttribute(prefill_tc05_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+        cudaFuncSetAttribute(prefill_tc05_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+        cudaFuncSetAttribute(prefill_tc05_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+        cudaFuncSetAttribute(prefill_tc05_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+        cudaFuncSetAttribute(prefill_tc05_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+    }
     dim3 grid((n_tok + 2 * P.tpt - 1) / (2 * P.tpt), kv_heads);
     static long long *trace = nullptr;
     P.trace = nullptr;
@@ -620,7 +634,14 @@ int prefill_tc05(const sf37kv_cache *cache, const void *q, const float *gate, fl
         cudaMemset(trace, 0, 16 * 16 * sizeof(long long));
         P.trace = trace;
     }
-    prefill_tc05_kernel<<<grid, 576, sm, stream>>>(P);
+    switch (poly) {
+        case 0: prefill_tc05_kernel<0><<<grid, 576, sm, stream>>>(P); break;
+        case 1: prefill_tc05_kernel<1><<<grid, 576, sm, stream>>>(P); break;
+        case 2: prefill_tc05_kernel<2><<<grid, 576, sm, stream>>>(P); break;
+        case 8: prefill_tc05_kernel<8><<<grid, 576, sm, stream>>>(P); break;
+        case 4: prefill_tc05_kernel<4><<<grid, 576, sm, stream>>>(P); break;
+        default: prefill_tc05_kernel<0><<<grid, 576, sm, stream>>>(P); break;
+    }
     g_launches++;
     if (P.dbg & 8) {
         long long h[256];
