@@ -413,81 +413,26 @@ __global__ void __launch_bounds__(576, 1) prefill_tc05_kernel(const __grid_const
         const uint32_t full_lo = start_of(P.pos0 + ttl, P), full_hi = P.pos0 + tt0;
         float m = -INFINITY, l = 0.f;
         bool ok = true;
-        for (uint32_t j = 0; j < ntiles; j++) {
-            const uint32_t k0 = kbeg + j * 128u;
-            if (r == 0 && hh == 0) TC05_TRACE(5 + 4 * t_id, j);
-            __syncwarp();
-            const bool got_s = !abort_sh && wait_bar_warp(bar(B_SFULL + t_id), j & 1u);
-            fence_after();
-            if (r == 0 && hh == 0) TC05_TRACE(6 + 4 * t_id, j);
-            const bool full = k0 >= full_lo && k0 + 127u <= full_hi;
-            float mxa = -INFINITY, mxb = -INFINITY;
-#pragma unroll 1
-            for (int q2 = 0; q2 < 2 && got_s; q2++) {
-                float v[32];
-                tmem_ld32(t_s + cb + q2 * 32u, v);
-                tmem_wait_ld();
-                if (full) {
-#pragma unroll
-                    for (int i = 0; i < 32; i += 2) {
-                        mxa = fmaxf(mxa, v[i]);
-                        mxb = fmaxf(mxb, v[i + 1]);
-                    }
-                } else {
-                    const uint32_t kb = k0 + cb + (uint32_t)(q2 * 32);
-#pragma unroll
-                    for (int i = 0; i < 32; i++) {
-                        const uint32_t kp = kb + (uint32_t)i;
-                        const bool okk = kp >= s_row && kp <= p_row && kp < kend;
-                        mxa = fmaxf(mxa, okk ? v[i] : -INFINITY);
-                    }
-                }
-            }
-            xch[j & 1u][t_id][hh][r] = fmaxf(mxa, mxb);
-            if (pair_any(!got_s)) { abort_sh = 1; ok = false; break; }
-            const float mx = fmaxf(xch[j & 1u][t_id][0][r], xch[j & 1u][t_id][1][r]) * P.qscale;
-            const bool need = mx > m + 8.0f;  // identical in both halves of the row
-            if (r == 0 && hh == 0) TC05_TRACE(7 + 4 * t_id, j);
-            const bool got_o = j == 0 || (!abort_sh && wait_bar_warp(bar(B_ODONE + t_id), (j - 1) & 1u));
-            fence_after();
-            if (r == 0 && hh == 0 && j == 2) TC05_TRACE(13 + t_id, 7);
-            if (got_o && __any_sync(0xffffffffu, need)) {
-                const float mn = need ? mx : m;
-                const float alpha = (m == -INFINITY) ? 0.f : fast_exp2(m - mn);
-                if (j > 0) {
-#pragma unroll
-                    for (int q2 = 0; q2 < 2; q2++) {
-                        float v[32];
-                        tmem_ld32(t_o + cb + q2 * 32u, v);
-                        tmem_wait_ld();
-#pragma unroll
-                        for (int i = 0; i < 32; i++) v[i] *= need ? alpha : 1.0f;
-                        tmem_st32(t_o + cb + q2 * 32u, v);
-                    }
-                    tmem_wait_st();
-                }
-                if (need) {
-                    l *= alpha;
-                    m = mn;
-                }
-            }
-            const float mu = m == -INFINITY ? 0.f : m;
-            const float qs = P.qscale;
-            uint32_t w[2][16];
-            float la = 0.f, lb = 0.f;
-            if (r == 0 && hh == 0 && j == 2) TC05_TRACE(13 + t_id, 0);
+        const float qs = P.qscale;
+        // One pass over this thread's 64 scores of tile k0 with reference max
+        // mu: P (packed f16) into w, sums into la, and the largest exponent
+        // x = s * qs - mu (log2 units) into xm.
+        auto pass = [&](uint32_t k0, bool full, float mu, uint32_t (&w)[2][16], float &la, float &xm) {
+            float lb = 0.f, xa = -INFINITY, xb = -INFINITY;
+            la = 0.f;
 #pragma unroll
             for (int q2 = 0; q2 < 2; q2++) {
                 float v[32];
                 tmem_ld32(t_s + cb + q2 * 32u, v);
                 tmem_wait_ld();
-                if (r == 0 && hh == 0 && j == 2) TC05_TRACE(13 + t_id, 1 + 2 * q2);
-                if (full) {  // branch-free body: lets the compiler interleave the 16 pairs
+                if (full) {
 #pragma unroll
                     for (int i = 0; i < 16; i++) {
-                        const float p0 = fast_exp2(fmaf(v[2 * i], qs, -mu));
-                        const float y1 = fmaf(v[2 * i + 1], qs, -mu);
-                        const float p1 = (POLY > 0 && (i % POLY) == 0) ? exp2_fma(y1) : fast_exp2(y1);
+                        const float x0 = fmaf(v[2 * i], qs, -mu), x1 = fmaf(v[2 * i + 1], qs, -mu);
+                        xa = fmaxf(xa, x0);
+                        xb = fmaxf(xb, x1);
+                        const float p0 = fast_exp2(x0);
+                        const float p1 = (POLY > 0 && (i % POLY) == 0) ? exp2_fma(x1) : fast_exp2(x1);
                         la += p0;
                         lb += p1;
                         w[q2][i] = pack_h2(p0, p1);
@@ -501,24 +446,71 @@ __global__ void __launch_bounds__(576, 1) prefill_tc05_kernel(const __grid_const
                         const bool ok1 = kp + 1u >= s_row && kp + 1u <= p_row && kp + 1u < kend;
                         const float x0 = ok0 ? fmaf(v[2 * i], qs, -mu) : -INFINITY;
                         const float x1 = ok1 ? fmaf(v[2 * i + 1], qs, -mu) : -INFINITY;
-                        const float p0 = fast_exp2(x0), p1 = (POLY > 0 && (i % POLY) == 0) ? exp2_fma(x1) : fast_exp2(x1);
+                        xa = fmaxf(xa, x0);
+                        xb = fmaxf(xb, x1);
+                        const float p0 = fast_exp2(x0);
+                        const float p1 = (POLY > 0 && (i % POLY) == 0) ? exp2_fma(x1) : fast_exp2(x1);
                         la += p0;
                         lb += p1;
                         w[q2][i] = pack_h2(p0, p1);
                     }
                 }
-                if (r == 0 && hh == 0 && j == 2) TC05_TRACE(13 + t_id, 2 + 2 * q2);
             }
-            l += la + lb;
-            // P overwrites S columns the partner half may still be reading:
-            // both halves finish their loads first.
-            if (pair_any(!got_o)) { abort_sh = 1; ok = false; break; }
+            la += lb;
+            xm = fmaxf(xa, xb);
+        };
+        for (uint32_t j = 0; j < ntiles; j++) {
+            const uint32_t k0 = kbeg + j * 128u;
+            if (r == 0 && hh == 0) TC05_TRACE(5 + 4 * t_id, j);
+            __syncwarp();
+            const bool got_s = !abort_sh && wait_bar_warp(bar(B_SFULL + t_id), j & 1u);
+            fence_after();
+            if (r == 0 && hh == 0) TC05_TRACE(6 + 4 * t_id, j);
+            // s_full(j) follows every earlier MMA of the issuing thread, so
+            // PV_t(j-1) is complete: O_t is stable and P_t may be rewritten.
+            const bool full = k0 >= full_lo && k0 + 127u <= full_hi;
+            uint32_t w[2][16];
+            float la = 0.f, xm = -INFINITY;
+            const float mu0 = m == -INFINITY ? 0.f : m;
+            if (got_s) pass(k0, full, mu0, w, la, xm);
+            if (pair_any(!got_s)) { abort_sh = 1; ok = false; break; }
+            // The running max only moves when some exponent exceeds 8 (or on
+            // the first tile); then the row max is exchanged with the partner
+            // half, O and l are rescaled and P is recomputed.
+            const bool need = m == -INFINITY || xm > 8.0f;
+            if (r == 0 && hh == 0) TC05_TRACE(7 + 4 * t_id, j);
+            if (pair_any(need)) {
+                xch[j & 1u][t_id][hh][r] = xm + mu0;
+                pair_any(false);
+                const float mx = fmaxf(xch[j & 1u][t_id][0][r], xch[j & 1u][t_id][1][r]);
+                const bool row_need = mx > -INFINITY && (m == -INFINITY || mx > m + 8.0f);
+                if (__any_sync(0xffffffffu, row_need)) {
+                    const float alpha = (m == -INFINITY || !row_need) ? (row_need ? 0.f : 1.f) : fast_exp2(m - mx);
+                    if (j > 0) {
+#pragma unroll
+                        for (int q2 = 0; q2 < 2; q2++) {
+                            float v[32];
+                            tmem_ld32(t_o + cb + q2 * 32u, v);
+                            tmem_wait_ld();
+#pragma unroll
+                            for (int i = 0; i < 32; i++) v[i] *= alpha;
+                            tmem_st32(t_o + cb + q2 * 32u, v);
+                        }
+                        tmem_wait_st();
+                    }
+                    if (row_need) {
+                        l *= alpha;
+                        m = mx;
+                    }
+                    pass(k0, full, m == -INFINITY ? 0.f : m, w, la, xm);
+                }
+                pair_any(false);  // both halves have re-read S before P overwrites it
+            }
+            l += la;
             // keys cb .. cb+63 -> P columns cb/2 .. cb/2 + 31
-            if (r == 0 && hh == 0 && j == 2) TC05_TRACE(13 + t_id, 5);
             tmem_st16u(t_s + cb / 2u, w[0]);
             tmem_st16u(t_s + cb / 2u + 16u, w[1]);
             tmem_wait_st();
-            if (r == 0 && hh == 0 && j == 2) TC05_TRACE(13 + t_id, 6);
             fence_before();
             if (r == 0 && hh == 0) TC05_TRACE(8 + 4 * t_id, j);
             bar_arrive(bar(B_PFULL + t_id));  // P_t ready (S_t fully consumed)
