@@ -31,17 +31,12 @@ struct PackJob {
 
 struct PackParams {
     PackJob job[kMaxJobs];
-    uint32_t n_jobs;
+    uint32_t n_jobs, total_rows;
     uint32_t kv_dim, group, groups;
     uint64_t row_bytes;
     int variant;
 };
 
-__device__ __forceinline__ uint32_t locate(const PackParams &P, uint32_t row) {
-    uint32_t j = 0;
-    while (j + 1 < P.n_jobs && P.job[j + 1].row_begin <= row) j++;
-    return j;
-}
 
 // Loads 8 consecutive cache elements as f32.
 template <typename T>
@@ -99,117 +94,170 @@ __device__ __forceinline__ void store_bytes8(uint8_t *dst, uint32_t lo, uint32_t
     }
 }
 
-// Row r of the job's section: K row (kv = 0) or V row (kv = 1) at ring slot.
+// Encodes (FMT) the 8 elements x of row `out` starting at element e0.
+template <int FMT>
+__device__ __forceinline__ void encode8(const PackParams &P, const float (&x)[8], uint8_t *out, uint32_t e0) {
+    if (FMT == SF37KV_FMT_RAW_F32) {
+        uint8_t *o = out + (uint64_t)e0 * 4u;
+        if (((uintptr_t)o & 15u) == 0) {
+            reinterpret_cast<float4 *>(o)[0] = make_float4(x[0], x[1], x[2], x[3]);
+            reinterpret_cast<float4 *>(o)[1] = make_float4(x[4], x[5], x[6], x[7]);
+        } else {
+            for (int i = 0; i < 8; i += 2)
+                store_bytes8(o + 4 * i, __float_as_uint(x[i]), __float_as_uint(x[i + 1]));
+        }
+        return;
+    }
+    // payload_encode_kv_row_i8_grouped: max |x| over finite values.
+    const uint32_t tpg = P.group >> 3;  // threads per group
+    float m = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        const float a = fabsf(x[i]);
+        if (isfinite(a) && a > m) m = a;
+    }
+    // Groups are whole and lane-aligned, so a lane's partners are active.
+    const unsigned act = __activemask();
+    for (uint32_t s = 1; s < tpg; s <<= 1) m = fmaxf(m, __shfl_xor_sync(act, m, s));
+    float scale, inv;
+    if (m > 0.f) {
+        if (P.variant == 1) {
+            // -ffast-math form: m * (1/127), x * (1/scale), IEEE-rounded.
+            scale = __fmul_rn(m, 1.0f / 127.0f);
+            inv = __frcp_rn(scale);
+        } else {
+            scale = __fdiv_rn(m, 127.0f);
+            inv = 0.f;
+        }
+    } else {
+        scale = 1.0f;
+        inv = 1.0f;
+    }
+    const uint32_t grp = e0 / P.group;
+    if ((threadIdx.x & (tpg - 1u)) == 0) {
+        uint8_t *so = out + (uint64_t)grp * 4u;
+        const uint32_t u = __float_as_uint(scale);
+        if (((uintptr_t)so & 3u) == 0) *reinterpret_cast<uint32_t *>(so) = u;
+        else
+            for (int i = 0; i < 4; i++) so[i] = (uint8_t)(u >> (8 * i));
+    }
+    uint32_t q[8];
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        float v = isfinite(x[i]) ? x[i] : 0.f;
+        const float y = (P.variant == 1 || m <= 0.f) ? __fmul_rn(v, inv) : __fdiv_rn(v, scale);
+        int qi = __float2int_rn(y);
+        qi = qi > 127 ? 127 : (qi < -127 ? -127 : qi);
+        q[i] = (uint32_t)(qi & 0xff);
+    }
+    const uint32_t lo = q[0] | (q[1] << 8) | (q[2] << 16) | (q[3] << 24);
+    const uint32_t hi = q[4] | (q[5] << 8) | (q[6] << 16) | (q[7] << 24);
+    store_bytes8(out + (uint64_t)P.groups * 4u + e0, lo, hi);
+}
+
+// Decodes (FMT) the 8 elements of encoded row `in` starting at element e0.
+template <int FMT>
+__device__ __forceinline__ void decode8(const PackParams &P, const uint8_t *in, uint32_t e0, float (&x)[8]) {
+    if (FMT == SF37KV_FMT_RAW_F32) {
+        const uint8_t *p = in + (uint64_t)e0 * 4u;
+        if (((uintptr_t)p & 15u) == 0) {
+            const float4 a = __ldcs(reinterpret_cast<const float4 *>(p));
+            const float4 b = __ldcs(reinterpret_cast<const float4 *>(p) + 1);
+            x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w;
+            x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
+        } else {
+            for (int i = 0; i < 8; i++) {
+                uint32_t u = 0;
+                for (int bb = 0; bb < 4; bb++) u |= (uint32_t)p[4 * i + bb] << (8 * bb);
+                x[i] = __uint_as_float(u);
+            }
+        }
+        return;
+    }
+    // payload_decode_kv_row_i8_grouped (sf37.c:6661-6674): q * scale.
+    const uint32_t grp = e0 / P.group;
+    const uint8_t *sp = in + (uint64_t)grp * 4u;
+    uint32_t su = 0;
+    for (int bb = 0; bb < 4; bb++) su |= (uint32_t)sp[bb] << (8 * bb);
+    const float scale = __uint_as_float(su);
+    const uint8_t *qp = in + (uint64_t)P.groups * 4u + e0;
+#pragma unroll
+    for (int i = 0; i < 8; i++) x[i] = __fmul_rn((float)(int8_t)qp[i], scale);
+}
+
+// Each CTA handles a run of kRowsPerCta encoded rows (row = 2 * position +
+// {0: K, 1: V} of a layer section); position r lives at ring slot
+// (first_pos + r) % cap.  In the common case (8 * blockDim >= kv_dim) the
+// next row's elements are loaded before the current row is encoded.
+constexpr uint32_t kRowsPerCta = 16;
+
+struct RowRef {
+    uint32_t j, local;
+};
+__device__ __forceinline__ void advance(const PackParams &P, uint32_t row, RowRef &ref) {
+    while (ref.j + 1 < P.n_jobs && P.job[ref.j + 1].row_begin <= row) ref.j++;
+    ref.local = row - P.job[ref.j].row_begin;
+}
+
+template <typename T>
+__device__ __forceinline__ const T *row_src(const PackParams &P, const RowRef &ref) {
+    const PackJob &J = P.job[ref.j];
+    const uint32_t r = ref.local >> 1, kv = ref.local & 1u;
+    const uint64_t slot = (uint64_t)((J.first_pos + r) % J.cap);
+    return reinterpret_cast<const T *>(kv ? J.v : J.k) + slot * P.kv_dim;
+}
+
 template <typename T, int FMT>
 __global__ void __launch_bounds__(128) pack_kernel(uint8_t *dst, const __grid_constant__ PackParams P) {
-    const uint32_t row = blockIdx.x;
-    const uint32_t j = locate(P, row);
-    const PackJob &J = P.job[j];
-    const uint32_t local = row - J.row_begin;
-    const uint32_t r = local >> 1, kv = local & 1u;
-    const uint64_t slot = (uint64_t)((J.first_pos + r) % J.cap);
-    const T *src = reinterpret_cast<const T *>(kv ? J.v : J.k) + slot * P.kv_dim;
-    uint8_t *out = dst + J.offset + (uint64_t)local * P.row_bytes;
-    const uint32_t tpg = P.group >> 3;  // threads per group
-    for (uint32_t e0 = threadIdx.x * 8u; e0 < P.kv_dim; e0 += blockDim.x * 8u) {
+    const uint32_t row0 = blockIdx.x * kRowsPerCta;
+    const uint32_t row1 = min(row0 + kRowsPerCta, P.total_rows);
+    RowRef ref{0, 0};
+    advance(P, row0, ref);
+    const uint32_t e0 = threadIdx.x * 8u;
+    if (blockDim.x * 8u >= P.kv_dim) {
+        const bool act = e0 < P.kv_dim;
         float x[8];
-        load8<T>(src + e0, x);
-        if (FMT == SF37KV_FMT_RAW_F32) {
-            uint8_t *o = out + (uint64_t)e0 * 4u;
-            if (((uintptr_t)o & 15u) == 0) {
-                reinterpret_cast<float4 *>(o)[0] = make_float4(x[0], x[1], x[2], x[3]);
-                reinterpret_cast<float4 *>(o)[1] = make_float4(x[4], x[5], x[6], x[7]);
-            } else {
-                for (int i = 0; i < 8; i += 2)
-                    store_bytes8(o + 4 * i, __float_as_uint(x[i]), __float_as_uint(x[i + 1]));
+        if (act) load8<T>(row_src<T>(P, ref) + e0, x);
+        for (uint32_t row = row0; row < row1; row++) {
+            const RowRef cur = ref;
+            float xn[8];
+            if (row + 1 < row1) {
+                advance(P, row + 1, ref);
+                if (act) load8<T>(row_src<T>(P, ref) + e0, xn);
             }
-        } else {
-            // payload_encode_kv_row_i8_grouped: max |x| over finite values.
-            float m = 0.f;
+            if (act)
+                encode8<FMT>(P, x, dst + P.job[cur.j].offset + (uint64_t)cur.local * P.row_bytes, e0);
 #pragma unroll
-            for (int i = 0; i < 8; i++) {
-                const float a = fabsf(x[i]);
-                if (isfinite(a) && a > m) m = a;
+            for (int i = 0; i < 8; i++) x[i] = xn[i];
+        }
+    } else {
+        for (uint32_t row = row0; row < row1; row++) {
+            advance(P, row, ref);
+            const T *src = row_src<T>(P, ref);
+            uint8_t *out = dst + P.job[ref.j].offset + (uint64_t)ref.local * P.row_bytes;
+            for (uint32_t e = e0; e < P.kv_dim; e += blockDim.x * 8u) {
+                float x[8];
+                load8<T>(src + e, x);
+                encode8<FMT>(P, x, out, e);
             }
-            // Groups are whole and lane-aligned, so a lane's partners are active.
-            const unsigned act = __activemask();
-            for (uint32_t s = 1; s < tpg; s <<= 1) m = fmaxf(m, __shfl_xor_sync(act, m, s));
-            float scale, inv;
-            if (m > 0.f) {
-                if (P.variant == 1) {
-                    // -ffast-math form: m * (1/127), x * (1/scale), IEEE-rounded.
-                    scale = __fmul_rn(m, 1.0f / 127.0f);
-                    inv = __frcp_rn(scale);
-                } else {
-                    scale = __fdiv_rn(m, 127.0f);
-                    inv = 0.f;
-                }
-            } else {
-                scale = 1.0f;
-                inv = 1.0f;
-            }
-            const uint32_t grp = e0 / P.group;
-            if ((threadIdx.x & (tpg - 1u)) == 0) {
-                uint8_t *so = out + (uint64_t)grp * 4u;
-                const uint32_t u = __float_as_uint(scale);
-                if (((uintptr_t)so & 3u) == 0) *reinterpret_cast<uint32_t *>(so) = u;
-                else
-                    for (int i = 0; i < 4; i++) so[i] = (uint8_t)(u >> (8 * i));
-            }
-            uint32_t q[8];
-#pragma unroll
-            for (int i = 0; i < 8; i++) {
-                float v = isfinite(x[i]) ? x[i] : 0.f;
-                const float y = (P.variant == 1 || m <= 0.f) ? __fmul_rn(v, inv) : __fdiv_rn(v, scale);
-                int qi = __float2int_rn(y);
-                qi = qi > 127 ? 127 : (qi < -127 ? -127 : qi);
-                q[i] = (uint32_t)(qi & 0xff);
-            }
-            const uint32_t lo = q[0] | (q[1] << 8) | (q[2] << 16) | (q[3] << 24);
-            const uint32_t hi = q[4] | (q[5] << 8) | (q[6] << 16) | (q[7] << 24);
-            store_bytes8(out + (uint64_t)P.groups * 4u + e0, lo, hi);
         }
     }
 }
 
 template <typename T, int FMT>
 __global__ void __launch_bounds__(128) unpack_kernel(const uint8_t *src, const __grid_constant__ PackParams P) {
-    const uint32_t row = blockIdx.x;
-    const uint32_t j = locate(P, row);
-    const PackJob &J = P.job[j];
-    const uint32_t local = row - J.row_begin;
-    const uint32_t r = local >> 1, kv = local & 1u;
-    const uint64_t slot = (uint64_t)((J.first_pos + r) % J.cap);
-    T *dst = const_cast<T *>(reinterpret_cast<const T *>(kv ? J.v : J.k)) + slot * P.kv_dim;
-    const uint8_t *in = src + J.offset + (uint64_t)local * P.row_bytes;
-    for (uint32_t e0 = threadIdx.x * 8u; e0 < P.kv_dim; e0 += blockDim.x * 8u) {
-        float x[8];
-        if (FMT == SF37KV_FMT_RAW_F32) {
-            const uint8_t *p = in + (uint64_t)e0 * 4u;
-            if (((uintptr_t)p & 15u) == 0) {
-                const float4 a = __ldcs(reinterpret_cast<const float4 *>(p));
-                const float4 b = __ldcs(reinterpret_cast<const float4 *>(p) + 1);
-                x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w;
-                x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
-            } else {
-                for (int i = 0; i < 8; i++) {
-                    uint32_t u = 0;
-                    for (int bb = 0; bb < 4; bb++) u |= (uint32_t)p[4 * i + bb] << (8 * bb);
-                    x[i] = __uint_as_float(u);
-                }
-            }
-        } else {
-            // payload_decode_kv_row_i8_grouped (sf37.c:6661-6674): q * scale.
-            const uint32_t grp = e0 / P.group;
-            const uint8_t *sp = in + (uint64_t)grp * 4u;
-            uint32_t su = 0;
-            for (int bb = 0; bb < 4; bb++) su |= (uint32_t)sp[bb] << (8 * bb);
-            const float scale = __uint_as_float(su);
-            const uint8_t *qp = in + (uint64_t)P.groups * 4u + e0;
-#pragma unroll
-            for (int i = 0; i < 8; i++) x[i] = __fmul_rn((float)(int8_t)qp[i], scale);
+    const uint32_t row0 = blockIdx.x * kRowsPerCta;
+    const uint32_t row1 = min(row0 + kRowsPerCta, P.total_rows);
+    RowRef ref{0, 0};
+    for (uint32_t row = row0; row < row1; row++) {
+        advance(P, row, ref);
+        T *dst = const_cast<T *>(row_src<T>(P, ref));
+        const uint8_t *in = src + P.job[ref.j].offset + (uint64_t)ref.local * P.row_bytes;
+        for (uint32_t e0 = threadIdx.x * 8u; e0 < P.kv_dim; e0 += blockDim.x * 8u) {
+            float x[8];
+            decode8<FMT>(P, in, e0, x);
+            store8<T>(dst + e0, x);
         }
-        store8<T>(dst + e0, x);
     }
 }
 
@@ -266,7 +314,8 @@ static int launch_layers(void *buf, const sf37kv_pack_layer *layers, uint32_t n,
             if (rows > 0x7fffffffull) return set_error(SF37KV_EINVAL, "pack: too many rows");
         }
         if (P.n_jobs == 0) continue;
-        const unsigned grid = (unsigned)rows;
+        P.total_rows = (uint32_t)rows;
+        const unsigned grid = (unsigned)((rows + kRowsPerCta - 1) / kRowsPerCta);
         const unsigned threads = kv_dim / 8u < 128u ? ((kv_dim / 8u + 31u) & ~31u) : 128u;
         uint8_t *b = (uint8_t *)buf;
 #define SF37_PACK_LAUNCH(T, F)                                                         \
