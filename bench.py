@@ -461,6 +461,87 @@ def run_ours(args, rank, world):
     print(json.dumps(line), flush=True)
 
 
+def run_cfg1(args, rank, world):
+    """one layer, 2048 cached f16 rows + the appended row
+    at position 2048, 64 Q / 8 KV heads, d 128.  One step = one
+    sf37kv_decode (append + attention).  The 8.4 MB of K/V would sit in the
+    126 MB L2, so steps rotate over 16 independent cache copies (134 MB)."""
+    import torch
+    from sf37_b200 import kv
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(dev)
+    cap, ncopy = 2049, 16
+    g = torch.Generator(device=dev)
+    g.manual_seed(3)
+    copies = []
+    for _ in range(ncopy):
+        k = torch.randn(cap, KVH * HD, device=dev, generator=g).half()
+        v = torch.randn(cap, KVH * HD, device=dev, generator=g).half()
+        q = torch.randn(QH, HD, device=dev, generator=g)
+        gate = torch.randn(QH, device=dev, generator=g)
+        kn = torch.randn(KVH * HD, device=dev, generator=g)
+        vn = torch.randn(KVH * HD, device=dev, generator=g)
+        out = torch.empty(QH, HD, device=dev)
+        copies.append((kv.decode_layers_desc([dict(k_cache=k, v_cache=v, cap=cap, pos=2048, q=q, gate=gate,
+                                                   out=out, k_new=kn, v_new=vn)]), k, v, q, gate, kn, vn, out))
+    stream = torch.cuda.current_stream(dev)
+    for i in range(args.warmup * ncopy):
+        kv.decode(copies[i % ncopy][0], QH, KVH, HD, kv.F16, stream)
+    torch.cuda.synchronize(dev)
+    # The rotation over the 16 copies is captured once in a CUDA graph (the
+    # steps are microseconds long; host launch latency is not the path's).
+    gs = torch.cuda.Stream(dev)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=gs):
+        for i in range(ncopy):
+            kv.decode(copies[i][0], QH, KVH, HD, kv.F16, gs)
+    for _ in range(3):
+        graph.replay()
+    torch.cuda.synchronize(dev)
+    launches = 2 * args.steps * ncopy  # append + attention per step, replayed from the graph
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(gs)
+    with torch.cuda.stream(gs):
+        for _ in range(args.steps):
+            graph.replay()
+    e1.record(gs)
+    torch.cuda.synchronize(dev)
+    us = e0.elapsed_time(e1) * 1e3 / (args.steps * ncopy)
+    if rank != 0:
+        return
+    cpu = None
+    import oracle
+    if oracle.ref_available() and not args.no_cpu:
+        from sf37_b200 import synth
+        k, v, k_new, v_new, q, gate = synth.cfg1_inputs(0)
+        kc = np.zeros((cap, 1024), np.float32)
+        vc = np.zeros((cap, 1024), np.float32)
+        ts = []
+        for _ in range(5):
+            kc[:2048] = k
+            vc[:2048] = v
+            t0 = time.perf_counter()
+            n = oracle.ref_kv_cache_push(kc, vc, cap, 2048, k_new[None], v_new[None])
+            oracle.ref_attention_decode(q, kc, vc, n, cap, QH, 0, gate)
+            ts.append(time.perf_counter() - t0)
+        cpu = {"value": 1e6 / (min(ts) * 1e6), "unit": "steps/s", "cores": 1, "kind": "reference",
+               "sample": "one config-1 step (kv_cache_push + attention_decode + gate), best of 5"}
+    kvb = cap * KVH * HD * 2 * 2
+    peak, kind = _peaks()
+    line = {"metric": "config-1 decode step (1 layer, 2049 rows)", "value": 1e6 / us, "unit": "steps/s",
+            "n_gpus": world, "steps": args.steps * ncopy, "warmup": args.warmup, "ms_per_step": us / 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+            "data": "synthetic N(0,1)", "config": {"workload": "cfg1", "rows": cap,
+                                                   "l2": "16 rotating cache copies (134 MB > 126 MB L2)"},
+            "kv_read_GBps": kvb / (us * 1e-6) / 1e9,
+            "roofline": {"bound": "hbm", "kernel": "append + decode_f16_pipe_kernel", "achieved": kvb / (us * 1e-6) / 1e9,
+                         "peak": peak, "peak_kind": kind, "unit": "GB/s", "frac": kvb / (us * 1e-6) / 1e9 / peak},
+            "gpu_launches": launches}
+    if cpu:
+        line["cpu_baseline"] = cpu
+    print(json.dumps(line), flush=True)
+
+
 def run_snapshot(args, rank, world):
     """BASELINE config 5b: pack the 32768-token prefix of 48 f16 layers into
     pinned host memory in both reference formats (raw f32 rows, int8-grouped
@@ -613,7 +694,7 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
     ap.add_argument("--no-ref-gpu", action="store_true", help="skip the reference CUDA kernels leg")
     ap.add_argument("--workload", default="decode",
-                    choices=["decode", "prefill", "hybrid", "long", "snapshot"],
+                    choices=["decode", "prefill", "hybrid", "long", "snapshot", "cfg1"],
                     help="decode = BASELINE config 2 (default); hybrid = config 3; prefill = config 4; "
                          "long = config 5a; snapshot = config 5b")
     ap.add_argument("--quick", action="store_true",
@@ -639,6 +720,8 @@ def main():
         run_prefill(args, rank, world)
     elif args.workload == "snapshot":
         run_snapshot(args, rank, world)
+    elif args.workload == "cfg1":
+        run_cfg1(args, rank, world)
     else:
         run_ours(args, rank, world)
     if world > 1:

@@ -61,7 +61,29 @@ struct JobDev {
     float *out;
     uint32_t start, end, cap;
     uint32_t split_rows, n_splits, cta_begin;
+    const float *k_new, *v_new;  // appended row (position end-1) or nullptr
 };
+
+// The CTA owning the last split of (job, kvh) stores this KV head's slice of
+// the appended row (f32 -> T, round to nearest even) before any warp loads
+// rows; __syncthreads() plus L2-coherent cp.async.cg loads make it visible.
+template <typename T>
+__device__ __forceinline__ void fused_append(const JobDev &J, uint32_t kvh, uint32_t split, uint32_t kv_heads) {
+    if (!J.k_new || split + 1u != J.n_splits) return;
+    const uint32_t i = threadIdx.x;
+    if (i >= 64u) return;
+    const float *src = (i < 32u ? J.k_new : J.v_new) + kvh * 128u + (i & 31u) * 4u;
+    const float4 x = *reinterpret_cast<const float4 *>(src);
+    T *dst = reinterpret_cast<T *>(const_cast<void *>(i < 32u ? J.k : J.v)) +
+             (uint64_t)((J.end - 1u) % J.cap) * kv_heads * 128u + kvh * 128u + (i & 31u) * 4u;
+    if (sizeof(T) == 4) {
+        *reinterpret_cast<float4 *>(dst) = x;
+    } else {
+        const __half2 a = __floats2half2_rn(x.x, x.y), b = __floats2half2_rn(x.z, x.w);
+        *reinterpret_cast<uint2 *>(dst) =
+            make_uint2(*reinterpret_cast<const uint32_t *>(&a), *reinterpret_cast<const uint32_t *>(&b));
+    }
+}
 
 struct DecodeParams {
     JobDev job[kMaxJobs];
@@ -517,6 +539,7 @@ __global__ void __launch_bounds__(NW * 32, 1) decode_f16_pipe_kernel(const __gri
             Qs[(warp * 8 + kk) * 32 + lane] = make_uint4(r[0], r[1], r[2], r[3]);
         }
     }
+    fused_append<__half>(J, kvh, split, P.kv_heads);
     __syncthreads();
 
     const uint32_t row0 = J.start + split * J.split_rows;
@@ -727,6 +750,7 @@ __global__ void __launch_bounds__(NW * 32, 1) decode_f32_pipe_kernel(const __gri
             Qs[(warp * 8 + kk) * 32 + lane] = make_uint4(r0, r1, r2, r3);
         }
     }
+    fused_append<float>(J, kvh, split, P.kv_heads);
     __syncthreads();
 
     const uint32_t row0 = J.start + split * J.split_rows;
@@ -1146,7 +1170,7 @@ static int launch_generic(const AttnJob *jobs, uint32_t n, uint32_t q_heads, uin
         for (uint32_t i = base; i < n && i < base + kMaxJobs; i++) {
             const AttnJob &A = jobs[i];
             JobDev &D = P.job[P.n_jobs++];
-            D = JobDev{A.k, A.v, A.q, A.gate, A.out, A.start, A.end, A.cap, 0, 1, 0};
+            D = JobDev{A.k, A.v, A.q, A.gate, A.out, A.start, A.end, A.cap, 0, 1, 0, nullptr, nullptr};
         }
         const uint64_t warps = (uint64_t)P.n_jobs * q_heads;
         const unsigned grid = (unsigned)((warps + 7) / 8);
@@ -1183,6 +1207,26 @@ int attention_jobs(const AttnJob *jobs, uint32_t n, uint32_t q_heads, uint32_t k
             return set_error(SF37KV_EINVAL, "attention: job %u is invalid", i);
     }
     const uint32_t G = q_heads / kv_heads;
+    // Kernels that store appended rows themselves: the f16 cp.async pipeline
+    // (default variant) and the fp32 tensor-core pipeline (default); for the
+    // others the rows are appended by a separate launch first.
+    const char *ef = getenv("SF37KV_DECODE_F32");
+    const char *ek = getenv("SF37KV_DECODE_KERNEL");
+    const bool fuses = head_dim == 128 && G <= 16 &&
+                       ((dtype == SF37KV_F16 && !(ek && (!strcmp(ek, "reg2") || !strcmp(ek, "reg3")))) ||
+                        (dtype == SF37KV_F32 && !(ef && !strcmp(ef, "cuda"))));
+    if (!fuses) {
+        AppendJob aj[kMaxJobs];
+        for (uint32_t base = 0; base < n; base += kMaxJobs) {
+            uint32_t na = 0;
+            for (uint32_t i = base; i < n && i < base + kMaxJobs; i++)
+                if (jobs[i].k_new)
+                    aj[na++] = AppendJob{const_cast<void *>(jobs[i].k), const_cast<void *>(jobs[i].v), jobs[i].k_new,
+                                         jobs[i].v_new, jobs[i].end - 1u, 1, jobs[i].cap};
+            if (na)
+                if (int rc = append_jobs(aj, na, kv_heads * head_dim, dtype, stream)) return rc;
+        }
+    }
     const bool fast = head_dim == 128 && G <= 16 &&
                       (dtype == SF37KV_F16 || f32_gp(G) != 0 || !getenv("SF37KV_DECODE_F32"));
     if (!fast) return launch_generic(jobs, n, q_heads, kv_heads, head_dim, dtype, stream);
@@ -1238,7 +1282,8 @@ int attention_jobs(const AttnJob *jobs, uint32_t n, uint32_t q_heads, uint32_t k
             if (ns < 1) ns = 1;
             if (ns > 1) any_split = true;
             JobDev &D = P.job[i];
-            D = JobDev{A.k, A.v, A.q, A.gate, A.out, A.start, A.end, A.cap, sr, (uint32_t)ns, ctas};
+            D = JobDev{A.k, A.v, A.q, A.gate, A.out, A.start, A.end, A.cap, sr, (uint32_t)ns, ctas,
+                       fuses ? A.k_new : nullptr, fuses ? A.v_new : nullptr};
             if ((uint64_t)ctas + ns * kv_heads > 0x7fffffffull)
                 return set_error(SF37KV_EINVAL, "attention: grid too large");
             ctas += (uint32_t)ns * kv_heads;
@@ -1320,18 +1365,16 @@ extern "C" int sf37kv_decode(const sf37kv_decode_layer *layers, uint32_t n_layer
         for (uint32_t i = base; i < n_layers && m < (uint32_t)kMaxJobs; i++, m++) {
             const sf37kv_decode_layer &L = layers[i];
             if (L.cache.cap == 0) return set_error(SF37KV_EINVAL, "decode: layer %u cap 0", i);
-            if (L.k_new || L.v_new) {
-                if (!L.k_new || !L.v_new)
-                    return set_error(SF37KV_EINVAL, "decode: layer %u has only one of k_new/v_new", i);
-                aj[na++] = AppendJob{L.cache.k_cache, L.cache.v_cache, L.k_new, L.v_new, L.pos, 1,
-                                     L.cache.cap};
-            }
+            if ((L.k_new != nullptr) != (L.v_new != nullptr))
+                return set_error(SF37KV_EINVAL, "decode: layer %u has only one of k_new/v_new", i);
+            if (L.k_new && (((uintptr_t)L.k_new | (uintptr_t)L.v_new) & 15u))
+                return set_error(SF37KV_EINVAL, "decode: layer %u k_new/v_new must be 16-byte aligned", i);
             jobs[m] = AttnJob{L.cache.k_cache, L.cache.v_cache, L.q, L.gate, L.out,
                               start_at(L.pos, L.cache.cap, L.cache.sliding, L.cache.window),
-                              L.pos + 1u, L.cache.cap};
+                              L.pos + 1u, L.cache.cap, L.k_new, L.v_new};
         }
-        if (na)
-            if (int rc = append_jobs(aj, na, kv_heads * head_dim, dtype, s)) return rc;
+        (void)na;
+        (void)aj;
         if (int rc = attention_jobs(jobs, m, q_heads, kv_heads, head_dim, dtype, s)) return rc;
     }
     return SF37KV_OK;
@@ -1486,7 +1529,8 @@ int attention_jobs_prealloc(const AttnJob *jobs, uint32_t n, uint32_t q_heads, u
             ns = (rows + sr - 1) / sr;
             if (ns < 1) ns = 1;
             if (ns > 1) any_split = true;
-            P.job[i] = JobDev{A.k, A.v, A.q, A.gate, A.out, A.start, A.end, A.cap, sr, (uint32_t)ns, ctas};
+            P.job[i] = JobDev{A.k, A.v, A.q, A.gate, A.out, A.start, A.end, A.cap, sr, (uint32_t)ns, ctas,
+                              nullptr, nullptr};
             ctas += (uint32_t)ns * kv_heads;
         }
         P.total_ctas = ctas;

@@ -53,6 +53,9 @@ struct AttnJob {
     float *out;           // [q_heads][head_dim] f32
     uint32_t start, end;  // logical rows
     uint32_t cap;
+    // Optional row appended at position end-1 before attention (f32
+    // [kv_heads*head_dim]); the fast kernels store it themselves.
+    const float *k_new = nullptr, *v_new = nullptr;
 };
 
 // Launches attention for n jobs (any n; chunked internally).
