@@ -378,31 +378,59 @@ def run_ours(args, rank, world):
     achieved = att_bytes / (att_ms * 1e-3) / 1e9
     traffic = _traffic_from_profiles("decode_f16_pipe_cfg2.md") if (LAYERS == 48 and wl == "decode") else None
 
-    # End-to-end leg through the C ABI with host buffers: pinned host inputs
-    # (q, gate, new K/V rows) copied in, outputs copied out, every step.
+    # End-to-end leg through the C ABI with host buffers: every step copies its
+    # inputs (q, gate, new K/V rows) in from pinned host memory and its
+    # outputs back out.  The copies run on a side stream with double-buffered
+    # device inputs/outputs, so step i's copies overlap steps i-1 / i+1.
     h_q = torch.empty_like(q, device="cpu").pin_memory()
     h_gate = torch.empty_like(gate, device="cpu").pin_memory()
     h_kn = torch.empty_like(kn, device="cpu").pin_memory()
     h_vn = torch.empty_like(vn, device="cpu").pin_memory()
-    h_out = torch.empty(LAYERS, QH, HD).pin_memory() if world > 1 else \
-        torch.empty_like(out, device="cpu").pin_memory()
+    h_outs = [(torch.empty(LAYERS, QH, HD) if world > 1 else torch.empty_like(out, device="cpu")).pin_memory()
+              for _ in range(2)]
     for t_ in (h_q, h_gate, h_kn, h_vn):
         t_.normal_()
     h2d = sum(t_.numel() * t_.element_size() for t_ in (h_q, h_gate, h_kn, h_vn))
-    d2h = h_out.numel() * h_out.element_size()
-    e2e_desc = [descs(ctx + warm + steps + (i % 4)) for i in range(4)]
+    d2h = h_outs[0].numel() * h_outs[0].element_size()
+    bufs = [dict(q=q, gate=gate, kn=kn, vn=vn, out=out, gathered=gathered)]
+    bufs.append({k_: v_.clone() for k_, v_ in bufs[0].items()})
+
+    def descs_b(pos, B):
+        return kv.decode_layers_desc([
+            dict(k_cache=kc[l], v_cache=vc[l], cap=caps[l], sliding=sliding[l], window=512, pos=pos,
+                 q=B["q"][l], gate=B["gate"][l], out=B["out"][l], k_new=B["kn"][l], v_new=B["vn"][l])
+            for l in range(LAYERS)])
+
+    e2e_desc = [[descs_b(ctx + warm + steps + (i % 4), bufs[bb]) for bb in range(2)] for i in range(4)]
+    copy_s = torch.cuda.Stream(dev)   # host -> device
+    out_s = torch.cuda.Stream(dev)    # device -> host
+    ev_done = [torch.cuda.Event(), torch.cuda.Event()]
+    ev_out = [torch.cuda.Event(), torch.cuda.Event()]
+    ev_in = [torch.cuda.Event(), torch.cuda.Event()]
 
     def e2e_step(i):
-        q.copy_(h_q, non_blocking=True)
-        gate.copy_(h_gate, non_blocking=True)
-        kn.copy_(h_kn, non_blocking=True)
-        vn.copy_(h_vn, non_blocking=True)
-        kv.decode(e2e_desc[i % 4], qh_l, kvh_l, HD, kv.F16, stream)
+        bb = i & 1
+        B = bufs[bb]
+        copy_s.wait_event(ev_done[bb])  # step i-2 is done with these inputs
+        with torch.cuda.stream(copy_s):
+            B["q"].copy_(h_q, non_blocking=True)
+            B["gate"].copy_(h_gate, non_blocking=True)
+            B["kn"].copy_(h_kn, non_blocking=True)
+            B["vn"].copy_(h_vn, non_blocking=True)
+        ev_in[bb].record(copy_s)
+        stream.wait_event(ev_in[bb])
+        stream.wait_event(ev_out[bb])   # step i-2's outputs have been read out
+        kv.decode(e2e_desc[i % 4][bb], qh_l, kvh_l, HD, kv.F16, stream)
         if world > 1:
-            dist.all_gather_into_tensor(gathered, out)
-            h_out.view(LAYERS, world, qh_l, HD).copy_(gathered.permute(1, 0, 2, 3), non_blocking=True)
-        else:
-            h_out.copy_(out, non_blocking=True)
+            dist.all_gather_into_tensor(B["gathered"], B["out"])
+        ev_done[bb].record(stream)
+        out_s.wait_event(ev_done[bb])
+        with torch.cuda.stream(out_s):
+            if world > 1:
+                h_outs[bb].view(LAYERS, world, qh_l, HD).copy_(B["gathered"].permute(1, 0, 2, 3), non_blocking=True)
+            else:
+                h_outs[bb].copy_(B["out"], non_blocking=True)
+        ev_out[bb].record(out_s)
 
     for i in range(3):
         e2e_step(i)
@@ -411,6 +439,8 @@ def run_ours(args, rank, world):
     e0.record(stream)
     for i in range(steps):
         e2e_step(i)
+    stream.wait_stream(copy_s)
+    stream.wait_stream(out_s)
     e1.record(stream)
     barrier()
     e2e_ms = e0.elapsed_time(e1) / steps
