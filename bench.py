@@ -315,7 +315,18 @@ def run_ours(args, rank, world):
 
     all_desc = [descs(ctx + i) for i in range(warm + steps)]
 
+    # Multi-GPU output gather: by default the decode kernels store every
+    # output head straight into all ranks' buffers over NVLink (PeerGather);
+    # --gather nccl runs the decode and then an NCCL all-gather instead.
+    pg = None
+    if world > 1 and args.gather == "peer":
+        from sf37_b200.shard import PeerGather, ShardPlan
+        pg = PeerGather(ShardPlan(world, rank, KVH, QH, HD), LAYERS)
+
     def step(i):
+        if pg is not None:
+            pg.step(all_desc[i], kv.F16, stream)
+            return
         kv.decode(all_desc[i], qh_l, kvh_l, HD, kv.F16, stream)
         if world > 1:
             dist.all_gather_into_tensor(gathered, out)
@@ -420,9 +431,15 @@ def run_ours(args, rank, world):
         ev_in[bb].record(copy_s)
         stream.wait_event(ev_in[bb])
         stream.wait_event(ev_out[bb])   # step i-2's outputs have been read out
-        kv.decode(e2e_desc[i % 4][bb], qh_l, kvh_l, HD, kv.F16, stream)
-        if world > 1:
-            dist.all_gather_into_tensor(B["gathered"], B["out"])
+        if pg is not None:
+            # the peer buffer half is rewritten two steps later by the other
+            # ranks, so take a device copy on the decode stream first
+            pg.step(e2e_desc[i % 4][bb], kv.F16, stream)
+            B["gathered"].copy_(pg.gathered[pg.epoch & 1])
+        else:
+            kv.decode(e2e_desc[i % 4][bb], qh_l, kvh_l, HD, kv.F16, stream)
+            if world > 1:
+                dist.all_gather_into_tensor(B["gathered"], B["out"])
         ev_done[bb].record(stream)
         out_s.wait_event(ev_done[bb])
         with torch.cuda.stream(out_s):
@@ -448,6 +465,12 @@ def run_ours(args, rank, world):
         t = torch.tensor([e2e_ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_ms = float(t.item())
+    if pg is not None:
+        if kv.device_error(1):
+            raise RuntimeError("peer gather: a bounded wait timed out")
+        dist.barrier()
+        torch.cuda.synchronize(dev)
+        pg.close()
 
     ref_gpu = None
     if world == 1 and wl == "decode" and not args.no_ref_gpu:
@@ -471,7 +494,9 @@ def run_ours(args, rank, world):
                                           "512-row ring), decode after a 65536-token prefix"}[wl],
                    "layers": LAYERS, "ctx": ctx, "q_heads": QH, "kv_heads": KVH, "head_dim": HD,
                    "kv_heads_per_gpu": kvh_l,
-                   "parallelism": f"kv-head shard x{world}" + (" + NCCL all-gather" if world > 1 else ""),
+                   "parallelism": f"kv-head shard x{world}" + (
+                       "" if world == 1 else " + NCCL all-gather" if pg is None
+                       else " + output gather by peer-memory stores from the decode kernels"),
                    "l2": "no flush needed: 6.4 GB of KV per step >> 126 MB L2"},
         "kv_read_GBps": kv_bytes_step / (ms * 1e-3) / 1e9,
         "kv_read_frac_of_8TBps": kv_bytes_step / (ms * 1e-3) / 8e12,
@@ -721,6 +746,8 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--gather", default="peer", choices=["peer", "nccl"],
+                    help="multi-GPU output gather: decode-kernel stores into peer memory, or NCCL")
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
     ap.add_argument("--no-ref-gpu", action="store_true", help="skip the reference CUDA kernels leg")
     ap.add_argument("--workload", default="decode",

@@ -170,6 +170,47 @@ int sf37kv_unpack_from_host(const void *host_src, const sf37kv_pack_layer *layer
  * resets the flag. */
 int sf37kv_device_error(int clear);
 
+/* ---- multi-GPU output gather over peer memory (KV-head sharding) ----
+ * Each rank allocates one device buffer (sf37kv_dev_alloc) holding the
+ * gathered outputs [world][n_layers][q_heads_local][head_dim] f32, exports it
+ * with sf37kv_ipc_handle and maps every other rank's with sf37kv_ipc_open.
+ * peer_buf[p] / peer_flags[p]: rank p's buffer and its flag array (world
+ * u32, zero-initialized) as mapped in this process; my_flags = this rank's
+ * flag array; done_counter: one zeroed device u32 of this rank. */
+typedef struct {
+    void *peer_buf[8];
+    void *peer_flags[8];
+    void *my_flags;
+    void *done_counter;
+    uint32_t world;
+    uint32_t rank;
+} sf37kv_peer_gather;
+
+/* Zero-filled device memory (cudaMalloc; freed with sf37kv_dev_free). */
+void *sf37kv_dev_alloc(uint64_t bytes);
+void sf37kv_dev_free(void *p);
+/* CUDA IPC of a whole sf37kv_dev_alloc allocation; handle_out: 64 bytes. */
+int sf37kv_ipc_handle(void *dev_ptr, void *handle_out);
+void *sf37kv_ipc_open(const void *handle);
+void sf37kv_ipc_close(void *p);
+
+/* sf37kv_decode on this rank's KV-head slice (1..64 layers), with every
+ * output head stored into all ranks' gather buffers, laid out as f32
+ * [2][world][n_layers][q_heads][head_dim] with half (epoch & 1); layers[i].out
+ * is ignored (the output lands in this rank's own buffer at
+ * [epoch & 1][rank][i]).  This rank's epoch flag is raised in every rank's
+ * flag array after its last output is stored.  Epochs must increase by one
+ * per step, starting at 1 with zeroed flags.  Multi-GPU form of
+ * sf37_cuda_attention_decode_heads (sf37_cuda.h:108-118); the reference runs
+ * on one GPU and has no counterpart for the gather itself. */
+int sf37kv_decode_gather(const sf37kv_decode_layer *layers, uint32_t n_layers,
+                         uint32_t q_heads, uint32_t kv_heads, uint32_t head_dim,
+                         int dtype, const sf37kv_peer_gather *g, uint32_t epoch,
+                         void *stream);
+/* Waits on the stream (bounded, about 2 s) until every rank raised `epoch`;
+ * on timeout the device error flag is set to 2 (sf37kv_device_error). */
+int sf37kv_gather_wait(const sf37kv_peer_gather *g, uint32_t epoch, void *stream);
+
 /* Number of kernel launches this library has issued (process total). */
 uint64_t sf37kv_launch_count(void);
 

@@ -32,6 +32,11 @@ class AppendLayer(ctypes.Structure):
     _fields_ = [("cache", Cache), ("pos0", c_u32), ("n_tok", c_u32), ("k", c_vp), ("v", c_vp)]
 
 
+class PeerGather(ctypes.Structure):
+    _fields_ = [("peer_buf", c_vp * 8), ("peer_flags", c_vp * 8), ("my_flags", c_vp),
+                ("done_counter", c_vp), ("world", c_u32), ("rank", c_u32)]
+
+
 class PackLayer(ctypes.Structure):
     _fields_ = [("cache", Cache), ("first_pos", c_u32), ("rows", c_u32), ("offset", c_u64)]
 
@@ -88,6 +93,14 @@ SIGNATURES = {
                                         c_int, c_u32]),
     "sf37kv_launch_count": (c_u64, []),
     "sf37kv_device_error": (c_int, [c_int]),
+    "sf37kv_dev_alloc": (c_vp, [c_u64]),
+    "sf37kv_dev_free": (None, [c_vp]),
+    "sf37kv_ipc_handle": (c_int, [c_vp, c_vp]),
+    "sf37kv_ipc_open": (c_vp, [c_vp]),
+    "sf37kv_ipc_close": (None, [c_vp]),
+    "sf37kv_decode_gather": (c_int, [ctypes.POINTER(DecodeLayer), c_u32, c_u32, c_u32, c_u32, c_int,
+                                     ctypes.POINTER(PeerGather), c_u32, c_vp]),
+    "sf37kv_gather_wait": (c_int, [ctypes.POINTER(PeerGather), c_u32, c_vp]),
 }
 
 _lib = None

@@ -53,6 +53,10 @@ constexpr float kLog2e = 1.4426950408889634f;
 constexpr uint32_t kMaxSplits = 256;
 constexpr float kRescaleSlack = 8.0f;
 
+// Set by attention_jobs_gather for the duration of one attention_jobs call.
+static const GatherDev *g_gather_cur = nullptr;
+static uint64_t g_gather_off[kMaxJobs];
+
 struct JobDev {
     const void *k;
     const void *v;
@@ -62,6 +66,7 @@ struct JobDev {
     uint32_t start, end, cap;
     uint32_t split_rows, n_splits, cta_begin;
     const float *k_new, *v_new;  // appended row (position end-1) or nullptr
+    uint64_t gather_off;         // float offset of this job's block in the peers' gather buffers
 };
 
 // The CTA owning the last split of (job, kvh) stores this KV head's slice of
@@ -93,7 +98,33 @@ struct DecodeParams {
     float *part;
     uint32_t *counters;    // one per (job, kv head)
     float qscale;          // log2(e) / sqrt(head_dim)
+    GatherDev gat;
 };
+
+__device__ __forceinline__ void gather_store(const DecodeParams &P, const JobDev &J, uint64_t idx, float v) {
+    for (uint32_t p = 0; p < P.gat.world; p++)
+        if (p != P.gat.rank) P.gat.peer[p][J.gather_off + idx] = v;
+}
+__device__ __forceinline__ void gather_store4(const DecodeParams &P, const JobDev &J, uint64_t idx, float4 v) {
+    for (uint32_t p = 0; p < P.gat.world; p++)
+        if (p != P.gat.rank) *reinterpret_cast<float4 *>(P.gat.peer[p] + J.gather_off + idx) = v;
+}
+// Called by every CTA that wrote final outputs of one (job, kv head) group.
+__device__ __forceinline__ void gather_group_done(const DecodeParams &P) {
+    if (!P.gat.world) return;
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        if (atomicAdd(P.gat.done, 1u) == P.gat.total_groups - 1u) {
+            __threadfence_system();
+            for (uint32_t p = 0; p < P.gat.world; p++) {
+                uint32_t *f = P.gat.peer_flags[p] + P.gat.rank;
+                asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(f), "r"(P.gat.epoch) : "memory");
+            }
+            *P.gat.done = 0u;
+        }
+    }
+}
 
 // ------------------------------------------------------------ helpers
 __device__ __forceinline__ uint32_t locate_job(const DecodeParams &P, uint32_t cta) {
@@ -174,7 +205,9 @@ __device__ void finish_cta(const DecodeParams &P, const JobDev &J, uint32_t j, u
         if (single) {
             const uint32_t qh = kvh * G + h;
             const float g = J.gate ? sigmoid_dev(J.gate[qh]) : 1.0f;
-            J.out[(uint64_t)qh * 128u + d] = L > 0.f ? O / L * g : 0.f;
+            const float val = L > 0.f ? O / L * g : 0.f;
+            J.out[(uint64_t)qh * 128u + d] = val;
+            if (P.gat.world) gather_store(P, J, (uint64_t)qh * 128u + d, val);
         } else {
             part[h * 128u + d] = O;
             if (d == 0) {
@@ -184,7 +217,10 @@ __device__ void finish_cta(const DecodeParams &P, const JobDev &J, uint32_t j, u
         }
     }
     (void)heads_per_part;
-    if (single) return;
+    if (single) {
+        gather_group_done(P);
+        return;
+    }
 
     // Last-CTA election (threadFenceReduction pattern).
     __shared__ uint32_t s_last;
@@ -263,8 +299,10 @@ __device__ void finish_cta(const DecodeParams &P, const JobDev &J, uint32_t j, u
         r.w = L > 0.f ? acc.w / L * g : 0.f;
         (void)f;
         *reinterpret_cast<float4 *>(J.out + (uint64_t)qh * 128u + d4) = r;
+        if (P.gat.world) gather_store4(P, J, (uint64_t)qh * 128u + d4, r);
     }
     if (tid == 0) *ctr = 0u;  // ready for the next launch
+    gather_group_done(P);
 }
 
 // ------------------------------------------------------------ f16 kernel
@@ -1170,7 +1208,7 @@ static int launch_generic(const AttnJob *jobs, uint32_t n, uint32_t q_heads, uin
         for (uint32_t i = base; i < n && i < base + kMaxJobs; i++) {
             const AttnJob &A = jobs[i];
             JobDev &D = P.job[P.n_jobs++];
-            D = JobDev{A.k, A.v, A.q, A.gate, A.out, A.start, A.end, A.cap, 0, 1, 0, nullptr, nullptr};
+            D = JobDev{A.k, A.v, A.q, A.gate, A.out, A.start, A.end, A.cap, 0, 1, 0, nullptr, nullptr, 0};
         }
         const uint64_t warps = (uint64_t)P.n_jobs * q_heads;
         const unsigned grid = (unsigned)((warps + 7) / 8);
@@ -1267,6 +1305,8 @@ int attention_jobs(const AttnJob *jobs, uint32_t n, uint32_t q_heads, uint32_t k
         P.group = G;
         P.part_stride = (G * 130u + 3u) & ~3u;
         P.qscale = kLog2e / sqrtf(128.0f);
+        P.gat = g_gather_cur ? *g_gather_cur : GatherDev{};
+        if (P.gat.world) P.gat.total_groups = m * kv_heads;
         uint32_t ctas = 0;
         bool any_split = false;
         for (uint32_t i = 0; i < m; i++) {
@@ -1283,7 +1323,8 @@ int attention_jobs(const AttnJob *jobs, uint32_t n, uint32_t q_heads, uint32_t k
             if (ns > 1) any_split = true;
             JobDev &D = P.job[i];
             D = JobDev{A.k, A.v, A.q, A.gate, A.out, A.start, A.end, A.cap, sr, (uint32_t)ns, ctas,
-                       fuses ? A.k_new : nullptr, fuses ? A.v_new : nullptr};
+                       fuses ? A.k_new : nullptr, fuses ? A.v_new : nullptr,
+                       g_gather_cur ? g_gather_off[base + i] : 0};
             if ((uint64_t)ctas + ns * kv_heads > 0x7fffffffull)
                 return set_error(SF37KV_EINVAL, "attention: grid too large");
             ctas += (uint32_t)ns * kv_heads;
@@ -1530,7 +1571,7 @@ int attention_jobs_prealloc(const AttnJob *jobs, uint32_t n, uint32_t q_heads, u
             if (ns < 1) ns = 1;
             if (ns > 1) any_split = true;
             P.job[i] = JobDev{A.k, A.v, A.q, A.gate, A.out, A.start, A.end, A.cap, sr, (uint32_t)ns, ctas,
-                              nullptr, nullptr};
+                              nullptr, nullptr, 0};
             ctas += (uint32_t)ns * kv_heads;
         }
         P.total_ctas = ctas;
@@ -1540,6 +1581,7 @@ int attention_jobs_prealloc(const AttnJob *jobs, uint32_t n, uint32_t q_heads, u
     }
     P.part = part;
     P.counters = counters;
+    P.gat = GatherDev{};
     // Counters must start at zero; clear the ones this launch uses.
     if (int rc = check_cuda(cudaMemsetAsync(counters, 0, (size_t)n * kv_heads * 4u, stream),
                             "decode_noalloc counter clear"))
@@ -1560,6 +1602,26 @@ int attention_jobs_prealloc(const AttnJob *jobs, uint32_t n, uint32_t q_heads, u
     }
     g_launches++;
     return check_cuda(cudaGetLastError(), "decode_noalloc launch");
+}
+
+}  // namespace sf37kv
+
+namespace sf37kv {
+
+int attention_jobs_gather(const AttnJob *jobs, uint32_t n, uint32_t q_heads, uint32_t kv_heads,
+                          uint32_t head_dim, int dtype, cudaStream_t stream, const GatherDev *gat,
+                          const uint64_t *offsets) {
+    if (n > (uint32_t)kMaxJobs)
+        return set_error(SF37KV_EINVAL, "decode_gather: at most %d layers per call", kMaxJobs);
+    const uint32_t G = kv_heads ? q_heads / kv_heads : 0;
+    if (head_dim != 128 || G == 0 || G > 16 || (dtype == SF37KV_F32 && f32_gp(G) == 0 && getenv("SF37KV_DECODE_F32")))
+        return set_error(SF37KV_EUNSUPPORTED, "decode_gather: needs head_dim 128, group <= 16 and a fast kernel");
+    if (n == 0) return set_error(SF37KV_EINVAL, "decode_gather: no layers (the epoch flag would never rise)");
+    for (uint32_t i = 0; i < n; i++) g_gather_off[i] = offsets[i];
+    g_gather_cur = gat;
+    const int rc = attention_jobs(jobs, n, q_heads, kv_heads, head_dim, dtype, stream);
+    g_gather_cur = nullptr;
+    return rc;
 }
 
 }  // namespace sf37kv

@@ -70,6 +70,21 @@ int attention_jobs_prealloc(const AttnJob *jobs, uint32_t n, uint32_t q_heads, u
                             uint32_t head_dim, int dtype, cudaStream_t stream, float *part,
                             uint64_t part_bytes, uint32_t *counters, uint64_t n_counters);
 
+// Peer-memory output gather (multi-GPU): every final output value is also
+// stored into the gather buffer of each other rank (plain stores over
+// NVLink); the last group to finish on this GPU raises this rank's epoch flag
+// in every rank's flag array (system-scope release).  world == 0: disabled.
+struct GatherDev {
+    float *peer[8];
+    uint32_t *peer_flags[8];
+    uint32_t world, rank, epoch, total_groups;
+    uint32_t *done;  // groups finished in this launch (self-resetting)
+};
+
+int attention_jobs_gather(const AttnJob *jobs, uint32_t n, uint32_t q_heads, uint32_t kv_heads,
+                          uint32_t head_dim, int dtype, cudaStream_t stream, const GatherDev *gat,
+                          const uint64_t *offsets);
+
 // Logical start row of the query at position pos (sf37_cuda.cu:2752-2758).
 static inline uint32_t start_at(uint32_t pos, uint32_t cap, int sliding, uint32_t window) {
     const uint32_t have = pos + 1u;

@@ -104,7 +104,7 @@ def decode_layers_desc(layers):
     for i, L in enumerate(layers):
         arr[i] = DecodeLayer(cache_desc(L["k_cache"], L["v_cache"], L["cap"], L.get("sliding", 0),
                                         L.get("window", 512)), L["pos"], 0, _ptr(L["q"]),
-                             _ptr(L.get("gate")), _ptr(L["out"]), _ptr(L.get("k_new")),
+                             _ptr(L.get("gate")), _ptr(L.get("out")), _ptr(L.get("k_new")),
                              _ptr(L.get("v_new")))
     return arr
 
@@ -177,3 +177,8 @@ def set_stream(stream):
 
 def launch_count() -> int:
     return int(lib().sf37kv_launch_count())
+
+
+def device_error(clear=False) -> int:
+    """The device error flag (0 = none, 2 = a bounded wait timed out); syncs."""
+    return lib().sf37kv_device_error(int(bool(clear)))

@@ -64,3 +64,88 @@ def gather_outputs(out_local: torch.Tensor, plan: ShardPlan, group=None, gathere
     else:
         dist.all_gather(list(gathered.unbind(0)), out_local.contiguous(), group=group)
     return gathered.permute(1, 0, 2, 3).reshape(out_local.shape[0], plan.q_heads, out_local.shape[-1])
+
+
+class _CudaArray:
+    """__cuda_array_interface__ wrapper so torch can view library memory."""
+
+    def __init__(self, ptr, shape, typestr="<f4"):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr,
+                                         "data": (int(ptr), False), "version": 2}
+
+
+class PeerGather:
+    """Output gather over peer memory for sf37kv_decode_gather (see
+    include/sf37kv.h): one zero-filled device buffer per rank holding
+    [world][n_layers][q_local][head_dim] f32 outputs followed by the rank flag
+    array and a done counter, shared with the other ranks by CUDA IPC."""
+
+    def __init__(self, plan: ShardPlan, n_layers: int, group=None):
+        import ctypes
+        from ._lib import PeerGather as PG, lib
+        self.plan, self.n_layers = plan, n_layers
+        L = lib()
+        self._lib = L
+        floats = 2 * plan.world * n_layers * plan.q_local * plan.head_dim
+        self.off_flags = (floats * 4 + 255) // 256 * 256
+        self.off_done = self.off_flags + 256
+        self.base = L.sf37kv_dev_alloc(self.off_done + 256)
+        if not self.base:
+            raise RuntimeError("sf37kv_dev_alloc failed")
+        h = ctypes.create_string_buffer(64)
+        if L.sf37kv_ipc_handle(self.base, h):
+            raise RuntimeError("sf37kv_ipc_handle failed")
+        torch.cuda.synchronize()
+        handles = [None] * plan.world
+        dist.all_gather_object(handles, bytes(h.raw), group=group)
+        self.peers = []
+        st = PG()
+        for p in range(plan.world):
+            if p == plan.rank:
+                ptr = self.base
+            else:
+                ptr = L.sf37kv_ipc_open(ctypes.create_string_buffer(handles[p], 64))
+                if not ptr:
+                    raise RuntimeError(f"sf37kv_ipc_open of rank {p} failed")
+                self.peers.append(ptr)
+            st.peer_buf[p] = ptr
+            st.peer_flags[p] = ptr + self.off_flags
+        st.my_flags = self.base + self.off_flags
+        st.done_counter = self.base + self.off_done
+        st.world, st.rank = plan.world, plan.rank
+        self.struct = st
+        self.epoch = 0
+        self.gathered = torch.as_tensor(
+            _CudaArray(self.base, (2, plan.world, n_layers, plan.q_local, plan.head_dim)), device="cuda")
+        dist.barrier(group=group)
+
+    def heads(self) -> torch.Tensor:
+        """[n_layers, q_heads, head_dim] outputs of the last completed step
+        (valid on the stream after step(); a copy, since the half is reused
+        two steps later)."""
+        g = self.gathered[self.epoch & 1]
+        return g.permute(1, 0, 2, 3).reshape(self.n_layers, self.plan.q_heads, self.plan.head_dim)
+
+    def step(self, descs, dtype, stream=None):
+        """Decode this rank's slice, store outputs into every rank, wait for all."""
+        import ctypes
+        from ._lib import check
+        from .kv import decode_layers_desc
+        if isinstance(descs, list):
+            descs = decode_layers_desc(descs)
+        if len(descs) != self.n_layers:
+            raise ValueError(f"PeerGather was set up for {self.n_layers} layers, got {len(descs)}")
+        self.epoch += 1
+        sp = None if stream is None else ctypes.c_void_p(stream.cuda_stream)
+        check(self._lib.sf37kv_decode_gather(descs, len(descs), self.plan.q_local, self.plan.kv_local,
+                                             self.plan.head_dim, dtype, ctypes.byref(self.struct),
+                                             self.epoch, sp), "sf37kv_decode_gather")
+        check(self._lib.sf37kv_gather_wait(ctypes.byref(self.struct), self.epoch, sp), "sf37kv_gather_wait")
+
+    def close(self):
+        for p in self.peers:
+            self._lib.sf37kv_ipc_close(p)
+        self.peers = []
+        if self.base:
+            self._lib.sf37kv_dev_free(self.base)
+            self.base = None

@@ -1,5 +1,6 @@
 """GPU, 2 ranks over NCCL (needs >= 2 GPUs): KV-head-sharded decode through
-the C ABI plus the output all-gather equals the oracle on the full heads."""
+the C ABI plus the output gather (NCCL all-gather, or the decode kernels'
+own stores into peer memory) equals the oracle on the full heads."""
 import os
 import socket
 
@@ -13,10 +14,11 @@ pytestmark = [pytest.mark.gpu,
                                  reason="needs 2 GPUs")]
 
 
-def _worker(rank, world, port, result):
+def _worker(rank, world, port, result, mode="nccl"):
     import torch.distributed as dist
     from sf37_b200 import kv, synth
-    from sf37_b200.shard import ShardPlan, gather_outputs
+    from sf37_b200._lib import lib
+    from sf37_b200.shard import PeerGather, ShardPlan, gather_outputs
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
     dist.init_process_group("nccl", rank=rank, world_size=world)
@@ -31,15 +33,31 @@ def _worker(rank, world, port, result):
         descs.append(dict(k_cache=plan.slice_rows(k).half().contiguous(),
                           v_cache=plan.slice_rows(v).half().contiguous(), cap=cap, pos=pos,
                           q=plan.slice_q(q).contiguous(), out=outs[l]))
-    kv.decode(descs, plan.q_local, plan.kv_local, 128, kv.F16)
-    full = gather_outputs(outs, plan)
+    if mode == "nccl":
+        kv.decode(descs, plan.q_local, plan.kv_local, 128, kv.F16)
+        full = gather_outputs(outs, plan)
+        got = [full.cpu().numpy()]
+    else:
+        # three steps at positions 4997..4999 exercise both buffer halves
+        pg = PeerGather(plan, layers)
+        got = []
+        for p in (4997, 4998, 4999):
+            for d in descs:
+                d["pos"] = p
+            pg.step(descs, kv.F16)
+            got.append(pg.heads().cpu().numpy())
+        assert lib().sf37kv_device_error(1) == 0
+        dist.barrier()
+        torch.cuda.synchronize()
+        pg.close()
     if rank == 0:
-        result.put(full.cpu().numpy())
+        result.put(got)
     dist.barrier()
     dist.destroy_process_group()
 
 
-def test_sharded_decode_2gpu():
+@pytest.mark.parametrize("mode", ["nccl", "peer"])
+def test_sharded_decode_2gpu(mode):
     import oracle
     from sf37_b200 import synth
     from tests.helpers import assert_close
@@ -49,15 +67,18 @@ def test_sharded_decode_2gpu():
     s.close()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    ps = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    ps = [ctx.Process(target=_worker, args=(r, 2, port, q, mode)) for r in range(2)]
     for p in ps:
         p.start()
     got = q.get(timeout=300)
     for p in ps:
         p.join(timeout=120)
         assert p.exitcode == 0
+    positions = [4999] if mode == "nccl" else [4997, 4998, 4999]
+    assert len(got) == len(positions)
     for l in range(4):
         k = oracle.f16_bits_to_f32(oracle.f32_to_f16_bits(synth.normal(10 + l, (5000, 1024))))
         v = oracle.f16_bits_to_f32(oracle.f32_to_f16_bits(synth.normal(20 + l, (5000, 1024))))
-        want = oracle.attention_decode_at(synth.normal(30 + l, (64, 128)), k, v, None, 4999, 5000, 64, 8, 128)
-        assert_close(got[l], want)
+        for step, pos in enumerate(positions):
+            want = oracle.attention_decode_at(synth.normal(30 + l, (64, 128)), k, v, None, pos, 5000, 64, 8, 128)
+            assert_close(got[step][l], want)
