@@ -387,7 +387,11 @@ def run_ours(args, rank, world):
                     for l in range(LAYERS))
     peak, peak_kind = _peaks()
     achieved = att_bytes / (att_ms * 1e-3) / 1e9
+    # ncu DRAM bytes of the full 8-KV-head launch; a rank's launch reads
+    # kvh_l/8 of the same rows, so the capture scales by that share
     traffic = _traffic_from_profiles("decode_f16_pipe_cfg2.md") if (LAYERS == 48 and wl == "decode") else None
+    if traffic is not None:
+        traffic *= kvh_l / KVH
 
     # End-to-end leg through the C ABI with host buffers: every step copies its
     # inputs (q, gate, new K/V rows) in from pinned host memory and its

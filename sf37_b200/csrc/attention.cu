@@ -1289,12 +1289,24 @@ int attention_jobs(const AttnJob *jobs, uint32_t n, uint32_t q_heads, uint32_t k
             if (per < 128) per = 128;
             const uint64_t ctas1 = (uint64_t)m * kv_heads;
             if (ctas1 <= slots) {
-                // per-job split count from the wave size (jobs of similar length)
-                const uint64_t ns = slots / ctas1;
+                // Per-job split count (jobs of similar length): the one whose
+                // CTAs fill whole waves best, i.e. the fewest waves per unit of
+                // work, ceil(ns * ctas1 / slots) / ns; ties go to fewer splits
+                // (cheaper merge).  E.g. 192 groups on 296 slots: 3 splits
+                // (1.95 waves) rather than 1 (192 CTAs, 44 SMs doubly loaded).
+                uint64_t ns = 1;
+                double best = 1e30;
+                for (uint64_t c = 1; c <= slots / ctas1 * 2 + 2 && c <= kMaxSplits; c++) {
+                    const double cost = (double)((c * ctas1 + slots - 1) / slots) / (double)c;
+                    if (cost < best * 0.95) {
+                        best = cost;
+                        ns = c;
+                    }
+                }
                 uint64_t longest = 0;
                 for (uint32_t i = 0; i < m; i++) longest = std::max<uint64_t>(longest, jobs[base + i].end - jobs[base + i].start);
-                const uint64_t per2 = ((longest + ns - 1) / ns + 127) / 128 * 128;
-                if (per2 > per) per = per2;
+                per = ((longest + ns - 1) / ns + 127) / 128 * 128;
+                if (per < 128) per = 128;
             }
         }
         if (const char *e = getenv("SF37KV_SPLIT_ROWS")) per = strtoull(e, nullptr, 10) ? strtoull(e, nullptr, 10) : per;
