@@ -78,3 +78,31 @@ def test_native_rejects_bad_dtype_and_format():
     pk = (_lib.PackLayer * 1)()
     assert L.sf37kv_pack(None, pk, 1, 1024, 2, 7, 64, 1, None) == 1  # EINVAL: fmt
     assert L.sf37kv_pack(None, pk, 1, 1024, 2, 1, 48, 1, None) == 4  # EUNSUPPORTED: group
+
+
+def test_gather_rejects_bad_descriptors_without_launching():
+    L = _lib.lib()
+    lay = (_lib.DecodeLayer * 1)()
+    lay[0].cache.cap = 16
+    lay[0].cache.k_cache = lay[0].cache.v_cache = lay[0].q = 16
+    g = _lib.PeerGather()
+    g.world, g.rank = 9, 0
+    assert L.sf37kv_decode_gather(lay, 1, 8, 1, 128, 2, ctypes.byref(g), 1, None) == 1
+    assert "world" in _lib.last_error()
+    g.world, g.rank = 2, 2
+    assert L.sf37kv_decode_gather(lay, 1, 8, 1, 128, 2, ctypes.byref(g), 1, None) == 1
+    g.rank = 1
+    g.peer_buf[0] = g.peer_flags[0] = 256
+    # peer 1's buffer is NULL
+    assert L.sf37kv_decode_gather(lay, 1, 8, 1, 128, 2, ctypes.byref(g), 1, None) == 1
+    assert "peer 1" in _lib.last_error()
+    g.peer_buf[1] = g.peer_flags[1] = 512
+    # no done counter
+    assert L.sf37kv_decode_gather(lay, 1, 8, 1, 128, 2, ctypes.byref(g), 1, None) == 1
+    g.done_counter = 1024
+    # zero layers would never raise the epoch flag
+    assert L.sf37kv_decode_gather(lay, 0, 8, 1, 128, 2, ctypes.byref(g), 1, None) == 1
+    assert "no layers" in _lib.last_error()
+    # head_dim 64 has no gather kernel
+    assert L.sf37kv_decode_gather(lay, 1, 8, 1, 64, 2, ctypes.byref(g), 1, None) == 4
+    assert L.sf37kv_gather_wait(None, 1, None) == 1
