@@ -13,6 +13,8 @@
  *   payload_encode_kv_row_i8_grouped   sf37.c:6633-6659
  *   payload_decode_kv_row_i8_grouped   sf37.c:6661-6674
  *   payload_encoded_kv_row_bytes       sf37.c:6628-6631
+ *   sf37_session_save_snapshot / _load_snapshot  sf37.c:7235-7500
+ *   sf37_session_save_payload / _load_payload    sf37.c:6922-7233
  */
 #include "sf37.c"
 
@@ -124,4 +126,93 @@ int sf37ref_decode_step_layers(float **k, float **v, uint32_t *n_live, uint32_t 
     }
     for (uint32_t t = 0; t < started; t++) pthread_join(th[t], NULL);
     return 1;
+}
+
+/* ---- session checkpoints through the reference's own writers/loaders ----
+ * A CPU-backend sf37_session (no engine, sf37.c:4510-4533) is filled with
+ * the given state and handed to sf37_session_save_snapshot (sf37.c:7235),
+ * sf37_session_save_payload (6922), sf37_session_load_snapshot (7347) or
+ * sf37_session_load_payload (7038).  On the CPU backend a layer's live rows
+ * are layer->k / layer->v rows [n - rows, n) (sf37.c:7322-7336), and the raw
+ * snapshot stores a layer's K rows followed by its V rows; the payload rows
+ * are K, V interleaved as on the CUDA backend. */
+static void sf37ref_session_init(sf37_session *s, int ctx, const int *tokens, int n_tokens,
+                                 float *logits, float *hidden, float **k, float **v,
+                                 const uint32_t *n_rows) {
+    memset(s, 0, sizeof(*s));
+    s->ctx_size = ctx;
+    s->checkpoint.v = (int *)malloc(sizeof(int) * (size_t)(n_tokens > 0 ? n_tokens : 1));
+    if (n_tokens > 0) memcpy(s->checkpoint.v, tokens, sizeof(int) * (size_t)n_tokens);
+    s->checkpoint.len = n_tokens;
+    s->checkpoint.cap = n_tokens > 0 ? n_tokens : 1;
+    s->checkpoint_valid = true;
+    s->logits = logits;
+    s->hidden = hidden;
+    for (uint32_t il = 0; il < SF37_MAIN_LAYERS; il++) {
+        s->cpu_cache.layer[il].k = k[il];
+        s->cpu_cache.layer[il].v = v[il];
+        s->cpu_cache.layer[il].n = n_rows ? n_rows[il] : 0;
+        s->cpu_cache.layer[il].cap = (uint32_t)ctx;
+    }
+    s->cpu_cache.cap = (uint32_t)ctx;
+}
+
+/* kind 0: raw snapshot, 1: payload.  Returns the bytes written into out,
+ * or -1 with the reference's message in err. */
+int64_t sf37ref_session_save(int kind, int ctx, const int *tokens, int n_tokens, float *logits,
+                             float *hidden, float **k, float **v, const uint32_t *n_rows,
+                             uint8_t *out, uint64_t out_cap, char *err, size_t errlen) {
+    sf37_session s;
+    sf37ref_session_init(&s, ctx, tokens, n_tokens, logits, hidden, k, v, n_rows);
+    int64_t n = -1;
+    if (kind == 0) {
+        sf37_session_snapshot snap = {0};
+        if (sf37_session_save_snapshot(&s, &snap, err, errlen) == 0 && snap.len <= out_cap) {
+            memcpy(out, snap.ptr, (size_t)snap.len);
+            n = (int64_t)snap.len;
+        }
+        sf37_session_snapshot_free(&snap);
+    } else {
+        FILE *fp = tmpfile();
+        if (fp && sf37_session_save_payload(&s, fp, err, errlen) == 0) {
+            const long len = ftell(fp);
+            rewind(fp);
+            if (len >= 0 && (uint64_t)len <= out_cap && fread(out, 1, (size_t)len, fp) == (size_t)len)
+                n = len;
+        }
+        if (fp) fclose(fp);
+    }
+    free(s.checkpoint.v);
+    return n;
+}
+
+/* Loads buf into a CPU session of context ctx whose layer caches k[il],
+ * v[il] hold ctx rows each.  Returns the reference's code (0 = success);
+ * on success n_rows[il] = the rows restored, tokens / *n_tokens / logits /
+ * hidden are written. */
+int sf37ref_session_load(int kind, const uint8_t *buf, uint64_t len, int ctx, int *tokens,
+                         int *n_tokens, float *logits, float *hidden, float **k, float **v,
+                         uint32_t *n_rows, char *err, size_t errlen) {
+    sf37_session s;
+    sf37ref_session_init(&s, ctx, NULL, 0, logits, hidden, k, v, NULL);
+    int rc;
+    if (kind == 0) {
+        sf37_session_snapshot snap = {(uint8_t *)buf, len, len};
+        rc = sf37_session_load_snapshot(&s, &snap, err, errlen);
+    } else {
+        FILE *fp = tmpfile();
+        rc = 1;
+        if (fp && fwrite(buf, 1, (size_t)len, fp) == (size_t)len) {
+            rewind(fp);
+            rc = sf37_session_load_payload(&s, fp, len, err, errlen);
+        }
+        if (fp) fclose(fp);
+    }
+    if (rc == 0) {
+        *n_tokens = s.checkpoint.len;
+        if (s.checkpoint.len > 0) memcpy(tokens, s.checkpoint.v, sizeof(int) * (size_t)s.checkpoint.len);
+        for (uint32_t il = 0; il < SF37_MAIN_LAYERS; il++) n_rows[il] = s.cpu_cache.layer[il].n;
+    }
+    free(s.checkpoint.v);
+    return rc;
 }

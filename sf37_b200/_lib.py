@@ -41,7 +41,20 @@ class PackLayer(ctypes.Structure):
     _fields_ = [("cache", Cache), ("first_pos", c_u32), ("rows", c_u32), ("offset", c_u64)]
 
 
+class SessionLayout(ctypes.Structure):
+    _fields_ = [("n_layers", c_u32), ("kv_heads", c_u32), ("head_dim", c_u32), ("vocab", c_u32),
+                ("embd", c_u32), ("sliding_window", c_u32), ("full_every", c_u32),
+                ("payload_group", c_u32)]
+
+
+class Session(ctypes.Structure):
+    _fields_ = [("layout", SessionLayout), ("ctx_size", ctypes.c_int32), ("n_tokens", c_u32),
+                ("tokens", c_vp), ("logits", c_vp), ("hidden", c_vp), ("caches", ctypes.POINTER(Cache)),
+                ("dtype", c_int), ("backend_kind", c_u32)]
+
+
 TP = ctypes.POINTER(Tensor)
+SP = ctypes.POINTER(Session)
 
 # name -> (restype, argtypes); every symbol include/*.h declares.
 SIGNATURES = {
@@ -101,6 +114,15 @@ SIGNATURES = {
     "sf37kv_decode_gather": (c_int, [ctypes.POINTER(DecodeLayer), c_u32, c_u32, c_u32, c_u32, c_int,
                                      ctypes.POINTER(PeerGather), c_u32, c_vp]),
     "sf37kv_gather_wait": (c_int, [ctypes.POINTER(PeerGather), c_u32, c_vp]),
+    # include/sf37kv_session.h
+    "sf37kv_session_layout_default": (SessionLayout, []),
+    "sf37kv_session_snapshot_bytes": (c_u64, [SP]),
+    "sf37kv_session_payload_bytes": (c_u64, [SP]),
+    "sf37kv_session_save_snapshot": (c_int, [SP, c_vp, c_u64, ctypes.POINTER(c_u64), ctypes.c_char_p,
+                                             ctypes.c_size_t]),
+    "sf37kv_session_load_snapshot": (c_int, [SP, c_vp, c_u64, ctypes.c_char_p, ctypes.c_size_t]),
+    "sf37kv_session_save_payload": (c_int, [SP, c_int, ctypes.c_char_p, ctypes.c_size_t]),
+    "sf37kv_session_load_payload": (c_int, [SP, c_int, c_u64, ctypes.c_char_p, ctypes.c_size_t]),
 }
 
 _lib = None

@@ -41,6 +41,14 @@ int scratch_get(uint64_t part_bytes, uint64_t n_counters, Scratch *out);
 void scratch_release();
 void staging_release();  // snapshot staging buffers
 
+// Snapshot sections streamed through pinned chunks to / from a host callback
+// (returns nonzero to stop; the call then fails with SF37KV_EINVAL and the
+// callback's own message stays the last error).  Synchronous.
+int pack_stream(const sf37kv_pack_layer *layers, uint32_t n, uint32_t kv_dim, int dtype, int fmt,
+                uint32_t group, int (*sink)(const void *, uint64_t, void *), void *ctx);
+int unpack_stream(const sf37kv_pack_layer *layers, uint32_t n, uint32_t kv_dim, int dtype, int fmt,
+                  uint32_t group, int (*source)(void *, uint64_t, void *), void *ctx);
+
 // ---------------------------------------------------------------- attention
 // One attention "job": one query vector set (q_heads heads) over logical
 // rows [start, end) of one cache.  A decode layer is one job; a prefill token

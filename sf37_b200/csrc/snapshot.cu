@@ -421,12 +421,144 @@ static int host_pipeline(void *host, const sf37kv_pack_layer *layers, uint32_t n
     return SF37KV_OK;
 }
 
+// ---------------------------------------------------------------- streams
+// Packed bytes to / from a host callback (a file descriptor, a socket) in
+// chunks of at most kStageBytes, through two pinned host buffers: the device
+// packs and copies chunk c while the host consumes chunk c-1 (pack), or the
+// host produces chunk c while the device copies in and unpacks chunk c-1
+// (unpack).  A chunk is a run of whole rows of one or more consecutive layer
+// sections, so the callback sees the sections' bytes in order.
+static void *g_hbuf[2] = {nullptr, nullptr};
+static cudaEvent_t g_ev_host[2];
+
+static int host_buffers_init() {
+    if (int rc = staging_init()) return rc;
+    if (g_hbuf[0]) return SF37KV_OK;
+    for (int i = 0; i < 2; i++) {
+        if (int rc = check_cuda(cudaHostAlloc(&g_hbuf[i], kStageBytes, cudaHostAllocDefault), "pinned stream buffer"))
+            return rc;
+        if (int rc = check_cuda(cudaEventCreateWithFlags(&g_ev_host[i], cudaEventDisableTiming), "event")) return rc;
+    }
+    return SF37KV_OK;
+}
+
+namespace {
+struct Chunk {
+    sf37kv_pack_layer piece[kMaxJobs];
+    uint32_t n = 0;
+    uint64_t bytes = 0;
+};
+
+// Cuts the layer sections into chunks of whole rows, each <= cap_bytes.
+struct Chunker {
+    const sf37kv_pack_layer *layers;
+    uint32_t n_layers, li = 0;
+    uint64_t r0 = 0, rb, cap_rows;
+    bool next(Chunk *c) {
+        c->n = 0;
+        c->bytes = 0;
+        uint64_t room = cap_rows;
+        while (li < n_layers && room > 0 && c->n < (uint32_t)kMaxJobs) {
+            const sf37kv_pack_layer &L = layers[li];
+            const uint64_t left = L.rows - r0;
+            if (left == 0) {
+                li++;
+                r0 = 0;
+                continue;
+            }
+            const uint64_t take = left < room ? left : room;
+            sf37kv_pack_layer p = L;
+            p.first_pos = L.first_pos + (uint32_t)r0;
+            p.rows = (uint32_t)take;
+            p.offset = c->bytes;
+            c->piece[c->n++] = p;
+            c->bytes += 2ull * take * rb;
+            room -= take;
+            r0 += take;
+            if (r0 == L.rows) {
+                li++;
+                r0 = 0;
+            }
+        }
+        return c->n > 0;
+    }
+};
+}  // namespace
+
+int pack_stream(const sf37kv_pack_layer *layers, uint32_t n, uint32_t kv_dim, int dtype, int fmt,
+                uint32_t group, int (*sink)(const void *, uint64_t, void *), void *ctx) {
+    if (int rc = validate(kv_dim, dtype, fmt, group)) return rc;
+    if (int rc = host_buffers_init()) return rc;
+    const uint64_t rb = row_bytes_of(kv_dim, fmt, group);
+    Chunker ck{layers, n, 0, 0, rb, kStageBytes / (2 * rb)};
+    if (ck.cap_rows == 0) return set_error(SF37KV_EUNSUPPORTED, "pack: row larger than staging");
+    cudaEventRecord(g_ev_start, current_stream());
+    cudaStreamWaitEvent(g_work_stream, g_ev_start, 0);
+    Chunk c;
+    uint64_t pending[2] = {0, 0};
+    int b = 0, rc = SF37KV_OK;
+    bool have_prev = false;
+    while (rc == SF37KV_OK && ck.next(&c)) {
+        // buffer b was consumed by the host before the previous iteration ended
+        rc = launch_layers(g_stage[b], c.piece, c.n, kv_dim, dtype, fmt, group, 1, 0, g_work_stream);
+        if (!rc) rc = check_cuda(cudaMemcpyAsync(g_hbuf[b], g_stage[b], c.bytes, cudaMemcpyDeviceToHost,
+                                                 g_work_stream), "stream D2H");
+        if (!rc) rc = check_cuda(cudaEventRecord(g_ev_host[b], g_work_stream), "event");
+        pending[b] = c.bytes;
+        if (!rc && have_prev) {
+            rc = check_cuda(cudaEventSynchronize(g_ev_host[b ^ 1]), "stream sync");
+            if (!rc && sink(g_hbuf[b ^ 1], pending[b ^ 1], ctx)) rc = SF37KV_EINVAL;
+        }
+        have_prev = true;
+        b ^= 1;
+    }
+    if (!rc && have_prev) {
+        rc = check_cuda(cudaEventSynchronize(g_ev_host[b ^ 1]), "stream sync");
+        if (!rc && sink(g_hbuf[b ^ 1], pending[b ^ 1], ctx)) rc = SF37KV_EINVAL;
+    }
+    (void)cudaStreamSynchronize(g_work_stream);
+    return rc;
+}
+
+int unpack_stream(const sf37kv_pack_layer *layers, uint32_t n, uint32_t kv_dim, int dtype, int fmt,
+                  uint32_t group, int (*source)(void *, uint64_t, void *), void *ctx) {
+    if (int rc = validate(kv_dim, dtype, fmt, group)) return rc;
+    if (int rc = host_buffers_init()) return rc;
+    const uint64_t rb = row_bytes_of(kv_dim, fmt, group);
+    Chunker ck{layers, n, 0, 0, rb, kStageBytes / (2 * rb)};
+    if (ck.cap_rows == 0) return set_error(SF37KV_EUNSUPPORTED, "pack: row larger than staging");
+    cudaEventRecord(g_ev_start, current_stream());
+    cudaStreamWaitEvent(g_work_stream, g_ev_start, 0);
+    Chunk c;
+    int b = 0, rc = SF37KV_OK;
+    bool used[2] = {false, false};
+    while (rc == SF37KV_OK && ck.next(&c)) {
+        // the H2D copy of chunk c-2 out of this host buffer must be done
+        if (used[b]) rc = check_cuda(cudaEventSynchronize(g_ev_host[b]), "stream sync");
+        if (!rc && source(g_hbuf[b], c.bytes, ctx)) rc = SF37KV_EINVAL;
+        if (!rc) rc = check_cuda(cudaMemcpyAsync(g_stage[b], g_hbuf[b], c.bytes, cudaMemcpyHostToDevice,
+                                                 g_work_stream), "stream H2D");
+        if (!rc) rc = check_cuda(cudaEventRecord(g_ev_host[b], g_work_stream), "event");
+        if (!rc) rc = launch_layers(g_stage[b], c.piece, c.n, kv_dim, dtype, fmt, group, 1, 1, g_work_stream);
+        used[b] = true;
+        b ^= 1;
+    }
+    const int rs = check_cuda(cudaStreamSynchronize(g_work_stream), "stream sync");
+    return rc ? rc : rs;
+}
+
 void staging_release() {
-    for (int i = 0; i < 2; i++)
+    for (int i = 0; i < 2; i++) {
         if (g_stage[i]) {
             cudaFree(g_stage[i]);
             g_stage[i] = nullptr;
         }
+        if (g_hbuf[i]) {
+            cudaFreeHost(g_hbuf[i]);
+            g_hbuf[i] = nullptr;
+            cudaEventDestroy(g_ev_host[i]);
+        }
+    }
 }
 
 }  // namespace sf37kv

@@ -13,6 +13,8 @@ Fixtures (all inputs are regenerable from the seeds in sf37_b200.synth):
                     output without and with the sigmoid gate
   sliding_decode.npz 96 Q heads (group 12), 600 rows, sliding window 512
   kv_push.npz       kv_cache_push of 6 rows into a capacity-4 linear cache
+  sessions.npz      session snapshot / payload bytes and loader messages
+                    (see sessions() below)
 """
 import os
 import sys
@@ -67,5 +69,38 @@ def main():
     print("golden fixtures written to", OUT)
 
 
+
+def sessions():
+    """sessions.npz: the reference's own sf37_session_save_snapshot and
+    sf37_session_save_payload on a CPU session (ctx 3, 2 tokens, values on a
+    1/2 grid), and the message its loaders give for each corruption in
+    tests/session_cases.py (both loaders, on the reference's own bytes)."""
+    from oracle import session as S
+    from tests import session_cases as C
+    ctx, n = 3, 2
+    toks, lg, hd, kc, vc = C.state(7, ctx, n, [ctx] * C.LAYERS, coarse=True)
+    rows = S.layer_rows(n, ctx, [ctx] * C.LAYERS)
+    kr = [C.live_rows_in_order(kc[i], n, rows[i], ctx) for i in range(C.LAYERS)]
+    vr = [C.live_rows_in_order(vc[i], n, rows[i], ctx) for i in range(C.LAYERS)]
+    snap = S.ref_session_save(0, ctx, toks, lg, hd, kr, vr)
+    pay = S.ref_session_save(1, ctx, toks, lg, hd, kr, vr)
+    names, msgs = [], []
+    for kind, buf in ((0, snap), (1, pay)):
+        for name, bad, lctx in C.corruptions(kind, buf, ctx):
+            try:
+                S.ref_session_load(kind, bad, lctx)
+                msg = ""
+            except S.LoadError as e:
+                msg = str(e)
+            names.append(f"{kind}:{name}")
+            msgs.append(msg)
+    np.savez_compressed(os.path.join(OUT, "sessions.npz"), snapshot=np.frombuffer(snap, np.uint8),
+                        payload=np.frombuffer(pay, np.uint8), names=np.array(names), msgs=np.array(msgs))
+
+
 if __name__ == "__main__":
-    main()
+    if len(sys.argv) > 1 and sys.argv[1] == "sessions":
+        sessions()
+    else:
+        main()
+        sessions()
