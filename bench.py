@@ -652,6 +652,7 @@ def run_snapshot(args, rank, world):
                      "device_pack_GBps": (kv_read + total) / (ms * 1e-3) / 1e9,
                      "host_pack_s": t_pack, "host_pack_GBps": total / t_pack / 1e9,
                      "host_restore_s": t_unpack, "host_restore_GBps": total / t_unpack / 1e9}
+    sess = session_leg(dev, layers, kd, rows) if world == 1 else None
     if rank != 0:
         return
     peak, kind = _peaks()
@@ -665,7 +666,83 @@ def run_snapshot(args, rank, world):
         "formats": res,
         "roofline": {"bound": "hbm", "kernel": "pack_kernel (raw, device buffer)",
                      "achieved": r["device_pack_GBps"], "peak": peak, "peak_kind": kind, "unit": "GB/s",
-                     "frac": r["device_pack_GBps"] / peak}}), flush=True)
+                     "frac": r["device_pack_GBps"] / peak},
+        "session": sess}), flush=True)
+
+
+def session_leg(dev, layers, kd, rows):
+    """Whole session checkpoints through sf37kv_session_* (48 f16 layers of
+    `rows` live rows): the payload written to a file and read back, and the
+    raw snapshot written to pinned memory; beside it, the reference's own
+    CUDA-backend per-row loops (two synchronous 4 KiB tensor reads per row,
+    its own encoder and fwrite) timed on one fp32 layer and scaled to 48."""
+    import ctypes
+    import shutil
+    import tempfile
+    import torch
+    from sf37_b200.session import Session, default_layout
+    L = default_layout()
+    L.n_layers = len(layers)
+    s = Session(rows, [(d["k_cache"], d["v_cache"]) for d in layers], layout=L)
+    s.set_tokens(np.arange(rows) % L.vocab)
+    out = {}
+    d = "/dev/shm" if shutil.disk_usage("/dev/shm").free > 2 * s.payload_bytes() else tempfile.gettempdir()
+    with tempfile.NamedTemporaryFile(dir=d) as f:
+        t0 = time.perf_counter()
+        nb = s.save_payload(f)
+        os.fsync(f.fileno())
+        out["payload_save_s"] = time.perf_counter() - t0
+        f.seek(0)
+        t0 = time.perf_counter()
+        s.load_payload(f.fileno(), nb)
+        out["payload_load_s"] = time.perf_counter() - t0
+    out.update(payload_bytes=nb, file_dir=d, payload_save_GBps=nb / out["payload_save_s"] / 1e9,
+               payload_load_GBps=nb / out["payload_load_s"] / 1e9)
+    buf = torch.empty(s.snapshot_bytes(), dtype=torch.uint8, pin_memory=True)
+    s.save_snapshot(buf)  # page-in
+    t0 = time.perf_counter()
+    s.save_snapshot(buf)
+    out["snapshot_save_s"] = time.perf_counter() - t0
+    t0 = time.perf_counter()
+    s.load_snapshot(buf)
+    out["snapshot_load_s"] = time.perf_counter() - t0
+    out["snapshot_bytes"] = buf.numel()
+    del buf
+    try:
+        import oracle
+        if not (oracle.ref_available() and oracle.ref_cuda_available()):
+            raise RuntimeError("oracle/_ref not built")
+        R = oracle.ref()
+        RC = oracle.ref_cuda()
+        rd = ctypes.cast(RC.sf37_cuda_tensor_read, ctypes.c_void_p)
+        R.sf37ref_payload_rows_cuda.argtypes = [ctypes.c_void_p] * 3 + [ctypes.c_uint32] * 3 + [ctypes.c_int]
+        R.sf37ref_snapshot_rows_cuda.argtypes = [ctypes.c_void_p] * 3 + [ctypes.c_uint32] * 3 + [ctypes.c_void_p]
+        k = layers[0]["k_cache"].float()
+        v = layers[0]["v_cache"].float()
+        kt = oracle.RefTensor(k.data_ptr(), k.numel() * 4)
+        vt = oracle.RefTensor(v.data_ptr(), v.numel() * 4)
+        torch.cuda.synchronize(dev)
+        with open(os.devnull, "wb") as f:
+            t0 = time.perf_counter()
+            rc = R.sf37ref_payload_rows_cuda(rd, ctypes.addressof(kt), ctypes.addressof(vt), 0, rows, rows,
+                                             f.fileno())
+            t_pay = time.perf_counter() - t0
+        host = np.empty(2 * rows * kd * 4, np.uint8)
+        t0 = time.perf_counter()
+        rc |= R.sf37ref_snapshot_rows_cuda(rd, ctypes.addressof(kt), ctypes.addressof(vt), 0, rows, rows,
+                                           host.ctypes.data)
+        t_snap = time.perf_counter() - t0
+        if rc:
+            raise RuntimeError("reference row loop failed")
+        n = len(layers)
+        out["reference_per_row"] = {
+            "payload_save_s": t_pay * n, "snapshot_save_s": t_snap * n,
+            "sample": f"1 of {n} layers ({rows} rows, fp32 cache: the reference's only type), x{n}",
+            "payload_speedup": t_pay * n / out["payload_save_s"],
+            "snapshot_speedup": t_snap * n / out["snapshot_save_s"]}
+    except Exception as e:  # the reference library is test infrastructure
+        out["reference_per_row"] = {"unavailable": str(e)}
+    return out
 
 
 def run_prefill(args, rank, world):

@@ -19,6 +19,7 @@
 #include "sf37.c"
 
 #include <pthread.h>
+#include <unistd.h>
 
 /* One linear CPU layer cache, as sf37_layer_kv_cache (sf37.c:199-204). */
 uint64_t sf37ref_layer_cache_bytes(uint32_t cap) {
@@ -214,5 +215,51 @@ int sf37ref_session_load(int kind, const uint8_t *buf, uint64_t len, int ctx, in
         for (uint32_t il = 0; il < SF37_MAIN_LAYERS; il++) n_rows[il] = s.cpu_cache.layer[il].n;
     }
     free(s.checkpoint.v);
+    return rc;
+}
+
+/* ---- the reference's CUDA-backend per-row checkpoint loops (timing) ----
+ * The session writers read each live row with two synchronous 4 KiB
+ * sf37_cuda_tensor_read calls (sf37.c:7298-7320 snapshot, 6976-7009
+ * payload).  These restate those loops for one layer with the reference's
+ * own tensor_read (passed in from the reference CUDA library) and encoder,
+ * so the bench can time the reference path on a B200.  Rows are f32
+ * [cap][1024]. */
+typedef int (*sf37ref_read_fn)(const void *tensor, uint64_t off, void *dst, uint64_t bytes);
+
+int sf37ref_snapshot_rows_cuda(sf37ref_read_fn rd, const void *k_tensor, const void *v_tensor,
+                               uint32_t first_pos, uint32_t rows, uint32_t cap, uint8_t *dst) {
+    const uint64_t row = (uint64_t)SF37_KV_HEADS * SF37_HEAD_DIM * sizeof(float);
+    for (uint32_t r = 0; r < rows; r++) {
+        const uint64_t off = (uint64_t)((first_pos + r) % cap) * row;
+        if (!rd(k_tensor, off, dst, row)) return 1;
+        dst += row;
+        if (!rd(v_tensor, off, dst, row)) return 1;
+        dst += row;
+    }
+    return 0;
+}
+
+int sf37ref_payload_rows_cuda(sf37ref_read_fn rd, const void *k_tensor, const void *v_tensor,
+                              uint32_t first_pos, uint32_t rows, uint32_t cap, int fd) {
+    const uint32_t kv_row = SF37_KV_HEADS * SF37_HEAD_DIM;
+    const uint32_t group = SF37_SESSION_PAYLOAD_KV_GROUP;
+    const uint64_t enc_bytes = payload_encoded_kv_row_bytes(kv_row, group);
+    float row_buf[SF37_KV_HEADS * SF37_HEAD_DIM];
+    uint8_t enc[SF37_KV_HEADS * SF37_HEAD_DIM + 64 * sizeof(float)];
+    FILE *fp = fdopen(dup(fd), "wb");
+    if (!fp) return 1;
+    int rc = 0;
+    for (uint32_t r = 0; rc == 0 && r < rows; r++) {
+        const uint64_t off = (uint64_t)((first_pos + r) % cap) * kv_row * sizeof(float);
+        for (int which = 0; which < 2 && rc == 0; which++) {
+            if (!rd(which ? v_tensor : k_tensor, off, row_buf, (uint64_t)kv_row * sizeof(float))) rc = 1;
+            else {
+                payload_encode_kv_row_i8_grouped(row_buf, kv_row, group, enc);
+                if (fwrite(enc, 1, (size_t)enc_bytes, fp) != (size_t)enc_bytes) rc = 1;
+            }
+        }
+    }
+    if (fclose(fp) != 0) rc = 1;
     return rc;
 }

@@ -17,6 +17,8 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <atomic>
+#include <thread>
 #include <unistd.h>
 #include <vector>
 
@@ -181,30 +183,34 @@ int check_header(const sf37kv_session *s, const uint32_t *h, const uint32_t *row
 }
 
 // ------------------------------------------------------------ fd io
-struct FdSink {
+// A file descriptor at a position.  Seekable files (regular files, tmpfs)
+// are accessed with pread/pwrite, large transfers split across threads
+// (page-cache copies and tmpfs page allocation scale with threads); pipes and
+// sockets fall back to sequential read/write.
+struct FdIo {
     int fd;
+    bool seekable;
+    int64_t off;          // next file offset (seekable only)
+    uint64_t *remaining;  // loader: bytes of the record not yet read
     char *err;
     size_t errlen;
 };
 
-int write_all(int fd, const void *p, uint64_t n) {
-    const uint8_t *b = (const uint8_t *)p;
-    while (n > 0) {
-        const size_t c = n > kIoChunk ? (size_t)kIoChunk : (size_t)n;
-        const ssize_t w = write(fd, b, c);
-        if (w < 0 && errno == EINTR) continue;
-        if (w <= 0) return 1;
-        b += w;
-        n -= (uint64_t)w;
-    }
-    return 0;
+FdIo fd_io(int fd, uint64_t *remaining, char *err, size_t errlen) {
+    const off_t o = lseek(fd, 0, SEEK_CUR);
+    return FdIo{fd, o >= 0, (int64_t)o, remaining, err, errlen};
 }
 
-int read_all(int fd, void *p, uint64_t n) {
-    uint8_t *b = (uint8_t *)p;
+// Ends a call: a seekable fd is left at the end of what was transferred, as
+// sequential I/O would leave it.
+void fd_done(const FdIo &io) {
+    if (io.seekable) (void)lseek(io.fd, (off_t)io.off, SEEK_SET);
+}
+
+int seq_io(int fd, uint8_t *b, uint64_t n, bool wr) {
     while (n > 0) {
         const size_t c = n > kIoChunk ? (size_t)kIoChunk : (size_t)n;
-        const ssize_t r = read(fd, b, c);
+        const ssize_t r = wr ? write(fd, b, c) : read(fd, b, c);
         if (r < 0 && errno == EINTR) continue;
         if (r <= 0) return 1;
         b += r;
@@ -213,24 +219,58 @@ int read_all(int fd, void *p, uint64_t n) {
     return 0;
 }
 
-int sink_fd(const void *p, uint64_t n, void *ctx) {
-    FdSink *S = (FdSink *)ctx;
-    if (write_all(S->fd, p, n)) return fail(S->err, S->errlen, "failed to write session payload");
+int pos_io(int fd, uint8_t *b, uint64_t n, int64_t off, bool wr) {
+    while (n > 0) {
+        const size_t c = n > kIoChunk ? (size_t)kIoChunk : (size_t)n;
+        const ssize_t r = wr ? pwrite(fd, b, c, (off_t)off) : pread(fd, b, c, (off_t)off);
+        if (r < 0 && errno == EINTR) continue;
+        if (r <= 0) return 1;
+        b += r;
+        off += r;
+        n -= (uint64_t)r;
+    }
     return 0;
 }
 
-struct FdSource {
-    int fd;
-    uint64_t *remaining;
-    char *err;
-    size_t errlen;
-};
+int par_io(FdIo &io, void *p, uint64_t n, bool wr) {
+    uint8_t *b = (uint8_t *)p;
+    if (!io.seekable) return seq_io(io.fd, b, n, wr);
+    constexpr uint64_t kMinPart = 4ull << 20;
+    unsigned nt = std::thread::hardware_concurrency();
+    nt = nt < 1 ? 1 : nt > 8 ? 8 : nt;
+    if (n < 2 * kMinPart || nt == 1) {
+        const int rc = pos_io(io.fd, b, n, io.off, wr);
+        if (!rc) io.off += (int64_t)n;
+        return rc;
+    }
+    if ((uint64_t)nt > n / kMinPart) nt = (unsigned)(n / kMinPart);
+    const uint64_t part = ((n + nt - 1) / nt + 4095) & ~4095ull;
+    std::atomic<int> bad{0};
+    std::vector<std::thread> th;
+    for (unsigned t = 0; t < nt; t++) {
+        const uint64_t a = (uint64_t)t * part;
+        if (a >= n) break;
+        const uint64_t len = n - a < part ? n - a : part;
+        th.emplace_back([&, a, len] {
+            if (pos_io(io.fd, b + a, len, io.off + (int64_t)a, wr)) bad = 1;
+        });
+    }
+    for (auto &x : th) x.join();
+    if (!bad) io.off += (int64_t)n;
+    return bad.load();
+}
+
+int sink_fd(const void *p, uint64_t n, void *ctx) {
+    FdIo *S = (FdIo *)ctx;
+    if (par_io(*S, const_cast<void *>(p), n, true)) return fail(S->err, S->errlen, "failed to write session payload");
+    return 0;
+}
 
 // payload_read_bytes (sf37.c:6753-6772): fails on a short file or when the
 // record's byte budget is exhausted.
 int source_fd(void *p, uint64_t n, void *ctx) {
-    FdSource *S = (FdSource *)ctx;
-    if (n > *S->remaining || read_all(S->fd, p, n)) return fail(S->err, S->errlen, "truncated session payload");
+    FdIo *S = (FdIo *)ctx;
+    if (n > *S->remaining || par_io(*S, p, n, false)) return fail(S->err, S->errlen, "truncated session payload");
     *S->remaining -= n;
     return 0;
 }
@@ -314,11 +354,11 @@ extern "C" int sf37kv_session_load_snapshot(sf37kv_session *s, const void *src, 
     const uint64_t rb = (uint64_t)kv_row(L) * 4u;
     for (uint32_t il = 0; il < L.n_layers; il++) kv_bytes += 2ull * rows[il] * rb;
     if (kv_bytes > len - pos) return fail(err, errlen, "failed to restore CUDA KV cache from snapshot");
+    // checked before any cache write (the reference checks after restoring)
+    if (pos + kv_bytes != len) return fail(err, errlen, "session snapshot has trailing bytes");
     const auto sec = kv_sections(s, rows.data(), token_count, rb);
     if (sf37kv_unpack_from_host(p + pos, sec.data(), L.n_layers, kv_row(L), s->dtype, SF37KV_FMT_RAW_F32, 0))
         return fail_last(err, errlen, "failed to restore CUDA KV cache from snapshot");
-    pos += kv_bytes;
-    if (pos != len) return fail(err, errlen, "session snapshot has trailing bytes");
     for (uint32_t i = 0; i < token_count; i++) s->tokens[i] = (int32_t)toks[i];
     s->n_tokens = token_count;
     return 0;
@@ -330,27 +370,28 @@ extern "C" int sf37kv_session_save_payload(const sf37kv_session *s, int fd, char
     if (err && errlen) err[0] = 0;
     const sf37kv_session_layout &L = s->layout;
     const std::vector<uint8_t> pre = build_prefix(s, true);
-    if (write_all(fd, pre.data(), pre.size())) return fail(err, errlen, "failed to write session payload");
+    FdIo io = fd_io(fd, nullptr, err, errlen);
+    if (sink_fd(pre.data(), pre.size(), &io)) {
+        fd_done(io);
+        return 1;
+    }
     std::vector<uint32_t> rows(L.n_layers);
     for (uint32_t il = 0; il < L.n_layers; il++) rows[il] = layer_rows(s, il);
     const uint64_t rb = encoded_row_bytes(kv_row(L), L.payload_group);
     const auto sec = kv_sections(s, rows.data(), s->n_tokens, rb);
-    FdSink sink{fd, err, errlen};
     const int rc = pack_stream(sec.data(), L.n_layers, kv_row(L), s->dtype, SF37KV_FMT_I8_GROUPED, L.payload_group,
-                               sink_fd, &sink);
+                               sink_fd, &io);
+    fd_done(io);
     if (rc == SF37KV_EINVAL && err && errlen && err[0]) return 1;  // the sink's message
     if (rc) return fail_last(err, errlen, "failed to read CUDA K cache for payload");
     return 0;
 }
 
-extern "C" int sf37kv_session_load_payload(sf37kv_session *s, int fd, uint64_t payload_bytes, char *err,
-                                           size_t errlen) {
-    if (!descriptor_ok(s) || fd < 0 || payload_bytes == 0 || !s->tokens || !s->logits || !s->hidden)
-        return fail(err, errlen, "invalid session payload load");
-    if (err && errlen) err[0] = 0;
+namespace sf37kv {
+namespace {
+int load_payload_body(sf37kv_session *s, FdIo &src, uint64_t payload_bytes, char *err, size_t errlen) {
     const sf37kv_session_layout &L = s->layout;
-    uint64_t remaining = payload_bytes;
-    FdSource src{fd, &remaining, err, errlen};
+    uint64_t &remaining = *src.remaining;
     uint32_t h[kPayFields];
     if (source_fd(h, sizeof(h), &src)) return 1;
     if (h[0] != kPayMagic || h[1] != kPayVersion) return fail(err, errlen, "unsupported session payload version");
@@ -380,4 +421,18 @@ extern "C" int sf37kv_session_load_payload(sf37kv_session *s, int fd, uint64_t p
     for (uint32_t i = 0; i < token_count; i++) s->tokens[i] = (int32_t)toks[i];
     s->n_tokens = token_count;
     return 0;
+}
+}  // namespace
+}  // namespace sf37kv
+
+extern "C" int sf37kv_session_load_payload(sf37kv_session *s, int fd, uint64_t payload_bytes, char *err,
+                                           size_t errlen) {
+    if (!descriptor_ok(s) || fd < 0 || payload_bytes == 0 || !s->tokens || !s->logits || !s->hidden)
+        return fail(err, errlen, "invalid session payload load");
+    if (err && errlen) err[0] = 0;
+    uint64_t remaining = payload_bytes;
+    FdIo src = fd_io(fd, &remaining, err, errlen);
+    const int rc = load_payload_body(s, src, payload_bytes, err, errlen);
+    fd_done(src);
+    return rc;
 }
