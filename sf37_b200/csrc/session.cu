@@ -14,6 +14,9 @@
 // 7347-7478 and 7038-7185 (the loaders and their checks, restated in order
 // with the same messages).
 #include <cerrno>
+#include <fcntl.h>
+#include <sys/mman.h>
+#include <sys/stat.h>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -187,6 +190,9 @@ int check_header(const sf37kv_session *s, const uint32_t *h, const uint32_t *row
 // are accessed with pread/pwrite, large transfers split across threads
 // (page-cache copies and tmpfs page allocation scale with threads); pipes and
 // sockets fall back to sequential read/write.
+// A writer to a regular file first allocates the record's range
+// (fallocate) and maps it, so that the threads copy straight into the page
+// cache: parallel pwrite calls on one file serialize on its inode lock.
 struct FdIo {
     int fd;
     bool seekable;
@@ -194,6 +200,9 @@ struct FdIo {
     uint64_t *remaining;  // loader: bytes of the record not yet read
     char *err;
     size_t errlen;
+    uint8_t *map = nullptr;  // writer: mapping of [map_base, map_base + map_len)
+    int64_t map_base = 0;
+    uint64_t map_len = 0;
 };
 
 FdIo fd_io(int fd, uint64_t *remaining, char *err, size_t errlen) {
@@ -201,9 +210,28 @@ FdIo fd_io(int fd, uint64_t *remaining, char *err, size_t errlen) {
     return FdIo{fd, o >= 0, (int64_t)o, remaining, err, errlen};
 }
 
-// Ends a call: a seekable fd is left at the end of what was transferred, as
-// sequential I/O would leave it.
-void fd_done(const FdIo &io) {
+// Maps [off, off + bytes) of a regular file for writing; silently keeps the
+// pwrite path when the file system cannot allocate or map.
+void fd_map_for_write(FdIo &io, uint64_t bytes) {
+    struct stat st;
+    if (!io.seekable || bytes < (64ull << 20) || fstat(io.fd, &st) != 0 || !S_ISREG(st.st_mode)) return;
+    if (fallocate(io.fd, 0, (off_t)io.off, (off_t)bytes) != 0) return;
+    const int64_t base = io.off & ~(int64_t)4095;
+    const uint64_t len = bytes + (uint64_t)(io.off - base);
+    void *m = mmap(nullptr, len, PROT_READ | PROT_WRITE, MAP_SHARED, io.fd, (off_t)base);
+    if (m == MAP_FAILED) return;
+    io.map = (uint8_t *)m;
+    io.map_base = base;
+    io.map_len = len;
+}
+
+// Ends a call: unmaps, and leaves a seekable fd at the end of what was
+// transferred, as sequential I/O would.
+void fd_done(FdIo &io) {
+    if (io.map) {
+        munmap(io.map, io.map_len);
+        io.map = nullptr;
+    }
     if (io.seekable) (void)lseek(io.fd, (off_t)io.off, SEEK_SET);
 }
 
@@ -245,6 +273,8 @@ int par_io(FdIo &io, void *p, uint64_t n, bool wr) {
     }
     if ((uint64_t)nt > n / kMinPart) nt = (unsigned)(n / kMinPart);
     const uint64_t part = ((n + nt - 1) / nt + 4095) & ~4095ull;
+    const bool mapped = wr && io.map && io.off >= io.map_base &&
+                        (uint64_t)(io.off - io.map_base) + n <= io.map_len;
     std::atomic<int> bad{0};
     std::vector<std::thread> th;
     for (unsigned t = 0; t < nt; t++) {
@@ -252,7 +282,8 @@ int par_io(FdIo &io, void *p, uint64_t n, bool wr) {
         if (a >= n) break;
         const uint64_t len = n - a < part ? n - a : part;
         th.emplace_back([&, a, len] {
-            if (pos_io(io.fd, b + a, len, io.off + (int64_t)a, wr)) bad = 1;
+            if (mapped) memcpy(io.map + (io.off - io.map_base) + a, b + a, len);
+            else if (pos_io(io.fd, b + a, len, io.off + (int64_t)a, wr)) bad = 1;
         });
     }
     for (auto &x : th) x.join();
@@ -371,6 +402,7 @@ extern "C" int sf37kv_session_save_payload(const sf37kv_session *s, int fd, char
     const sf37kv_session_layout &L = s->layout;
     const std::vector<uint8_t> pre = build_prefix(s, true);
     FdIo io = fd_io(fd, nullptr, err, errlen);
+    fd_map_for_write(io, sf37kv_session_payload_bytes(s));
     if (sink_fd(pre.data(), pre.size(), &io)) {
         fd_done(io);
         return 1;
