@@ -190,8 +190,8 @@ int check_header(const sf37kv_session *s, const uint32_t *h, const uint32_t *row
 // are accessed with pread/pwrite, large transfers split across threads
 // (page-cache copies and tmpfs page allocation scale with threads); pipes and
 // sockets fall back to sequential read/write.
-// A writer to a regular file first allocates the record's range
-// (fallocate) and maps it, so that the threads copy straight into the page
+// A writer to a regular file first extends the file over the record's range
+// and maps it, so that the threads copy straight into the page
 // cache: parallel pwrite calls on one file serialize on its inode lock.
 struct FdIo {
     int fd;
@@ -215,7 +215,10 @@ FdIo fd_io(int fd, uint64_t *remaining, char *err, size_t errlen) {
 void fd_map_for_write(FdIo &io, uint64_t bytes) {
     struct stat st;
     if (!io.seekable || bytes < (64ull << 20) || fstat(io.fd, &st) != 0 || !S_ISREG(st.st_mode)) return;
-    if (fallocate(io.fd, 0, (off_t)io.off, (off_t)bytes) != 0) return;
+    // extend (sparse) rather than fallocate: the pages are then allocated by
+    // the copying threads' faults, in parallel
+    const off_t end = (off_t)io.off + (off_t)bytes;
+    if (st.st_size < end && ftruncate(io.fd, end) != 0) return;
     const int64_t base = io.off & ~(int64_t)4095;
     const uint64_t len = bytes + (uint64_t)(io.off - base);
     void *m = mmap(nullptr, len, PROT_READ | PROT_WRITE, MAP_SHARED, io.fd, (off_t)base);
