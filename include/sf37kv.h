@@ -103,6 +103,35 @@ int sf37kv_decode_noalloc(const sf37kv_decode_layer *layers, uint32_t n_layers,
                           uint32_t q_heads, uint32_t kv_heads, uint32_t head_dim,
                           int dtype, void *stream);
 
+/* q/k head preparation fused into a decode step (the step before the
+ * path: sf37_cuda_head_rms_norm_rope_qk_bf16_mapped, sf37_cuda.cu:2265-2316
+ * and 6187-6240; CPU form sf37.c:2223-2231).  For each query head and each
+ * head of the appended K row: RMS norm (double sum of squares,
+ * scale = 1 / sqrtf(mean + eps)) times (w + 1) with bf16 weights w, then
+ * split-half RoPE over the first rotary_dim dims at the layer's position:
+ * pair (i, i + rotary_dim/2) rotated by (float)(pos * inv_freq(i)),
+ * inv_freq(i) = theta^(-2i/rotary_dim), with the llama3 smoothing when
+ * llama3 != 0 (sf37.c:1995-2013).  The reference model uses rotary_dim 64,
+ * theta 5e6, llama3 on full layers and 128, 1e4, off on sliding layers
+ * (sf37.c:1983-1993), eps 1e-5. */
+typedef struct {
+    const uint16_t *q_norm;  /* bf16 [head_dim], device */
+    const uint16_t *k_norm;  /* bf16 [head_dim], device (needed with k_new) */
+    double theta;
+    uint32_t rotary_dim;     /* even, <= head_dim */
+    uint32_t llama3;
+    float eps;
+    uint32_t reserved;
+} sf37kv_qk_prep;
+
+/* sf37kv_decode with layers[i].q and layers[i].k_new taken BEFORE head norm
+ * and RoPE: prep[i] is applied inside the decode kernel, the cache receives
+ * the prepared K row, and q/k_new in memory are left unchanged.  One launch
+ * for all layers, as sf37kv_decode.  head_dim 128, group <= 16. */
+int sf37kv_decode_prep(const sf37kv_decode_layer *layers, const sf37kv_qk_prep *prep,
+                       uint32_t n_layers, uint32_t q_heads, uint32_t kv_heads,
+                       uint32_t head_dim, int dtype, void *stream);
+
 /* Append n_tok rows per layer: row t -> slot (pos0 + t) % cap
  * (store_kv_cache_batch_kernel, sf37_cuda.cu:6355-6372). */
 typedef struct {

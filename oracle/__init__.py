@@ -76,6 +76,7 @@ def lib():
         L.orc_payload_decode_row.argtypes = [_vp, _u32, _u32, _vp]
         L.orc_pack_layer.argtypes = [_vp, _vp, _vp, _int, _u32, _u32, _u32, _u32, _int, _u32, _int]
         L.orc_unpack_layer.argtypes = [_vp, _vp, _vp, _int, _u32, _u32, _u32, _u32, _int, _u32]
+        L.orc_qk_prep.argtypes = [_vp, _u32, _u32, _vp, _u32, ctypes.c_double, _int, _u32, ctypes.c_float]
         _lib = L
     return _lib
 
@@ -205,7 +206,29 @@ def unpack_layer(src, k_cache, v_cache, first_pos, rows, cap, kv_dim, fmt=0, gro
                            kv_dim, fmt, group)
 
 
+def qk_prep(x, w_bf16, rotary_dim, theta, llama3, pos, eps=1e-5):
+    """RMS norm (weight w + 1) + split-half RoPE of heads x [..., 128] (copy)."""
+    x = np.ascontiguousarray(x, np.float32).copy()
+    w = np.ascontiguousarray(w_bf16, np.uint16)
+    lib().orc_qk_prep(_ptr(x), x.size // x.shape[-1], x.shape[-1], _ptr(w), rotary_dim, theta, int(llama3),
+                      pos, eps)
+    return x
+
+
+def bf16_bits_to_f32(w):
+    return (np.asarray(w, np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
 # ----------------------------------------------- the reference's own CPU code
+def ref_qk_prep(x, w_bf16, rotary_dim, theta, llama3, pos):
+    """The reference's head_rms_norm_weight1 + apply_rope_one (copy of x)."""
+    R = ref()
+    R.sf37ref_qk_prep.argtypes = [_vp, _u32, _vp, _u32, ctypes.c_double, _int, _u32]
+    x = np.ascontiguousarray(x, np.float32).copy()
+    w = np.ascontiguousarray(bf16_bits_to_f32(w_bf16), np.float32)
+    R.sf37ref_qk_prep(_ptr(x), x.size // 128, _ptr(w), rotary_dim, theta, int(llama3), pos)
+    return x
+
 def ref_payload_encode_rows(rows: np.ndarray, group=64) -> np.ndarray:
     rows = np.ascontiguousarray(rows, np.float32).reshape(-1, rows.shape[-1])
     R = ref()

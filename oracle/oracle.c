@@ -316,3 +316,45 @@ void orc_unpack_layer(const uint8_t *src, void *k_cache, void *v_cache, int elem
     }
     free(row);
 }
+
+/* ---- q/k head preparation (the step before the append) ----
+ * head_rms_norm_weight1 (sf37.c:1921-1929) with sf37_rms_norm_weight1
+ * (sf37_ops.c:22-28) and apply_rope_one (sf37.c:2015-2031) with
+ * sf37_inv_freq (sf37.c:1995-2013), on n_head heads of x in place.
+ * w: bf16 bits [head_dim] (the model's q_norm / k_norm). */
+static double orc_inv_freq(uint32_t pair, uint32_t dim, double theta, int llama3) {
+    double inv = 1.0 / pow(theta, (double)(pair * 2u) / (double)dim);
+    if (!llama3) return inv;
+    const double factor = 2.0, low_ff = 1.0, high_ff = 32.0, old_ctx = 131072.0;
+    const double low_wl = old_ctx / low_ff, high_wl = old_ctx / high_ff;
+    const double wavelen = 2.0 * 3.14159265358979323846 / inv;
+    if (wavelen > low_wl) return inv / factor;
+    if (wavelen < high_wl) return inv;
+    const double smooth = (old_ctx / wavelen - low_ff) / (high_ff - low_ff);
+    return (1.0 - smooth) * inv / factor + smooth * inv;
+}
+
+void orc_qk_prep(float *x, uint32_t n_head, uint32_t head_dim, const uint16_t *w, uint32_t rotary_dim,
+                 double theta, int llama3, uint32_t pos, float eps) {
+    for (uint32_t h = 0; h < n_head; h++) {
+        float *head = x + (uint64_t)h * head_dim;
+        double ss = 0.0;
+        for (uint32_t i = 0; i < head_dim; i++) ss += (double)head[i] * (double)head[i];
+        const float scale = 1.0f / sqrtf((float)(ss / (double)head_dim) + eps);
+        for (uint32_t i = 0; i < head_dim; i++) {
+            uint32_t bits = (uint32_t)w[i] << 16;
+            float wf;
+            memcpy(&wf, &bits, 4);
+            head[i] = head[i] * scale * (wf + 1.0f);
+        }
+        const uint32_t half = rotary_dim / 2u;
+        for (uint32_t i = 0; i < half; i++) {
+            const double inv = orc_inv_freq(i, rotary_dim, theta, llama3);
+            const float c = cosf((float)((double)pos * inv));
+            const float s = sinf((float)((double)pos * inv));
+            const float a = head[i], b = head[i + half];
+            head[i] = a * c - b * s;
+            head[i + half] = b * c + a * s;
+        }
+    }
+}

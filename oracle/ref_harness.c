@@ -263,3 +263,13 @@ int sf37ref_payload_rows_cuda(sf37ref_read_fn rd, const void *k_tensor, const vo
     if (fclose(fp) != 0) rc = 1;
     return rc;
 }
+
+/* ---- q/k head preparation, the reference CPU form ----
+ * head_rms_norm_weight1 (sf37.c:1921) + apply_rope_one (sf37.c:2015) on
+ * n_head heads of x in place; w: f32 [128] (the bf16 weights widened, as
+ * tensor_bf16_to_f32 does, sf37.c:2223). */
+void sf37ref_qk_prep(float *x, uint32_t n_head, const float *w, uint32_t rotary_dim, double theta,
+                     int llama3, uint32_t pos) {
+    head_rms_norm_weight1(x, n_head, SF37_HEAD_DIM, w, SF37_RMS_EPS);
+    apply_rope_one(x, n_head, SF37_HEAD_DIM, rotary_dim, theta, llama3 != 0, pos);
+}

@@ -37,6 +37,11 @@ class PeerGather(ctypes.Structure):
                 ("done_counter", c_vp), ("world", c_u32), ("rank", c_u32)]
 
 
+class QkPrep(ctypes.Structure):
+    _fields_ = [("q_norm", c_vp), ("k_norm", c_vp), ("theta", ctypes.c_double), ("rotary_dim", c_u32),
+                ("llama3", c_u32), ("eps", c_float), ("reserved", c_u32)]
+
+
 class PackLayer(ctypes.Structure):
     _fields_ = [("cache", Cache), ("first_pos", c_u32), ("rows", c_u32), ("offset", c_u64)]
 
@@ -111,6 +116,8 @@ SIGNATURES = {
     "sf37kv_ipc_handle": (c_int, [c_vp, c_vp]),
     "sf37kv_ipc_open": (c_vp, [c_vp]),
     "sf37kv_ipc_close": (None, [c_vp]),
+    "sf37kv_decode_prep": (c_int, [ctypes.POINTER(DecodeLayer), ctypes.POINTER(QkPrep), c_u32, c_u32, c_u32,
+                                   c_u32, c_int, c_vp]),
     "sf37kv_decode_gather": (c_int, [ctypes.POINTER(DecodeLayer), c_u32, c_u32, c_u32, c_u32, c_int,
                                      ctypes.POINTER(PeerGather), c_u32, c_vp]),
     "sf37kv_gather_wait": (c_int, [ctypes.POINTER(PeerGather), c_u32, c_vp]),

@@ -67,17 +67,93 @@ struct JobDev {
     uint32_t split_rows, n_splits, cta_begin;
     const float *k_new, *v_new;  // appended row (position end-1) or nullptr
     uint64_t gather_off;         // float offset of this job's block in the peers' gather buffers
+    // q/k head preparation (qn == nullptr: none): RMS norm with weight
+    // (w + 1) then split-half RoPE over `rotary` dims at position end-1.
+    const uint16_t *qn, *kn;     // bf16 [128] norm weights
+    double theta;
+    uint32_t rotary, llama3;
+    float eps;
 };
+
+// inv_freq of RoPE pair `pair` (sf37_inv_freq, sf37.c:1995-2013 and
+// sf37_cuda.cu:2221-2241), in double as the reference.
+__device__ __forceinline__ double rope_inv_freq(uint32_t pair, uint32_t dim, double theta, uint32_t llama3) {
+    const double inv = 1.0 / pow(theta, (double)(pair * 2u) / (double)dim);
+    if (!llama3) return inv;
+    const double factor = 2.0, low_ff = 1.0, high_ff = 32.0, old_ctx = 131072.0;
+    const double low_wl = old_ctx / low_ff, high_wl = old_ctx / high_ff;
+    const double wavelen = 2.0 * 3.14159265358979323846 / inv;
+    if (wavelen > low_wl) return inv / factor;
+    if (wavelen < high_wl) return inv;
+    const double smooth = (old_ctx / wavelen - low_ff) / (high_ff - low_ff);
+    return (1.0 - smooth) * inv / factor + smooth * inv;
+}
+
+// The G query heads of KV head kvh (and, with_k, the new K row's head kvh)
+// normalized and rotated into shared memory Qf [G][128] / Kf [128]:
+//   head_rms_norm_weight1 (sf37.c:1921-1929 -> sf37_rms_norm_weight1,
+//   sf37_ops.c:22-28: double sum of squares, scale = 1 / sqrtf(mean + eps),
+//   x * scale * (w + 1)), then apply_rope_one (sf37.c:2015-2031): pairs
+//   (i, i + rotary/2), angle (float)(pos * inv_freq(i)).
+// One warp per head; every warp of the CTA takes part.
+__device__ __noinline__ void prep_heads(const JobDev &J, uint32_t kvh, uint32_t G, bool with_k, float *Qf,
+                                        float *Kf) {
+    const uint32_t lane = threadIdx.x & 31u, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    const uint32_t pos = J.end - 1u;
+    const uint32_t half = J.rotary >> 1;
+    float cs[2], sn[2];
+#pragma unroll
+    for (int u = 0; u < 2; u++) {
+        const uint32_t i = lane + 32u * u;
+        cs[u] = 1.f;
+        sn[u] = 0.f;
+        if (i < half) {
+            const float ang = (float)((double)pos * rope_inv_freq(i, J.rotary, J.theta, J.llama3));
+            sincosf(ang, &sn[u], &cs[u]);
+        }
+    }
+    const uint32_t nh = G + (with_k ? 1u : 0u);
+    for (uint32_t h = warp; h < nh; h += nw) {
+        const bool isk = h == G;
+        const float *src = isk ? J.k_new + kvh * 128u : J.q + (uint64_t)(kvh * G + h) * 128u;
+        const uint16_t *w = isk ? J.kn : J.qn;
+        float *dst = isk ? Kf : Qf + h * 128u;
+        const float4 x = reinterpret_cast<const float4 *>(src)[lane];
+        double ss = (double)x.x * x.x + (double)x.y * x.y + (double)x.z * x.z + (double)x.w * x.w;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        const float scale = 1.0f / sqrtf((float)(ss / 128.0) + J.eps);
+        const uint2 wb = reinterpret_cast<const uint2 *>(w)[lane];
+        const float w0 = __uint_as_float(wb.x << 16) + 1.0f, w1 = __uint_as_float(wb.x & 0xffff0000u) + 1.0f;
+        const float w2 = __uint_as_float(wb.y << 16) + 1.0f, w3 = __uint_as_float(wb.y & 0xffff0000u) + 1.0f;
+        reinterpret_cast<float4 *>(dst)[lane] =
+            make_float4(x.x * scale * w0, x.y * scale * w1, x.z * scale * w2, x.w * scale * w3);
+        __syncwarp();
+#pragma unroll
+        for (int u = 0; u < 2; u++) {
+            const uint32_t i = lane + 32u * u;
+            if (i < half) {
+                const float a = dst[i], b = dst[i + half];
+                dst[i] = a * cs[u] - b * sn[u];
+                dst[i + half] = b * cs[u] + a * sn[u];
+            }
+        }
+        __syncwarp();
+    }
+}
 
 // The CTA owning the last split of (job, kvh) stores this KV head's slice of
 // the appended row (f32 -> T, round to nearest even) before any warp loads
 // rows; __syncthreads() plus L2-coherent cp.async.cg loads make it visible.
 template <typename T>
-__device__ __forceinline__ void fused_append(const JobDev &J, uint32_t kvh, uint32_t split, uint32_t kv_heads) {
+__device__ __forceinline__ void fused_append(const JobDev &J, uint32_t kvh, uint32_t split, uint32_t kv_heads,
+                                             const float *kf = nullptr) {
     if (!J.k_new || split + 1u != J.n_splits) return;
     const uint32_t i = threadIdx.x;
     if (i >= 64u) return;
-    const float *src = (i < 32u ? J.k_new : J.v_new) + kvh * 128u + (i & 31u) * 4u;
+    // kf: the prepared K head in shared memory (prep_heads), else the raw row
+    const float *src = i < 32u ? (kf ? kf + (i & 31u) * 4u : J.k_new + kvh * 128u + (i & 31u) * 4u)
+                               : J.v_new + kvh * 128u + (i & 31u) * 4u;
     const float4 x = *reinterpret_cast<const float4 *>(src);
     T *dst = reinterpret_cast<T *>(const_cast<void *>(i < 32u ? J.k : J.v)) +
              (uint64_t)((J.end - 1u) % J.cap) * kv_heads * 128u + kvh * 128u + (i & 31u) * 4u;
@@ -554,10 +630,17 @@ __global__ void __launch_bounds__(NW * 32, 1) decode_f16_pipe_kernel(const __gri
     const uint32_t g = lane >> 2, t = lane & 3u;
     const uint32_t mt = warp % n_mt, stream = warp / n_mt;
 
+    // Optional q/k preparation into the (not yet used) stage buffers.
+    float *Qf = reinterpret_cast<float *>(smem_raw), *Kf = Qf + 16 * 128;
+    const bool prep = J.qn != nullptr;
+    if (prep) {
+        prep_heads(J, kvh, G, J.k_new && split + 1u == J.n_splits, Qf, Kf);
+        __syncthreads();
+    }
     if (warp < n_mt) {
         const uint32_t hg = warp * 8u + g;
         const bool valid = hg < G;
-        const float *qp = J.q + (uint64_t)(kvh * G + (valid ? hg : 0u)) * 128u;
+        const float *qp = prep ? Qf + (valid ? hg : 0u) * 128u : J.q + (uint64_t)(kvh * G + (valid ? hg : 0u)) * 128u;
 #pragma unroll
         for (int kk = 0; kk < 8; kk++) {
             uint32_t r[4];
@@ -577,7 +660,7 @@ __global__ void __launch_bounds__(NW * 32, 1) decode_f16_pipe_kernel(const __gri
             Qs[(warp * 8 + kk) * 32 + lane] = make_uint4(r[0], r[1], r[2], r[3]);
         }
     }
-    fused_append<__half>(J, kvh, split, P.kv_heads);
+    fused_append<__half>(J, kvh, split, P.kv_heads, prep ? Kf : nullptr);
     __syncthreads();
 
     const uint32_t row0 = J.start + split * J.split_rows;
@@ -774,10 +857,16 @@ __global__ void __launch_bounds__(NW * 32, 1) decode_f32_pipe_kernel(const __gri
     const uint32_t g = lane >> 2, t = lane & 3u;
     const uint32_t mt = warp % n_mt, stream = warp / n_mt;
 
+    float *Qf = reinterpret_cast<float *>(smem_raw), *Kf = Qf + 16 * 128;
+    const bool prep = J.qn != nullptr;
+    if (prep) {
+        prep_heads(J, kvh, G, J.k_new && split + 1u == J.n_splits, Qf, Kf);
+        __syncthreads();
+    }
     if (warp < n_mt) {
         const uint32_t hg = warp * 8u + g;
         const bool valid = hg < G;
-        const float *qp = J.q + (uint64_t)(kvh * G + (valid ? hg : 0u)) * 128u;
+        const float *qp = prep ? Qf + (valid ? hg : 0u) * 128u : J.q + (uint64_t)(kvh * G + (valid ? hg : 0u)) * 128u;
 #pragma unroll
         for (int kk = 0; kk < 8; kk++) {
             const float4 x = valid ? *reinterpret_cast<const float4 *>(qp + 16 * kk + 4 * t)
@@ -788,7 +877,7 @@ __global__ void __launch_bounds__(NW * 32, 1) decode_f32_pipe_kernel(const __gri
             Qs[(warp * 8 + kk) * 32 + lane] = make_uint4(r0, r1, r2, r3);
         }
     }
-    fused_append<float>(J, kvh, split, P.kv_heads);
+    fused_append<float>(J, kvh, split, P.kv_heads, prep ? Kf : nullptr);
     __syncthreads();
 
     const uint32_t row0 = J.start + split * J.split_rows;
@@ -1253,6 +1342,11 @@ int attention_jobs(const AttnJob *jobs, uint32_t n, uint32_t q_heads, uint32_t k
     const bool fuses = head_dim == 128 && G <= 16 &&
                        ((dtype == SF37KV_F16 && !(ek && (!strcmp(ek, "reg2") || !strcmp(ek, "reg3")))) ||
                         (dtype == SF37KV_F32 && !(ef && !strcmp(ef, "cuda"))));
+    bool any_prep = false;
+    for (uint32_t i = 0; i < n; i++) any_prep |= jobs[i].prep != nullptr;
+    if (any_prep && !fuses)
+        return set_error(SF37KV_EUNSUPPORTED,
+                         "decode_prep: needs head_dim 128, group <= 16 and the default pipelined kernels");
     if (!fuses) {
         AppendJob aj[kMaxJobs];
         for (uint32_t base = 0; base < n; base += kMaxJobs) {
@@ -1337,6 +1431,14 @@ int attention_jobs(const AttnJob *jobs, uint32_t n, uint32_t q_heads, uint32_t k
             D = JobDev{A.k, A.v, A.q, A.gate, A.out, A.start, A.end, A.cap, sr, (uint32_t)ns, ctas,
                        fuses ? A.k_new : nullptr, fuses ? A.v_new : nullptr,
                        g_gather_cur ? g_gather_off[base + i] : 0};
+            if (A.prep) {
+                D.qn = A.prep->q_norm;
+                D.kn = A.prep->k_norm;
+                D.theta = A.prep->theta;
+                D.rotary = A.prep->rotary_dim;
+                D.llama3 = A.prep->llama3;
+                D.eps = A.prep->eps;
+            }
             if ((uint64_t)ctas + ns * kv_heads > 0x7fffffffull)
                 return set_error(SF37KV_EINVAL, "attention: grid too large");
             ctas += (uint32_t)ns * kv_heads;
@@ -1407,14 +1509,13 @@ int attention_jobs(const AttnJob *jobs, uint32_t n, uint32_t q_heads, uint32_t k
 using namespace sf37kv;
 
 // ------------------------------------------------------------ native API
-extern "C" int sf37kv_decode(const sf37kv_decode_layer *layers, uint32_t n_layers, uint32_t q_heads,
-                             uint32_t kv_heads, uint32_t head_dim, int dtype, void *stream) {
+static int decode_layers(const sf37kv_decode_layer *layers, const sf37kv_qk_prep *prep, uint32_t n_layers,
+                         uint32_t q_heads, uint32_t kv_heads, uint32_t head_dim, int dtype, void *stream) {
     if (!layers && n_layers) return set_error(SF37KV_EINVAL, "decode: layers is NULL");
     cudaStream_t s = stream ? (cudaStream_t)stream : current_stream();
-    AppendJob aj[kMaxJobs];
     AttnJob jobs[kMaxJobs];
     for (uint32_t base = 0; base < n_layers; base += kMaxJobs) {
-        uint32_t na = 0, m = 0;
+        uint32_t m = 0;
         for (uint32_t i = base; i < n_layers && m < (uint32_t)kMaxJobs; i++, m++) {
             const sf37kv_decode_layer &L = layers[i];
             if (L.cache.cap == 0) return set_error(SF37KV_EINVAL, "decode: layer %u cap 0", i);
@@ -1424,13 +1525,36 @@ extern "C" int sf37kv_decode(const sf37kv_decode_layer *layers, uint32_t n_layer
                 return set_error(SF37KV_EINVAL, "decode: layer %u k_new/v_new must be 16-byte aligned", i);
             jobs[m] = AttnJob{L.cache.k_cache, L.cache.v_cache, L.q, L.gate, L.out,
                               start_at(L.pos, L.cache.cap, L.cache.sliding, L.cache.window),
-                              L.pos + 1u, L.cache.cap, L.k_new, L.v_new};
+                              L.pos + 1u, L.cache.cap, L.k_new, L.v_new, prep ? &prep[i] : nullptr};
+            if (prep) {
+                const sf37kv_qk_prep &Q = prep[i];
+                if (!Q.q_norm || (L.k_new && !Q.k_norm))
+                    return set_error(SF37KV_EINVAL, "decode_prep: layer %u norm weight is NULL", i);
+                if (Q.rotary_dim == 0 || Q.rotary_dim > head_dim || (Q.rotary_dim & 1u))
+                    return set_error(SF37KV_EINVAL, "decode_prep: layer %u rotary_dim %u must be even and <= %u",
+                                     i, Q.rotary_dim, head_dim);
+                if ((((uintptr_t)L.q | (uintptr_t)Q.q_norm | (uintptr_t)Q.k_norm) & 7u) ||
+                    ((uintptr_t)L.q & 15u))
+                    return set_error(SF37KV_EINVAL, "decode_prep: layer %u q must be 16-byte and the weights "
+                                                    "8-byte aligned", i);
+            }
         }
-        (void)na;
-        (void)aj;
         if (int rc = attention_jobs(jobs, m, q_heads, kv_heads, head_dim, dtype, s)) return rc;
     }
     return SF37KV_OK;
+}
+
+extern "C" int sf37kv_decode(const sf37kv_decode_layer *layers, uint32_t n_layers, uint32_t q_heads,
+                             uint32_t kv_heads, uint32_t head_dim, int dtype, void *stream) {
+    return decode_layers(layers, nullptr, n_layers, q_heads, kv_heads, head_dim, dtype, stream);
+}
+
+extern "C" int sf37kv_decode_prep(const sf37kv_decode_layer *layers, const sf37kv_qk_prep *prep,
+                                  uint32_t n_layers, uint32_t q_heads, uint32_t kv_heads, uint32_t head_dim,
+                                  int dtype, void *stream) {
+    if (!prep && n_layers) return set_error(SF37KV_EINVAL, "decode_prep: prep is NULL");
+    if (head_dim != 128) return set_error(SF37KV_EUNSUPPORTED, "decode_prep: head_dim must be 128");
+    return decode_layers(layers, prep, n_layers, q_heads, kv_heads, head_dim, dtype, stream);
 }
 
 // ------------------------------------------------------------ drop-in API

@@ -64,6 +64,9 @@ struct AttnJob {
     // Optional row appended at position end-1 before attention (f32
     // [kv_heads*head_dim]); the fast kernels store it themselves.
     const float *k_new = nullptr, *v_new = nullptr;
+    // Optional q/k head preparation (RMS norm + RoPE) applied in the kernel
+    // to q and k_new before use (sf37kv_decode_prep).
+    const sf37kv_qk_prep *prep = nullptr;
 };
 
 // Launches attention for n jobs (any n; chunked internally).

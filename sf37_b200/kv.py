@@ -115,6 +115,25 @@ def decode(layers, q_heads, kv_heads, head_dim, dtype, stream=None):
           "sf37kv_decode")
 
 
+def qk_prep_desc(preps):
+    """preps: list of dicts q_norm, k_norm (bf16 tensors as int16/uint16/bfloat16),
+    rotary_dim, theta, llama3, eps.  Returns a ctypes array (reusable)."""
+    from ._lib import QkPrep
+    arr = (QkPrep * len(preps))()
+    for i, p in enumerate(preps):
+        arr[i] = QkPrep(_ptr(p["q_norm"]), _ptr(p.get("k_norm")), float(p["theta"]), int(p["rotary_dim"]),
+                        int(p.get("llama3", 0)), float(p.get("eps", 1e-5)), 0)
+    return arr
+
+
+def decode_prep(layers, preps, q_heads, kv_heads, head_dim, dtype, stream=None):
+    """sf37kv_decode with the q / k_new heads normalized and rotated in the kernel."""
+    arr = layers if not isinstance(layers, list) else decode_layers_desc(layers)
+    pa = preps if not isinstance(preps, list) else qk_prep_desc(preps)
+    check(lib().sf37kv_decode_prep(arr, pa, len(arr), q_heads, kv_heads, head_dim, dtype, _sp(stream)),
+          "sf37kv_decode_prep")
+
+
 def append(layers, kv_dim, dtype, stream=None):
     arr = (AppendLayer * len(layers))()
     for i, L in enumerate(layers):

@@ -15,6 +15,9 @@ Fixtures (all inputs are regenerable from the seeds in sf37_b200.synth):
   kv_push.npz       kv_cache_push of 6 rows into a capacity-4 linear cache
   sessions.npz      session snapshot / payload bytes and loader messages
                     (see sessions() below)
+  qk_prep.npz       head_rms_norm_weight1 + apply_rope_one on 9 heads at 6
+                    positions, full-layer (64, 5e6, llama3) and sliding-layer
+                    (128, 1e4) parameters
 """
 import os
 import sys
@@ -98,9 +101,25 @@ def sessions():
                         payload=np.frombuffer(pay, np.uint8), names=np.array(names), msgs=np.array(msgs))
 
 
+QK_POS = (0, 1, 511, 4097, 32768, 131071)
+
+
+def qk_prep():
+    rng = np.random.default_rng(21)
+    x = (rng.standard_normal((len(QK_POS), 9, 128)) * 3).astype(np.float32)
+    w = ((rng.standard_normal(128) * 0.3).astype(np.float32).view(np.uint32) >> 16).astype(np.uint16)
+    full = np.stack([oracle.ref_qk_prep(x[i], w, 64, 5e6, 1, p) for i, p in enumerate(QK_POS)])
+    sliding = np.stack([oracle.ref_qk_prep(x[i], w, 128, 1e4, 0, p) for i, p in enumerate(QK_POS)])
+    np.savez_compressed(os.path.join(OUT, "qk_prep.npz"), x=x, w=w, pos=np.array(QK_POS), full=full,
+                        sliding=sliding)
+
+
 if __name__ == "__main__":
     if len(sys.argv) > 1 and sys.argv[1] == "sessions":
         sessions()
+    elif len(sys.argv) > 1 and sys.argv[1] == "qk_prep":
+        qk_prep()
     else:
         main()
         sessions()
+        qk_prep()

@@ -124,3 +124,32 @@ def test_attention_matches_live_reference(n, sliding, q_heads):
     want = oracle.ref_attention_decode(q, k, v, n, n, q_heads, sliding, gate)
     got = oracle.attention_decode_at(q, k, v, gate, n - 1, n, q_heads, 8, 128, sliding, 512)
     assert_close(got, want, atol=1e-6, rtol=1e-5)
+
+
+# q/k head preparation: fast-math in the reference build (FMA contraction,
+# reassociated products) moves results by about one ulp, so the restatement
+# is pinned within 2 ulp-scale bounds rather than bit for bit.
+QK_ATOL, QK_RTOL = 2e-6, 1e-6
+
+
+def test_qk_prep_matches_reference_golden():
+    g = _g("qk_prep.npz")
+    for i, p in enumerate(g["pos"]):
+        got_f = oracle.qk_prep(g["x"][i], g["w"], 64, 5e6, True, int(p))
+        got_s = oracle.qk_prep(g["x"][i], g["w"], 128, 1e4, False, int(p))
+        np.testing.assert_allclose(got_f, g["full"][i], rtol=QK_RTOL, atol=QK_ATOL)
+        np.testing.assert_allclose(got_s, g["sliding"][i], rtol=QK_RTOL, atol=QK_ATOL)
+
+
+@pytest.mark.skipif(not oracle.ref_available(), reason="oracle/_ref not built")
+def test_qk_prep_matches_live_reference():
+    rng = np.random.default_rng(5)
+    w = ((rng.standard_normal(128) * 0.3).astype(np.float32).view(np.uint32) >> 16).astype(np.uint16)
+    for p in rng.integers(0, 262144, 40):
+        x = (rng.standard_normal((16, 128)) * 4).astype(np.float32)
+        for rot, th, ll in ((64, 5e6, 1), (128, 1e4, 0), (32, 1e4, 0)):
+            np.testing.assert_allclose(oracle.qk_prep(x, w, rot, th, ll, int(p)),
+                                       oracle.ref_qk_prep(x, w, rot, th, ll, int(p)), rtol=QK_RTOL, atol=QK_ATOL)
+    # zero head: scale = 1/sqrt(eps) times zero stays zero
+    z = np.zeros((1, 128), np.float32)
+    assert not np.any(oracle.qk_prep(z, w, 64, 5e6, 1, 9))
