@@ -323,11 +323,25 @@ def run_ours(args, rank, world):
         from sf37_b200.shard import PeerGather, ShardPlan
         pg = PeerGather(ShardPlan(world, rank, KVH, QH, HD), LAYERS)
 
+    # --prep: q / new K heads arrive before head norm + RoPE, which run inside
+    # the decode kernel (full layers rotary 64 / theta 5e6 / llama3, sliding
+    # layers 128 / 1e4, sf37.c:1983-1993).
+    prep_arr = None
+    if args.prep:
+        qw = torch.randn(LAYERS, HD, device=dev, generator=g).mul_(0.3).to(torch.bfloat16)
+        kw = torch.randn(LAYERS, HD, device=dev, generator=g).mul_(0.3).to(torch.bfloat16)
+        prep_arr = kv.qk_prep_desc([
+            dict(q_norm=qw[l], k_norm=kw[l], rotary_dim=64 if l % 4 == 0 else 128,
+                 theta=5e6 if l % 4 == 0 else 1e4, llama3=int(l % 4 == 0), eps=1e-5) for l in range(LAYERS)])
+
     def step(i):
         if pg is not None:
             pg.step(all_desc[i], kv.F16, stream)
             return
-        kv.decode(all_desc[i], qh_l, kvh_l, HD, kv.F16, stream)
+        if prep_arr is not None:
+            kv.decode_prep(all_desc[i], prep_arr, qh_l, kvh_l, HD, kv.F16, stream)
+        else:
+            kv.decode(all_desc[i], qh_l, kvh_l, HD, kv.F16, stream)
         if world > 1:
             dist.all_gather_into_tensor(gathered, out)
 
@@ -498,6 +512,7 @@ def run_ours(args, rank, world):
                                           "512-row ring), decode after a 65536-token prefix"}[wl],
                    "layers": LAYERS, "ctx": ctx, "q_heads": QH, "kv_heads": KVH, "head_dim": HD,
                    "kv_heads_per_gpu": kvh_l,
+                   "qk_prep_fused": bool(args.prep),
                    "parallelism": f"kv-head shard x{world}" + (
                        "" if world == 1 else " + NCCL all-gather" if pg is None
                        else " + output gather by peer-memory stores from the decode kernels"),
@@ -829,6 +844,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--gather", default="peer", choices=["peer", "nccl"],
                     help="multi-GPU output gather: decode-kernel stores into peer memory, or NCCL")
+    ap.add_argument("--prep", action="store_true",
+                    help="decode workloads: fuse the q/k head norm + RoPE into the step (sf37kv_decode_prep)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
     ap.add_argument("--no-ref-gpu", action="store_true", help="skip the reference CUDA kernels leg")
     ap.add_argument("--workload", default="decode",

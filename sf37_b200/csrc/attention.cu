@@ -68,62 +68,64 @@ struct JobDev {
     const float *k_new, *v_new;  // appended row (position end-1) or nullptr
     uint64_t gather_off;         // float offset of this job's block in the peers' gather buffers
     // q/k head preparation (qn == nullptr: none): RMS norm with weight
-    // (w + 1) then split-half RoPE over `rotary` dims at position end-1.
+    // (w + 1) then split-half RoPE over `rotary` dims with the cos/sin table
+    // DecodeParams::rope[rope_idx].
     const uint16_t *qn, *kn;     // bf16 [128] norm weights
-    double theta;
-    uint32_t rotary, llama3;
+    uint32_t rotary, rope_idx;
     float eps;
 };
 
-// inv_freq of RoPE pair `pair` (sf37_inv_freq, sf37.c:1995-2013 and
-// sf37_cuda.cu:2221-2241), in double as the reference.
-__device__ __forceinline__ double rope_inv_freq(uint32_t pair, uint32_t dim, double theta, uint32_t llama3) {
-    const double inv = 1.0 / pow(theta, (double)(pair * 2u) / (double)dim);
-    if (!llama3) return inv;
-    const double factor = 2.0, low_ff = 1.0, high_ff = 32.0, old_ctx = 131072.0;
-    const double low_wl = old_ctx / low_ff, high_wl = old_ctx / high_ff;
-    const double wavelen = 2.0 * 3.14159265358979323846 / inv;
-    if (wavelen > low_wl) return inv / factor;
-    if (wavelen < high_wl) return inv;
-    const double smooth = (old_ctx / wavelen - low_ff) / (high_ff - low_ff);
-    return (1.0 - smooth) * inv / factor + smooth * inv;
-}
+// RoPE cos/sin tables of one decode launch: one per distinct (rotary_dim,
+// theta, llama3, position), cos of pairs 0..63 then sin.  Computed on the
+// host with the reference's own arithmetic (see rope_table below).
+constexpr int kMaxRope = 8;
 
 // The G query heads of KV head kvh (and, with_k, the new K row's head kvh)
 // normalized and rotated into shared memory Qf [G][128] / Kf [128]:
 //   head_rms_norm_weight1 (sf37.c:1921-1929 -> sf37_rms_norm_weight1,
 //   sf37_ops.c:22-28: double sum of squares, scale = 1 / sqrtf(mean + eps),
 //   x * scale * (w + 1)), then apply_rope_one (sf37.c:2015-2031): pairs
-//   (i, i + rotary/2), angle (float)(pos * inv_freq(i)).
+//   (i, i + rotary/2) rotated by the host-made cos/sin table `rope`.
 // One warp per head; every warp of the CTA takes part.
-__device__ __noinline__ void prep_heads(const JobDev &J, uint32_t kvh, uint32_t G, bool with_k, float *Qf,
-                                        float *Kf) {
+__device__ __noinline__ void prep_heads(const float *rope, const JobDev &J, uint32_t kvh, uint32_t G,
+                                        bool with_k, float *Qf, float *Kf) {
     const uint32_t lane = threadIdx.x & 31u, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
-    const uint32_t pos = J.end - 1u;
     const uint32_t half = J.rotary >> 1;
+    const uint32_t nh = G + (with_k ? 1u : 0u);
+    // Issue every global load first (heads warp, warp + nw, ...; at most 5
+    // per warp for G <= 16 and 4 warps), then compute.
+    constexpr int kR = 5;
+    float4 xs[kR];
+#pragma unroll
+    for (int r = 0; r < kR; r++) {
+        const uint32_t h = warp + (uint32_t)r * nw;
+        xs[r] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (h < nh) {
+            const float *src = h == G ? J.k_new + kvh * 128u : J.q + (uint64_t)(kvh * G + h) * 128u;
+            xs[r] = reinterpret_cast<const float4 *>(src)[lane];
+        }
+    }
+    const uint2 wq = reinterpret_cast<const uint2 *>(J.qn)[lane];
+    const uint2 wk = with_k ? reinterpret_cast<const uint2 *>(J.kn)[lane] : make_uint2(0u, 0u);
     float cs[2], sn[2];
 #pragma unroll
     for (int u = 0; u < 2; u++) {
         const uint32_t i = lane + 32u * u;
-        cs[u] = 1.f;
-        sn[u] = 0.f;
-        if (i < half) {
-            const float ang = (float)((double)pos * rope_inv_freq(i, J.rotary, J.theta, J.llama3));
-            sincosf(ang, &sn[u], &cs[u]);
-        }
+        cs[u] = i < half ? rope[i] : 1.f;
+        sn[u] = i < half ? rope[64u + i] : 0.f;
     }
-    const uint32_t nh = G + (with_k ? 1u : 0u);
-    for (uint32_t h = warp; h < nh; h += nw) {
+#pragma unroll
+    for (int r = 0; r < kR; r++) {
+        const uint32_t h = warp + (uint32_t)r * nw;
+        if (h >= nh) break;
         const bool isk = h == G;
-        const float *src = isk ? J.k_new + kvh * 128u : J.q + (uint64_t)(kvh * G + h) * 128u;
-        const uint16_t *w = isk ? J.kn : J.qn;
+        const float4 x = xs[r];
+        const uint2 wb = isk ? wk : wq;
         float *dst = isk ? Kf : Qf + h * 128u;
-        const float4 x = reinterpret_cast<const float4 *>(src)[lane];
         double ss = (double)x.x * x.x + (double)x.y * x.y + (double)x.z * x.z + (double)x.w * x.w;
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
         const float scale = 1.0f / sqrtf((float)(ss / 128.0) + J.eps);
-        const uint2 wb = reinterpret_cast<const uint2 *>(w)[lane];
         const float w0 = __uint_as_float(wb.x << 16) + 1.0f, w1 = __uint_as_float(wb.x & 0xffff0000u) + 1.0f;
         const float w2 = __uint_as_float(wb.y << 16) + 1.0f, w3 = __uint_as_float(wb.y & 0xffff0000u) + 1.0f;
         reinterpret_cast<float4 *>(dst)[lane] =
@@ -175,6 +177,7 @@ struct DecodeParams {
     uint32_t *counters;    // one per (job, kv head)
     float qscale;          // log2(e) / sqrt(head_dim)
     GatherDev gat;
+    float rope[kMaxRope][128];  // q/k preparation tables (JobDev::rope_idx)
 };
 
 __device__ __forceinline__ void gather_store(const DecodeParams &P, const JobDev &J, uint64_t idx, float v) {
@@ -608,7 +611,7 @@ __device__ __forceinline__ uint4 lds128(uint32_t addr) {
     return r;
 }
 
-template <int NW, int S>
+template <int NW, int S, bool PREP = false>
 __global__ void __launch_bounds__(NW * 32, 1) decode_f16_pipe_kernel(const __grid_constant__ DecodeParams P) {
     extern __shared__ __align__(128) uint8_t smem_raw[];
     constexpr uint32_t kStage = 8192;  // 16 rows x 256 B for K, then V
@@ -629,39 +632,6 @@ __global__ void __launch_bounds__(NW * 32, 1) decode_f16_pipe_kernel(const __gri
     const uint32_t lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;
     const uint32_t g = lane >> 2, t = lane & 3u;
     const uint32_t mt = warp % n_mt, stream = warp / n_mt;
-
-    // Optional q/k preparation into the (not yet used) stage buffers.
-    float *Qf = reinterpret_cast<float *>(smem_raw), *Kf = Qf + 16 * 128;
-    const bool prep = J.qn != nullptr;
-    if (prep) {
-        prep_heads(J, kvh, G, J.k_new && split + 1u == J.n_splits, Qf, Kf);
-        __syncthreads();
-    }
-    if (warp < n_mt) {
-        const uint32_t hg = warp * 8u + g;
-        const bool valid = hg < G;
-        const float *qp = prep ? Qf + (valid ? hg : 0u) * 128u : J.q + (uint64_t)(kvh * G + (valid ? hg : 0u)) * 128u;
-#pragma unroll
-        for (int kk = 0; kk < 8; kk++) {
-            uint32_t r[4];
-#pragma unroll
-            for (int half = 0; half < 2; half++) {
-                const int w = 2 * kk + half;
-                const uint32_t dim = (4u * (w >> 2) + t) * 8u + 2u * (w & 3);
-                float2 x = valid ? *reinterpret_cast<const float2 *>(qp + dim) : make_float2(0.f, 0.f);
-                x.x *= P.qscale;
-                x.y *= P.qscale;
-                const __half2 hi = __floats2half2_rn(x.x, x.y);
-                const float2 hf = __half22float2(hi);
-                const __half2 lo = __floats2half2_rn(x.x - hf.x, x.y - hf.y);
-                r[half * 2] = h2_as_u32(hi);
-                r[half * 2 + 1] = h2_as_u32(lo);
-            }
-            Qs[(warp * 8 + kk) * 32 + lane] = make_uint4(r[0], r[1], r[2], r[3]);
-        }
-    }
-    fused_append<__half>(J, kvh, split, P.kv_heads, prep ? Kf : nullptr);
-    __syncthreads();
 
     const uint32_t row0 = J.start + split * J.split_rows;
     const uint32_t row1 = min(row0 + J.split_rows, J.end);
@@ -697,13 +667,57 @@ __global__ void __launch_bounds__(NW * 32, 1) decode_f16_pipe_kernel(const __gri
         cp_async_commit();
     };
 
+    // Optional q/k preparation (PREP = false compiles the plain kernel).  A
+    // CTA that does not append starts its first loads before preparing, so
+    // the preparation hides behind them; the appending CTA must store its
+    // row before any load can read it.
+    float *Qf = reinterpret_cast<float *>(smem_raw + NW * S * kStage + 2 * 8 * 32 * 16), *Kf = Qf + 16 * 128;
+    const bool prep = PREP && J.qn != nullptr;
+    const bool appender = J.k_new && split + 1u == J.n_splits;
+    const bool early = prep && !appender;
+    if (early) {
+#pragma unroll
+        for (int s = 0; s < S - 1; s++) issue(s);
+    }
+    if (prep) {
+        prep_heads(P.rope[J.rope_idx], J, kvh, G, appender, Qf, Kf);
+        __syncthreads();
+    }
+    if (warp < n_mt) {
+        const uint32_t hg = warp * 8u + g;
+        const bool valid = hg < G;
+        const float *qp = prep ? Qf + (valid ? hg : 0u) * 128u : J.q + (uint64_t)(kvh * G + (valid ? hg : 0u)) * 128u;
+#pragma unroll
+        for (int kk = 0; kk < 8; kk++) {
+            uint32_t r[4];
+#pragma unroll
+            for (int half = 0; half < 2; half++) {
+                const int w = 2 * kk + half;
+                const uint32_t dim = (4u * (w >> 2) + t) * 8u + 2u * (w & 3);
+                float2 x = valid ? *reinterpret_cast<const float2 *>(qp + dim) : make_float2(0.f, 0.f);
+                x.x *= P.qscale;
+                x.y *= P.qscale;
+                const __half2 hi = __floats2half2_rn(x.x, x.y);
+                const float2 hf = __half22float2(hi);
+                const __half2 lo = __floats2half2_rn(x.x - hf.x, x.y - hf.y);
+                r[half * 2] = h2_as_u32(hi);
+                r[half * 2 + 1] = h2_as_u32(lo);
+            }
+            Qs[(warp * 8 + kk) * 32 + lane] = make_uint4(r[0], r[1], r[2], r[3]);
+        }
+    }
+    fused_append<__half>(J, kvh, split, P.kv_heads, prep ? Kf : nullptr);
+    __syncthreads();
+
     float o[16][4];
 #pragma unroll
     for (int i = 0; i < 16; i++) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
     float m_run = -INFINITY, l_run = 0.f;
 
+    if (!early) {
 #pragma unroll
-    for (int s = 0; s < S - 1; s++) issue(s);
+        for (int s = 0; s < S - 1; s++) issue(s);
+    }
 
     for (uint32_t it = 0; it < nblk; it++) {
         cp_async_wait<S - 2>();
@@ -836,7 +850,7 @@ __device__ __forceinline__ void split2(float a, float b, uint32_t &hi, uint32_t 
     lo = *reinterpret_cast<const uint32_t *>(&l);
 }
 
-template <int NW, int S>
+template <int NW, int S, bool PREP = false>
 __global__ void __launch_bounds__(NW * 32, 1) decode_f32_pipe_kernel(const __grid_constant__ DecodeParams P) {
     extern __shared__ __align__(128) uint8_t smem_raw[];
     constexpr uint32_t kStage = 16384;  // 16 rows x 512 B for K, then V
@@ -856,29 +870,6 @@ __global__ void __launch_bounds__(NW * 32, 1) decode_f32_pipe_kernel(const __gri
     const uint32_t lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;
     const uint32_t g = lane >> 2, t = lane & 3u;
     const uint32_t mt = warp % n_mt, stream = warp / n_mt;
-
-    float *Qf = reinterpret_cast<float *>(smem_raw), *Kf = Qf + 16 * 128;
-    const bool prep = J.qn != nullptr;
-    if (prep) {
-        prep_heads(J, kvh, G, J.k_new && split + 1u == J.n_splits, Qf, Kf);
-        __syncthreads();
-    }
-    if (warp < n_mt) {
-        const uint32_t hg = warp * 8u + g;
-        const bool valid = hg < G;
-        const float *qp = prep ? Qf + (valid ? hg : 0u) * 128u : J.q + (uint64_t)(kvh * G + (valid ? hg : 0u)) * 128u;
-#pragma unroll
-        for (int kk = 0; kk < 8; kk++) {
-            const float4 x = valid ? *reinterpret_cast<const float4 *>(qp + 16 * kk + 4 * t)
-                                   : make_float4(0.f, 0.f, 0.f, 0.f);
-            uint32_t r0, r1, r2, r3;
-            split2(x.x * P.qscale, x.y * P.qscale, r0, r1);
-            split2(x.z * P.qscale, x.w * P.qscale, r2, r3);
-            Qs[(warp * 8 + kk) * 32 + lane] = make_uint4(r0, r1, r2, r3);
-        }
-    }
-    fused_append<float>(J, kvh, split, P.kv_heads, prep ? Kf : nullptr);
-    __syncthreads();
 
     const uint32_t row0 = J.start + split * J.split_rows;
     const uint32_t row1 = min(row0 + J.split_rows, J.end);
@@ -912,13 +903,48 @@ __global__ void __launch_bounds__(NW * 32, 1) decode_f32_pipe_kernel(const __gri
         cp_async_commit();
     };
 
+    // Optional q/k preparation (PREP = false compiles the plain kernel).  A
+    // CTA that does not append starts its first loads before preparing, so
+    // the preparation hides behind them; the appending CTA must store its
+    // row before any load can read it.
+    float *Qf = reinterpret_cast<float *>(smem_raw + NW * S * kStage + 2 * 8 * 32 * 16), *Kf = Qf + 16 * 128;
+    const bool prep = PREP && J.qn != nullptr;
+    const bool appender = J.k_new && split + 1u == J.n_splits;
+    const bool early = prep && !appender;
+    if (early) {
+#pragma unroll
+        for (int s = 0; s < S - 1; s++) issue(s);
+    }
+    if (prep) {
+        prep_heads(P.rope[J.rope_idx], J, kvh, G, appender, Qf, Kf);
+        __syncthreads();
+    }
+    if (warp < n_mt) {
+        const uint32_t hg = warp * 8u + g;
+        const bool valid = hg < G;
+        const float *qp = prep ? Qf + (valid ? hg : 0u) * 128u : J.q + (uint64_t)(kvh * G + (valid ? hg : 0u)) * 128u;
+#pragma unroll
+        for (int kk = 0; kk < 8; kk++) {
+            const float4 x = valid ? *reinterpret_cast<const float4 *>(qp + 16 * kk + 4 * t)
+                                   : make_float4(0.f, 0.f, 0.f, 0.f);
+            uint32_t r0, r1, r2, r3;
+            split2(x.x * P.qscale, x.y * P.qscale, r0, r1);
+            split2(x.z * P.qscale, x.w * P.qscale, r2, r3);
+            Qs[(warp * 8 + kk) * 32 + lane] = make_uint4(r0, r1, r2, r3);
+        }
+    }
+    fused_append<float>(J, kvh, split, P.kv_heads, prep ? Kf : nullptr);
+    __syncthreads();
+
     float o[16][4];
 #pragma unroll
     for (int i = 0; i < 16; i++) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
     float m_run = -INFINITY, l_run = 0.f;
 
+    if (!early) {
 #pragma unroll
-    for (int s = 0; s < S - 1; s++) issue(s);
+        for (int s = 0; s < S - 1; s++) issue(s);
+    }
 
     for (uint32_t it = 0; it < nblk; it++) {
         cp_async_wait<S - 2>();
@@ -1276,6 +1302,42 @@ constexpr int kNW = 4;  // warps per CTA of the fast kernels
 static size_t smem_f16() {
     return (size_t)(kNW * 16 * 128 + 32 * kNW) * 4 + 2 * 8 * 32 * 16;
 }
+// inv_freq of RoPE pair `pair`: sf37_inv_freq (sf37.c:1995-2013), double.
+static double rope_inv_freq(uint32_t pair, uint32_t dim, double theta, uint32_t llama3) {
+    const double inv = 1.0 / pow(theta, (double)(pair * 2u) / (double)dim);
+    if (!llama3) return inv;
+    const double factor = 2.0, low_ff = 1.0, high_ff = 32.0, old_ctx = 131072.0;
+    const double low_wl = old_ctx / low_ff, high_wl = old_ctx / high_ff;
+    const double wavelen = 2.0 * 3.14159265358979323846 / inv;
+    if (wavelen > low_wl) return inv / factor;
+    if (wavelen < high_wl) return inv;
+    const double smooth = (old_ctx / wavelen - low_ff) / (high_ff - low_ff);
+    return (1.0 - smooth) * inv / factor + smooth * inv;
+}
+
+// cos/sin of pair i at position pos, exactly as apply_rope_one computes
+// them on the CPU (sf37.c:2020-2024): libm cosf / sinf of the float angle.
+struct RopeKey {
+    uint32_t rotary, llama3, pos;
+    double theta;
+    bool operator==(const RopeKey &o) const {
+        return rotary == o.rotary && llama3 == o.llama3 && pos == o.pos && theta == o.theta;
+    }
+};
+
+static void rope_table(float *t, const RopeKey &k) {
+    for (uint32_t i = 0; i < 64; i++) {
+        t[i] = 1.f;
+        t[64 + i] = 0.f;
+        if (i < k.rotary / 2u) {
+            const float ang = (float)((double)k.pos * rope_inv_freq(i, k.rotary, k.theta, k.llama3));
+            t[i] = cosf(ang);
+            t[64 + i] = sinf(ang);
+        }
+    }
+}
+
+constexpr size_t kPrepSmem = (16 * 128 + 128) * 4;  // prepared q heads + K head (PREP kernels)
 static size_t smem_pipe(int nw, int stages) { return (size_t)nw * stages * 8192 + 2 * 8 * 32 * 16; }
 static size_t smem_pipe32(int nw, int stages) { return (size_t)nw * stages * 16384 + 2 * 8 * 32 * 16; }
 template <int GP, int R>
@@ -1364,8 +1426,26 @@ int attention_jobs(const AttnJob *jobs, uint32_t n, uint32_t q_heads, uint32_t k
     if (!fast) return launch_generic(jobs, n, q_heads, kv_heads, head_dim, dtype, stream);
 
     const int sms = num_sms();
-    for (uint32_t base = 0; base < n; base += kMaxJobs) {
-        const uint32_t m = (n - base) < (uint32_t)kMaxJobs ? (n - base) : (uint32_t)kMaxJobs;
+    for (uint32_t base = 0, m = 0; base < n; base += m) {
+        m = (n - base) < (uint32_t)kMaxJobs ? (n - base) : (uint32_t)kMaxJobs;
+        // q/k preparation: at most kMaxRope distinct RoPE tables per launch
+        RopeKey keys[kMaxRope];
+        uint32_t n_keys = 0, rope_idx[kMaxJobs] = {};
+        for (uint32_t i = 0; i < m; i++) {
+            const AttnJob &A = jobs[base + i];
+            if (!A.prep) continue;
+            const RopeKey k{A.prep->rotary_dim, A.prep->llama3, A.end - 1u, A.prep->theta};
+            uint32_t f = 0;
+            while (f < n_keys && !(keys[f] == k)) f++;
+            if (f == n_keys) {
+                if (n_keys == (uint32_t)kMaxRope) {
+                    m = i;  // the rest goes to the next launch
+                    break;
+                }
+                keys[n_keys++] = k;
+            }
+            rope_idx[i] = f;
+        }
         uint64_t total = 0;
         for (uint32_t i = 0; i < m; i++) total += (uint64_t)(jobs[base + i].end - jobs[base + i].start);
         total *= kv_heads;
@@ -1411,6 +1491,7 @@ int attention_jobs(const AttnJob *jobs, uint32_t n, uint32_t q_heads, uint32_t k
         P.group = G;
         P.part_stride = (G * 130u + 3u) & ~3u;
         P.qscale = kLog2e / sqrtf(128.0f);
+        for (uint32_t f = 0; f < n_keys; f++) rope_table(P.rope[f], keys[f]);
         P.gat = g_gather_cur ? *g_gather_cur : GatherDev{};
         if (P.gat.world) P.gat.total_groups = m * kv_heads;
         uint32_t ctas = 0;
@@ -1434,9 +1515,8 @@ int attention_jobs(const AttnJob *jobs, uint32_t n, uint32_t q_heads, uint32_t k
             if (A.prep) {
                 D.qn = A.prep->q_norm;
                 D.kn = A.prep->k_norm;
-                D.theta = A.prep->theta;
                 D.rotary = A.prep->rotary_dim;
-                D.llama3 = A.prep->llama3;
+                D.rope_idx = rope_idx[i];
                 D.eps = A.prep->eps;
             }
             if ((uint64_t)ctas + ns * kv_heads > 0x7fffffffull)
@@ -1470,7 +1550,14 @@ int attention_jobs(const AttnJob *jobs, uint32_t n, uint32_t q_heads, uint32_t k
                 cudaFuncSetAttribute(decode_f16_pipe_kernel<4, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      (int)smem_pipe(4, 3));
             }
-            switch (variant) {
+            static bool prep_attr = false;
+            if (any_prep && !prep_attr) {
+                cudaFuncSetAttribute(decode_f16_pipe_kernel<4, 3, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)(smem_pipe(4, 3) + kPrepSmem));
+                prep_attr = true;
+            }
+            if (any_prep) decode_f16_pipe_kernel<4, 3, true><<<ctas, 128, smem_pipe(4, 3) + kPrepSmem, stream>>>(P);
+            else switch (variant) {
                 case 1: decode_f16_pipe_kernel<4, 3><<<ctas, 128, smem_pipe(4, 3), stream>>>(P); break;
                 case 2: decode_f16_kernel<kNW, 2><<<ctas, kNW * 32, smem_f16(), stream>>>(P); break;
                 case 3: decode_f16_kernel<kNW, 3><<<ctas, kNW * 32, smem_f16(), stream>>>(P); break;
@@ -1485,7 +1572,15 @@ int attention_jobs(const AttnJob *jobs, uint32_t n, uint32_t q_heads, uint32_t k
                 cudaFuncSetAttribute(decode_f32_pipe_kernel<4, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      (int)smem_pipe32(4, 3));
             }
-            if (!f32_cuda) {
+            static bool prep_attr = false;
+            if (any_prep && !prep_attr) {
+                cudaFuncSetAttribute(decode_f32_pipe_kernel<4, 3, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)(smem_pipe32(4, 3) + kPrepSmem));
+                prep_attr = true;
+            }
+            if (any_prep) {
+                decode_f32_pipe_kernel<4, 3, true><<<ctas, 128, smem_pipe32(4, 3) + kPrepSmem, stream>>>(P);
+            } else if (!f32_cuda) {
                 decode_f32_pipe_kernel<4, 3><<<ctas, 128, smem_pipe32(4, 3), stream>>>(P);
             } else {
                 switch (G) {
