@@ -97,6 +97,16 @@ int sf37_cuda_attention_decode_heads_at(sf37_cuda_tensor *out_heads,
 int sf37_cuda_should_use_managed_kv_cache(uint64_t kv_cache_bytes,
                                           uint64_t context_bytes);
 
+/* sf37_cuda.h:134-137: Q8_0 matvec (the attention output projection after
+ * the decode; sf37_cuda.cu:3708-3734).  out f32 [out_dim], weights
+ * out_dim x (in_dim/32) blocks of 34 bytes, x f32 [in_dim].  Same sizes
+ * checks and 1/0 return; this build needs in_dim % 256 == 0 (true for every
+ * SF37 projection) and returns 0 with a message otherwise. */
+int sf37_cuda_matvec_q8_0(sf37_cuda_tensor *out,
+                          const sf37_cuda_tensor *weights,
+                          uint64_t in_dim, uint64_t out_dim,
+                          const sf37_cuda_tensor *x);
+
 /* sf37_cuda.h:241-248: append n_tok rows into ring slots (pos0+t) % cap. */
 int sf37_cuda_store_kv_cache_batch(sf37_cuda_tensor *k_cache,
                                    sf37_cuda_tensor *v_cache,

@@ -132,6 +132,27 @@ int sf37kv_decode_prep(const sf37kv_decode_layer *layers, const sf37kv_qk_prep *
                        uint32_t n_layers, uint32_t q_heads, uint32_t kv_heads,
                        uint32_t head_dim, int dtype, void *stream);
 
+/* ---- the attention output projection (the step after the path) ----
+ * out[r] = sum over 32-element blocks b of
+ *   (float)dot(wq[r][b], xq[b]) * wscale[r][b] * xscale[b]
+ * with Q8_0 weights (per row in_dim/32 blocks of 34 bytes: f16 scale, 32
+ * int8) and x quantized to the same blocks (scale amax/127, codes
+ * rint(x/scale) in [-128, 127]): sf37_q8_0_matvec (sf37_ops.c:57-123) and
+ * sf37_cuda_matvec_q8_0 (sf37_cuda.cu:3319-3349, 3433-3461, 3708-3734).
+ * x: f32 [in_dim] (e.g. the gated heads sf37kv_decode wrote), out: f32
+ * [out_dim].  in_dim a multiple of 256; weights and x 16-byte aligned. */
+typedef struct {
+    const void *weights;
+    const float *x;
+    float *out;
+} sf37kv_oproj_layer;
+
+/* One launch for n_layers independent layers sharing in_dim / out_dim. */
+int sf37kv_oproj_q8_0(const sf37kv_oproj_layer *layers, uint32_t n_layers, uint32_t in_dim,
+                      uint32_t out_dim, void *stream);
+/* The activation quantization alone: xq [n] int8, xscale [n/32] f32. */
+int sf37kv_q8_0_quantize(const float *x, int8_t *xq, float *xscale, uint64_t n, void *stream);
+
 /* Append n_tok rows per layer: row t -> slot (pos0 + t) % cap
  * (store_kv_cache_batch_kernel, sf37_cuda.cu:6355-6372). */
 typedef struct {

@@ -76,6 +76,8 @@ def lib():
         L.orc_payload_decode_row.argtypes = [_vp, _u32, _u32, _vp]
         L.orc_pack_layer.argtypes = [_vp, _vp, _vp, _int, _u32, _u32, _u32, _u32, _int, _u32, _int]
         L.orc_unpack_layer.argtypes = [_vp, _vp, _vp, _int, _u32, _u32, _u32, _u32, _int, _u32]
+        L.orc_q8_0_quantize.argtypes = [_vp, _vp, _vp, _u64]
+        L.orc_q8_0_matvec.argtypes = [_vp, _vp, _u64, _u64, _vp]
         L.orc_qk_prep.argtypes = [_vp, _u32, _u32, _vp, _u32, ctypes.c_double, _int, _u32, ctypes.c_float]
         _lib = L
     return _lib
@@ -215,11 +217,61 @@ def qk_prep(x, w_bf16, rotary_dim, theta, llama3, pos, eps=1e-5):
     return x
 
 
+def q8_0_quantize(x):
+    """(int8 codes [n], f32 scales [n/32]) of sf37_q8_0_quantize_activation."""
+    x = np.ascontiguousarray(x, np.float32).reshape(-1)
+    xq = np.zeros(((x.size + 31) // 32) * 32, np.int8)
+    xs = np.zeros((x.size + 31) // 32, np.float32)
+    lib().orc_q8_0_quantize(_ptr(x), _ptr(xq), _ptr(xs), x.size)
+    return xq, xs
+
+
+def q8_0_matvec(w, x, out_dim):
+    """sf37_q8_0_matvec: w uint8 [out_dim][in_dim/32*34], x f32 [in_dim]."""
+    x = np.ascontiguousarray(x, np.float32).reshape(-1)
+    w = np.ascontiguousarray(w, np.uint8)
+    out = np.zeros(out_dim, np.float32)
+    lib().orc_q8_0_matvec(_ptr(out), _ptr(w), x.size, out_dim, _ptr(x))
+    return out
+
+
+def q8_0_abs_terms(w, x, out_dim):
+    """sum_b |isum_b * wscale_b * xscale_b| per row: the magnitude a float
+    accumulation error is relative to."""
+    xq, xs = q8_0_quantize(x)
+    nb = xs.size
+    wb = np.asarray(w, np.uint8).reshape(out_dim, nb, 34)
+    ws = wb[:, :, :2].copy().view(np.float16).reshape(out_dim, nb).astype(np.float64)
+    wq = wb[:, :, 2:].view(np.int8).astype(np.int64)
+    isum = (wq * xq.reshape(nb, 32).astype(np.int64)[None]).sum(-1)
+    return np.abs(isum * ws * xs.astype(np.float64)[None]).sum(-1)
+
+
 def bf16_bits_to_f32(w):
     return (np.asarray(w, np.uint16).astype(np.uint32) << 16).view(np.float32)
 
 
 # ----------------------------------------------- the reference's own CPU code
+def ref_q8_0_quantize(x):
+    R = ref()
+    R.sf37_q8_0_quantize_activation.argtypes = [_vp, _vp, _vp, _u64]
+    x = np.ascontiguousarray(x, np.float32).reshape(-1)
+    xq = np.zeros(((x.size + 31) // 32) * 32, np.int8)
+    xs = np.zeros((x.size + 31) // 32, np.float32)
+    R.sf37_q8_0_quantize_activation(_ptr(x), _ptr(xq), _ptr(xs), x.size)
+    return xq, xs
+
+
+def ref_q8_0_matvec(w, x, out_dim):
+    R = ref()
+    R.sf37_q8_0_matvec.argtypes = [_vp, _vp, _u64, _u64, _vp]
+    x = np.ascontiguousarray(x, np.float32).reshape(-1)
+    w = np.ascontiguousarray(w, np.uint8)
+    out = np.zeros(out_dim, np.float32)
+    R.sf37_q8_0_matvec(_ptr(out), _ptr(w), x.size, out_dim, _ptr(x))
+    return out
+
+
 def ref_qk_prep(x, w_bf16, rotary_dim, theta, llama3, pos):
     """The reference's head_rms_norm_weight1 + apply_rope_one (copy of x)."""
     R = ref()

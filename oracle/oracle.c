@@ -358,3 +358,63 @@ void orc_qk_prep(float *x, uint32_t n_head, uint32_t head_dim, const uint16_t *w
         }
     }
 }
+
+/* ---- Q8_0 matvec (the o_proj step after the attention) ----
+ * sf37_q8_0_quantize_activation (sf37_ops.c:57-90): per 32-element block,
+ * d = amax / 127 (the reference build's -ffast-math turns the division by
+ * the constant into a product with its rounded reciprocal), iscale = 1 / d,
+ * q = lrintf(iscale * x) clamped to [-128, 127]; an all-zero block has
+ * d = 0 and q = 0.  sf37_q8_0_row_dot_prequant (sf37_ops.c:92-108): per
+ * weight block (f16 scale + 32 int8, 34 bytes) an exact integer dot,
+ * acc += isum * wscale * xscale in block order. */
+void orc_q8_0_quantize(const float *x, int8_t *xq, float *xs, uint64_t n) {
+    const uint64_t blocks = (n + 31u) / 32u;
+    for (uint64_t b = 0; b < blocks; b++) {
+        const uint64_t off = b * 32u;
+        const uint64_t len = n - off < 32u ? n - off : 32u;
+        float amax = 0.0f;
+        for (uint64_t i = 0; i < len; i++) {
+            const float a = fabsf(x[off + i]);
+            if (a > amax) amax = a;
+        }
+        if (amax == 0.0f) {
+            xs[b] = 0.0f;
+            memset(xq + off, 0, 32);
+            continue;
+        }
+        const float d = amax * (1.0f / 127.0f);
+        const float is = 1.0f / d;
+        xs[b] = d;
+        for (uint64_t i = 0; i < len; i++) {
+            int v = (int)lrintf(is * x[off + i]);
+            if (v > 127) v = 127;
+            if (v < -128) v = -128;
+            xq[off + i] = (int8_t)v;
+        }
+        for (uint64_t i = len; i < 32u; i++) xq[off + i] = 0;
+    }
+}
+
+void orc_q8_0_matvec(float *out, const uint8_t *w, uint64_t in_dim, uint64_t out_dim, const float *x) {
+    const uint64_t blocks = (in_dim + 31u) / 32u;
+    int8_t *xq = (int8_t *)malloc(blocks * 32u);
+    float *xs = (float *)malloc(blocks * sizeof(float));
+    if (!xq || !xs) abort();
+    orc_q8_0_quantize(x, xq, xs, in_dim);
+    for (uint64_t r = 0; r < out_dim; r++) {
+        const uint8_t *row = w + r * blocks * 34u;
+        float acc = 0.0f;
+        for (uint64_t b = 0; b < blocks; b++) {
+            const uint8_t *blk = row + b * 34u;
+            const float ws = orc_f16_to_f32((uint16_t)(blk[0] | (blk[1] << 8)));
+            const int8_t *wq = (const int8_t *)(blk + 2);
+            const uint64_t len = in_dim - b * 32u < 32u ? in_dim - b * 32u : 32u;
+            int isum = 0;
+            for (uint64_t i = 0; i < len; i++) isum += (int)wq[i] * (int)xq[b * 32u + i];
+            acc += (float)isum * ws * xs[b];
+        }
+        out[r] = acc;
+    }
+    free(xs);
+    free(xq);
+}

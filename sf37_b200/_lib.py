@@ -42,6 +42,10 @@ class QkPrep(ctypes.Structure):
                 ("llama3", c_u32), ("eps", c_float), ("reserved", c_u32)]
 
 
+class OprojLayer(ctypes.Structure):
+    _fields_ = [("weights", c_vp), ("x", c_vp), ("out", c_vp)]
+
+
 class PackLayer(ctypes.Structure):
     _fields_ = [("cache", Cache), ("first_pos", c_u32), ("rows", c_u32), ("offset", c_u64)]
 
@@ -80,6 +84,7 @@ SIGNATURES = {
     "sf37_cuda_gqa_single_token_heads": (c_int, [TP, TP, TP, c_u32, c_u32, c_u32]),
     "sf37_cuda_attention_decode_heads": (c_int, [TP] * 5 + [c_u32] * 5 + [c_int, c_u32]),
     "sf37_cuda_attention_decode_heads_at": (c_int, [TP] * 5 + [c_u32] * 5 + [c_int, c_u32]),
+    "sf37_cuda_matvec_q8_0": (c_int, [TP, TP, c_u64, c_u64, TP]),
     "sf37_cuda_should_use_managed_kv_cache": (c_int, [c_u64, c_u64]),
     "sf37_cuda_store_kv_cache_batch": (c_int, [TP] * 4 + [c_u32] * 4),
     "sf37_cuda_attention_prefill_heads": (c_int, [TP] * 5 + [c_u32] * 6 + [c_int, c_u32]),
@@ -118,6 +123,8 @@ SIGNATURES = {
     "sf37kv_ipc_close": (None, [c_vp]),
     "sf37kv_decode_prep": (c_int, [ctypes.POINTER(DecodeLayer), ctypes.POINTER(QkPrep), c_u32, c_u32, c_u32,
                                    c_u32, c_int, c_vp]),
+    "sf37kv_oproj_q8_0": (c_int, [ctypes.POINTER(OprojLayer), c_u32, c_u32, c_u32, c_vp]),
+    "sf37kv_q8_0_quantize": (c_int, [c_vp, c_vp, c_vp, c_u64, c_vp]),
     "sf37kv_decode_gather": (c_int, [ctypes.POINTER(DecodeLayer), c_u32, c_u32, c_u32, c_u32, c_int,
                                      ctypes.POINTER(PeerGather), c_u32, c_vp]),
     "sf37kv_gather_wait": (c_int, [ctypes.POINTER(PeerGather), c_u32, c_vp]),

@@ -51,3 +51,16 @@ def cfg1_inputs(seed: int = 0, cached: int = 2048, q_heads: int = 64, kv_heads: 
     q = normal(seed * 16 + 5, (q_heads, head_dim))
     gate = normal(seed * 16 + 6, (q_heads,))
     return k, v, k_new, v_new, q, gate
+
+
+def q8_0_weights(seed, out_dim, in_dim):
+    """Q8_0 weight rows [out_dim][in_dim/32 blocks x 34 bytes]: f16 scales in
+    [1e-3, 2e-2) and int8 codes uniform in [-127, 127] (the range the
+    reference's quantizer emits)."""
+    rng = np.random.default_rng(seed)
+    nb = in_dim // 32
+    w = np.empty((out_dim, nb, 34), np.uint8)
+    w[:, :, :2] = (rng.random((out_dim, nb)) * 0.019 + 0.001).astype(np.float16).view(np.uint8).reshape(
+        out_dim, nb, 2)
+    w[:, :, 2:] = rng.integers(-127, 128, (out_dim, nb, 32)).astype(np.int8).view(np.uint8)
+    return w.reshape(out_dim, nb * 34)

@@ -15,6 +15,9 @@ Fixtures (all inputs are regenerable from the seeds in sf37_b200.synth):
   kv_push.npz       kv_cache_push of 6 rows into a capacity-4 linear cache
   sessions.npz      session snapshot / payload bytes and loader messages
                     (see sessions() below)
+  q8_0.npz          sf37_q8_0_quantize_activation of an 8192-element x (with
+                    a zero block) and sf37_q8_0_matvec of 16 rows of Q8_0
+                    weights (sf37_b200.synth.q8_0_weights(31, 16, 8192))
   qk_prep.npz       head_rms_norm_weight1 + apply_rope_one on 9 heads at 6
                     positions, full-layer (64, 5e6, llama3) and sliding-layer
                     (128, 1e4) parameters
@@ -101,6 +104,15 @@ def sessions():
                         payload=np.frombuffer(pay, np.uint8), names=np.array(names), msgs=np.array(msgs))
 
 
+def q8_0():
+    x = synth.normal(30, (8192,)) * 2
+    x[64:96] = 0
+    w = synth.q8_0_weights(31, 16, 8192)
+    xq, xs = oracle.ref_q8_0_quantize(x)
+    out = oracle.ref_q8_0_matvec(w, x, 16)
+    np.savez_compressed(os.path.join(OUT, "q8_0.npz"), xq=xq, xs=xs, out=out)
+
+
 QK_POS = (0, 1, 511, 4097, 32768, 131071)
 
 
@@ -119,7 +131,10 @@ if __name__ == "__main__":
         sessions()
     elif len(sys.argv) > 1 and sys.argv[1] == "qk_prep":
         qk_prep()
+    elif len(sys.argv) > 1 and sys.argv[1] == "q8_0":
+        q8_0()
     else:
         main()
         sessions()
         qk_prep()
+        q8_0()

@@ -153,3 +153,47 @@ def test_qk_prep_matches_live_reference():
     # zero head: scale = 1/sqrt(eps) times zero stays zero
     z = np.zeros((1, 128), np.float32)
     assert not np.any(oracle.qk_prep(z, w, 64, 5e6, 1, 9))
+
+
+# ---- Q8_0 o_proj matvec ----
+def _tie_only(a_q, b_q, x, xs):
+    """Codes may differ only where x / scale sits on a .5 tie: the reference
+    build vectorizes iscale * x into a CPU-specific reciprocal estimate."""
+    d = np.nonzero(a_q != b_q)[0]
+    assert np.all(np.abs(a_q[d].astype(int) - b_q[d].astype(int)) == 1)
+    for i in d:
+        t = float(x[i]) / float(xs[i // 32])
+        assert abs(abs(t - np.trunc(t)) - 0.5) < 1e-5 * max(1.0, abs(t)), (i, t)
+    return d.size
+
+
+def test_q8_0_matches_reference_golden():
+    g = _g("q8_0.npz")
+    x = synth.normal(30, (8192,)) * 2
+    x[64:96] = 0
+    w = synth.q8_0_weights(31, 16, 8192)
+    xq, xs = oracle.q8_0_quantize(x)
+    assert np.array_equal(xs, g["xs"])
+    _tie_only(xq, g["xq"], x, xs)
+    assert not np.any(xq[64:96]) and xs[2] == 0
+    # the reference build reassociates the float accumulation: ulp-scale
+    out = oracle.q8_0_matvec(w, x, 16)
+    scale = oracle.q8_0_abs_terms(w, x, 16)
+    assert np.all(np.abs(out - g["out"]) <= 1e-6 * scale + 1e-7)
+
+
+@pytest.mark.skipif(not oracle.ref_available(), reason="oracle/_ref not built")
+def test_q8_0_matches_live_reference():
+    rng = np.random.default_rng(8)
+    ties = 0
+    for t in range(20):
+        x = (rng.standard_normal(4096) * rng.choice([1e-3, 1.0, 40.0])).astype(np.float32)
+        xq, xs = oracle.q8_0_quantize(x)
+        rq, rs = oracle.ref_q8_0_quantize(x)
+        assert np.array_equal(xs, rs)
+        ties += _tie_only(xq, rq, x, xs)
+        w = synth.q8_0_weights(100 + t, 32, 4096)
+        out = oracle.q8_0_matvec(w, x, 32)
+        ref = oracle.ref_q8_0_matvec(w, x, 32)
+        assert np.all(np.abs(out - ref) <= 1e-6 * oracle.q8_0_abs_terms(w, x, 32) + 1e-30)
+    assert ties < 20  # ties are rare (about 1 in 10^5 codes)
