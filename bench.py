@@ -30,6 +30,7 @@ sys.path.insert(0, ROOT)
 
 METRIC = "decode-attn KV-read GB/s (% of 8 TB/s) and tokens/s at 32K ctx, 1/2/4/8 B200"
 QH, KVH, HD, CTX = 64, 8, 128, 32768
+EMBD = 4096  # model width: o_proj output (sf37.c:36)
 LAYERS = 48  # --layers overrides (profiling runs use a small stack)
 
 
@@ -179,6 +180,63 @@ def cpu_baseline(rows):
                       f"reference's own kv_cache_push+attention_decode+gate, fp32 cache holding f16 "
                       f"values), extrapolated linearly to {LAYERS} layers",
             "kv_read_GBps": sample_layers * rows * KVH * HD * 2 * 4 / dt / 1e9}
+
+
+def oproj_leg(dev, stream, op_arr, op_w, x, op_out, steps, peak):
+    """The o_proj kernel alone over all layers (one launch), timed with CUDA
+    events per launch; and the reference's own quantize + matvec kernels
+    (sf37_cuda_matvec_q8_0 of oracle/_ref/libsf37ref_cuda.so), one call per
+    layer, on the same weights and inputs."""
+    import torch
+    from sf37_b200 import kv
+    n_layers = op_w.shape[0]
+    wbytes = op_w.numel()
+    for _ in range(3):
+        kv.oproj(op_arr, QH * HD, EMBD, stream)
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(max(steps, 20))]
+    for a, b_ in evs:
+        a.record(stream)
+        kv.oproj(op_arr, QH * HD, EMBD, stream)
+        b_.record(stream)
+    torch.cuda.synchronize(dev)
+    ms = sum(a.elapsed_time(b_) for a, b_ in evs) / len(evs)
+    alg = wbytes + n_layers * (QH * HD * 4 + EMBD * 4)
+    res = {"kernel": "oproj_q8_0_kernel", "layers": n_layers, "in_dim": QH * HD, "out_dim": EMBD,
+           "launch_ms": ms, "algorithmic_bytes_per_launch": alg,
+           "roofline": {"bound": "hbm", "achieved": alg / (ms * 1e-3) / 1e9, "peak": peak, "unit": "GB/s",
+                        "frac": alg / (ms * 1e-3) / 1e9 / peak}}
+    try:
+        import oracle
+        if not oracle.ref_cuda_available():
+            raise RuntimeError("oracle/_ref/libsf37ref_cuda.so not built")
+        R = oracle.ref_cuda()
+        import ctypes
+        TP = ctypes.POINTER(oracle.RefTensor)
+        R.sf37_cuda_matvec_q8_0.restype = ctypes.c_int
+        R.sf37_cuda_matvec_q8_0.argtypes = [TP, TP, ctypes.c_uint64, ctypes.c_uint64, TP]
+        refout = torch.empty(EMBD, device=dev)
+
+        def rt(t):
+            return oracle.ref_tensor(t.data_ptr(), t.numel() * t.element_size())
+        ts = [(rt(refout), rt(op_w[l]), rt(x[l])) for l in range(n_layers)]
+        for o, w, xx in ts[:3]:
+            R.sf37_cuda_matvec_q8_0(o, w, QH * HD, EMBD, xx)
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        reps = 5
+        for _ in range(reps):
+            for o, w, xx in ts:
+                if not R.sf37_cuda_matvec_q8_0(o, w, QH * HD, EMBD, xx):
+                    raise RuntimeError("reference matvec failed")
+        e1.record()
+        torch.cuda.synchronize(dev)
+        rms = e0.elapsed_time(e1) / reps
+        res["reference_kernels"] = {"ms_all_layers": rms, "GBps": alg / (rms * 1e-3) / 1e9,
+                                    "calls": f"{n_layers} x sf37_cuda_matvec_q8_0 (quantize + matvec kernels)"}
+    except Exception as e:
+        res["reference_kernels"] = {"unavailable": str(e)}
+    return res
 
 
 def reference_gpu_leg(dev, steps):
@@ -334,6 +392,21 @@ def run_ours(args, rank, world):
             dict(q_norm=qw[l], k_norm=kw[l], rotary_dim=64 if l % 4 == 0 else 128,
                  theta=5e6 if l % 4 == 0 else 1e4, llama3=int(l % 4 == 0), eps=1e-5) for l in range(LAYERS)])
 
+    # --oproj: the step continues with each layer's attention output
+    # projection (Q8_0 weights [4096][8192], sf37.c:3367): one more launch.
+    op_arr = None
+    if args.oproj:
+        if world > 1:
+            raise SystemExit("--oproj runs on one GPU")
+        from sf37_b200 import _lib
+        op_w = torch.randint(0, 256, (LAYERS, EMBD, (QH * HD // 32) * 34), dtype=torch.uint8, device=dev,
+                             generator=g)
+        op_w.view(LAYERS, EMBD, QH * HD // 32, 34)[..., 0:2] = torch.tensor([0x1f, 0x22], dtype=torch.uint8,
+                                                                             device=dev)  # f16 scales ~0.004
+        op_out = torch.empty(LAYERS, EMBD, device=dev)
+        op_arr = (_lib.OprojLayer * LAYERS)(*[_lib.OprojLayer(op_w[l].data_ptr(), out[l].data_ptr(),
+                                                              op_out[l].data_ptr()) for l in range(LAYERS)])
+
     def step(i):
         if pg is not None:
             pg.step(all_desc[i], kv.F16, stream)
@@ -342,6 +415,8 @@ def run_ours(args, rank, world):
             kv.decode_prep(all_desc[i], prep_arr, qh_l, kvh_l, HD, kv.F16, stream)
         else:
             kv.decode(all_desc[i], qh_l, kvh_l, HD, kv.F16, stream)
+        if op_arr is not None:
+            kv.oproj(op_arr, QH * HD, EMBD, stream)
         if world > 1:
             dist.all_gather_into_tensor(gathered, out)
 
@@ -401,6 +476,7 @@ def run_ours(args, rank, world):
                     for l in range(LAYERS))
     peak, peak_kind = _peaks()
     achieved = att_bytes / (att_ms * 1e-3) / 1e9
+    op_line = oproj_leg(dev, stream, op_arr, op_w, out, op_out, steps, peak) if op_arr is not None else None
     # ncu DRAM bytes of the full 8-KV-head launch; a rank's launch reads
     # kvh_l/8 of the same rows, so the capture scales by that share
     traffic = _traffic_from_profiles("decode_f16_pipe_cfg2.md") if (LAYERS == 48 and wl == "decode") else None
@@ -513,6 +589,7 @@ def run_ours(args, rank, world):
                    "layers": LAYERS, "ctx": ctx, "q_heads": QH, "kv_heads": KVH, "head_dim": HD,
                    "kv_heads_per_gpu": kvh_l,
                    "qk_prep_fused": bool(args.prep),
+                   "oproj_q8_0": bool(args.oproj),
                    "parallelism": f"kv-head shard x{world}" + (
                        "" if world == 1 else " + NCCL all-gather" if pg is None
                        else " + output gather by peer-memory stores from the decode kernels"),
@@ -532,6 +609,8 @@ def run_ours(args, rank, world):
         line["cpu_baseline"] = cpu
     if ref_gpu:
         line["reference_gpu"] = ref_gpu
+    if op_line:
+        line["oproj"] = op_line
     print(json.dumps(line), flush=True)
 
 
@@ -844,6 +923,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--gather", default="peer", choices=["peer", "nccl"],
                     help="multi-GPU output gather: decode-kernel stores into peer memory, or NCCL")
+    ap.add_argument("--oproj", action="store_true",
+                    help="decode workloads: add each layer's Q8_0 o_proj matvec to the step")
     ap.add_argument("--prep", action="store_true",
                     help="decode workloads: fuse the q/k head norm + RoPE into the step (sf37kv_decode_prep)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")

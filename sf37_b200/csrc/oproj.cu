@@ -11,8 +11,8 @@
 // 4096 x 8192), so the kernel is HBM-bound.  A CTA owns a contiguous run of
 // rows of one layer.  It first queues cp.async copies of its warps' first
 // rows into shared memory, then quantizes x (from L2) into shared memory
-// while those copies are in flight, then each warp walks its rows with a
-// two-stage row pipeline: 8 dp4a per block, a float accumulator per lane
+// while those copies are in flight, then each of its 8 warps walks its rows
+// with a three-stage row pipeline (16 rows, 139 KB, in flight per SM): 8 dp4a per block, a float accumulator per lane
 // and one warp reduction per row.  One launch covers many layers.
 #include <algorithm>
 #include <cstdio>
@@ -27,8 +27,6 @@ extern unsigned long long g_launches;
 
 namespace {
 
-constexpr int kWarps = 4;
-constexpr int kStages = 2;
 
 struct OprojJob {
     const uint8_t *w;
@@ -53,12 +51,17 @@ __device__ __forceinline__ void cp_async_wait() {
     asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
+// kWarps warps per CTA, kStages rows in flight per warp (8 x 3 for rows up
+// to 8.7 KB, fewer for wider rows so the stages fit in shared memory).
+template <int kWarps, int kStages>
 __global__ void __launch_bounds__(kWarps * 32) oproj_q8_0_kernel(const __grid_constant__ OprojParams P) {
     extern __shared__ __align__(16) uint8_t smem[];
     const uint32_t blocks = P.blocks, row_bytes = P.row_bytes;
-    int8_t *xq = reinterpret_cast<int8_t *>(smem);                        // [blocks][32]
-    float *xs = reinterpret_cast<float *>(smem + blocks * 32u);           // [blocks]
-    uint8_t *stage0 = smem + blocks * 36u;                                // [warps][stages][row_bytes]
+    // x codes by block pair p (blocks 2p, 2p+1) at 80 p: the 16-byte pad
+    // makes a lane's 16-byte reads of its pair bank-conflict free.
+    int8_t *xq = reinterpret_cast<int8_t *>(smem);                        // [blocks/2][80]
+    float *xs = reinterpret_cast<float *>(smem + blocks * 40u);           // [blocks]
+    uint8_t *stage0 = smem + blocks * 44u;                                // [warps][stages][row_bytes]
 
     const uint32_t j = blockIdx.x / P.ctas_per_job;
     const OprojJob &J = P.job[j];
@@ -85,22 +88,44 @@ __global__ void __launch_bounds__(kWarps * 32) oproj_q8_0_kernel(const __grid_co
     for (int s = 0; s < kStages - 1; s++) issue(s);
 
     // Quantize x while the first rows load: sf37_q8_0_quantize_activation
-    // (sf37_ops.c:57-90), one warp per 32-element block.
-    for (uint32_t b = warp; b < blocks; b += kWarps) {
-        const float v = J.x[b * 32u + lane];
-        float amax = fabsf(v);
+    // (sf37_ops.c:57-90).  Eight lanes per 32-element block (a float4 each),
+    // all of a thread's loads issued before any use.
+    {
+        constexpr int kPer = 8;  // blocks per 8-lane group per pass
+        const uint32_t grp = threadIdx.x >> 3, sub = threadIdx.x & 7u, n_grp = kWarps * 4u;
+        for (uint32_t b0 = grp; b0 < blocks; b0 += n_grp * kPer) {
+            float4 v[kPer];
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-        int q = 0;
-        float d = 0.f;
-        if (amax > 0.f) {
-            d = amax * (1.0f / 127.0f);
-            const float is = 1.0f / d;
-            q = __float2int_rn(is * v);
-            q = q > 127 ? 127 : (q < -128 ? -128 : q);
+            for (int u = 0; u < kPer; u++) {
+                const uint32_t b = b0 + (uint32_t)u * n_grp;
+                v[u] = b < blocks ? reinterpret_cast<const float4 *>(J.x + b * 32u)[sub]
+                                  : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+#pragma unroll
+            for (int u = 0; u < kPer; u++) {
+                const uint32_t b = b0 + (uint32_t)u * n_grp;
+                float amax = fmaxf(fmaxf(fabsf(v[u].x), fabsf(v[u].y)), fmaxf(fabsf(v[u].z), fabsf(v[u].w)));
+                amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+                amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+                amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 4));
+                if (b >= blocks) continue;
+                uint32_t packed = 0;
+                float d = 0.f;
+                if (amax > 0.f) {
+                    d = amax * (1.0f / 127.0f);
+                    const float is = 1.0f / d;
+                    const float e[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+#pragma unroll
+                    for (int c = 0; c < 4; c++) {
+                        int q = __float2int_rn(is * e[c]);
+                        q = q > 127 ? 127 : (q < -128 ? -128 : q);
+                        packed |= ((uint32_t)q & 0xffu) << (8 * c);
+                    }
+                }
+                *reinterpret_cast<uint32_t *>(xq + (b >> 1) * 80u + (b & 1u) * 32u + sub * 4u) = packed;
+                if (sub == 0) xs[b] = d;
+            }
         }
-        xq[b * 32u + lane] = (int8_t)q;
-        if (lane == 0) xs[b] = d;
     }
     __syncthreads();
 
@@ -109,39 +134,41 @@ __global__ void __launch_bounds__(kWarps * 32) oproj_q8_0_kernel(const __grid_co
         __syncwarp();
         issue(k + kStages - 1);
         const uint8_t *row = my_stage + (k % kStages) * row_bytes;
+        // Lane handles block pairs p = lane, lane + 32, ...: 68 bytes starting
+        // 4-byte aligned (17 words, stride 17 words across lanes: no bank
+        // conflicts).  Block 2p: f16 scale in bytes 0-1, codes in bytes
+        // 2-33 (funnel-shifted words); block 2p+1: scale in bytes 34-35,
+        // codes in words 9-16.
         float acc = 0.f;
-        for (uint32_t b = lane; b < blocks; b += 32u) {
-            const uint8_t *blk = row + b * 34u;
-            const float ws = __half2float(*reinterpret_cast<const __half *>(blk));
-            // 32 int8 weights at blk + 2: 4-byte aligned when b is odd,
-            // else shifted by 2 bytes (funnel-shift adjacent words).
-            int32_t wv[8];
-            if (b & 1u) {
-                const int32_t *p = reinterpret_cast<const int32_t *>(blk + 2);
+        const uint32_t *rw = reinterpret_cast<const uint32_t *>(row);
+        for (uint32_t p = lane; p < blocks / 2u; p += 32u) {
+            uint32_t w[17];
 #pragma unroll
-                for (int i = 0; i < 8; i++) wv[i] = p[i];
-            } else {
-                const uint32_t *p = reinterpret_cast<const uint32_t *>(blk);
-                uint32_t prev = p[0];
-#pragma unroll
-                for (int i = 0; i < 8; i++) {
-                    const uint32_t nxt = p[i + 1];
-                    wv[i] = (int32_t)__funnelshift_r(prev, nxt, 16);
-                    prev = nxt;
-                }
-            }
-            const int4 xa = *reinterpret_cast<const int4 *>(xq + b * 32u);
-            const int4 xb = *reinterpret_cast<const int4 *>(xq + b * 32u + 16u);
-            int isum = 0;
-            isum = __dp4a(wv[0], xa.x, isum);
-            isum = __dp4a(wv[1], xa.y, isum);
-            isum = __dp4a(wv[2], xa.z, isum);
-            isum = __dp4a(wv[3], xa.w, isum);
-            isum = __dp4a(wv[4], xb.x, isum);
-            isum = __dp4a(wv[5], xb.y, isum);
-            isum = __dp4a(wv[6], xb.z, isum);
-            isum = __dp4a(wv[7], xb.w, isum);
-            acc += (float)isum * ws * xs[b];
+            for (int i = 0; i < 17; i++) w[i] = rw[p * 17u + i];
+            const int4 *xp = reinterpret_cast<const int4 *>(xq + p * 80u);
+            const int4 x0 = xp[0], x1 = xp[1], x2 = xp[2], x3 = xp[3];
+            const float2 sx = *reinterpret_cast<const float2 *>(xs + 2u * p);
+            int s0 = 0, s1 = 0;
+            s0 = __dp4a((int)__funnelshift_r(w[0], w[1], 16), x0.x, s0);
+            s0 = __dp4a((int)__funnelshift_r(w[1], w[2], 16), x0.y, s0);
+            s0 = __dp4a((int)__funnelshift_r(w[2], w[3], 16), x0.z, s0);
+            s0 = __dp4a((int)__funnelshift_r(w[3], w[4], 16), x0.w, s0);
+            s0 = __dp4a((int)__funnelshift_r(w[4], w[5], 16), x1.x, s0);
+            s0 = __dp4a((int)__funnelshift_r(w[5], w[6], 16), x1.y, s0);
+            s0 = __dp4a((int)__funnelshift_r(w[6], w[7], 16), x1.z, s0);
+            s0 = __dp4a((int)__funnelshift_r(w[7], w[8], 16), x1.w, s0);
+            s1 = __dp4a((int)w[9], x2.x, s1);
+            s1 = __dp4a((int)w[10], x2.y, s1);
+            s1 = __dp4a((int)w[11], x2.z, s1);
+            s1 = __dp4a((int)w[12], x2.w, s1);
+            s1 = __dp4a((int)w[13], x3.x, s1);
+            s1 = __dp4a((int)w[14], x3.y, s1);
+            s1 = __dp4a((int)w[15], x3.z, s1);
+            s1 = __dp4a((int)w[16], x3.w, s1);
+            const float ws0 = __half2float(__ushort_as_half((unsigned short)(w[0] & 0xffffu)));
+            const float ws1 = __half2float(__ushort_as_half((unsigned short)(w[8] >> 16)));
+            acc += (float)s0 * ws0 * sx.x;
+            acc += (float)s1 * ws1 * sx.y;
         }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
@@ -150,9 +177,17 @@ __global__ void __launch_bounds__(kWarps * 32) oproj_q8_0_kernel(const __grid_co
     cp_async_wait<0>();
 }
 
-size_t oproj_smem(uint32_t blocks, uint32_t row_bytes) {
-    return (size_t)blocks * 36u + (size_t)kWarps * kStages * row_bytes;
+size_t oproj_smem(uint32_t blocks, uint32_t row_bytes, int warps, int stages) {
+    return (size_t)blocks * 44u + (size_t)warps * stages * row_bytes;
 }
+
+struct OprojConfig {
+    int warps, stages;
+    void (*kernel)(OprojParams);
+};
+const OprojConfig kConfigs[] = {{8, 3, oproj_q8_0_kernel<8, 3>},
+                                {8, 2, oproj_q8_0_kernel<8, 2>},
+                                {4, 2, oproj_q8_0_kernel<4, 2>}};
 
 }  // namespace
 
@@ -164,21 +199,30 @@ int oproj_q8_0(const sf37kv_oproj_layer *layers, uint32_t n, uint32_t in_dim, ui
     if (in_dim == 0 || in_dim % 256u || out_dim == 0)
         return set_error(SF37KV_EUNSUPPORTED, "oproj: in_dim %u must be a positive multiple of 256", in_dim);
     const uint32_t blocks = in_dim / 32u, row_bytes = blocks * 34u;
-    const size_t smem = oproj_smem(blocks, row_bytes);
-    if (smem > 227u * 1024u)
+    const OprojConfig *cfg = nullptr;
+    size_t smem = 0;
+    for (const OprojConfig &c : kConfigs) {
+        smem = oproj_smem(blocks, row_bytes, c.warps, c.stages);
+        if (smem <= 227u * 1024u) {
+            cfg = &c;
+            break;
+        }
+    }
+    if (!cfg)
         return set_error(SF37KV_EUNSUPPORTED, "oproj: in_dim %u needs %zu bytes of shared memory", in_dim, smem);
-    static size_t attr = 0;
-    if (smem > attr) {
-        if (int rc = check_cuda(cudaFuncSetAttribute(oproj_q8_0_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    static size_t attr[3] = {0, 0, 0};
+    const int ci = (int)(cfg - kConfigs);
+    if (smem > attr[ci]) {
+        if (int rc = check_cuda(cudaFuncSetAttribute(cfg->kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                      (int)smem),
                                 "oproj smem attribute"))
             return rc;
-        attr = smem;
+        attr[ci] = smem;
     }
     // Rows per CTA: the split of each layer that fills whole waves best
     // (fewest waves per unit of work), as the decode planning does.
     int per_sm = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, oproj_q8_0_kernel, kWarps * 32, smem) != cudaSuccess ||
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, cfg->kernel, cfg->warps * 32, smem) != cudaSuccess ||
         per_sm < 1) {
         (void)cudaGetLastError();
         per_sm = 1;
@@ -188,7 +232,7 @@ int oproj_q8_0(const sf37kv_oproj_layer *layers, uint32_t n, uint32_t in_dim, ui
         const uint64_t slots = (uint64_t)num_sms() * per_sm;
         uint64_t best_c = 1;
         double best = 1e30;
-        const uint64_t max_c = std::max<uint64_t>(1, out_dim / kWarps);
+        const uint64_t max_c = std::max<uint64_t>(1, out_dim / cfg->warps);
         for (uint64_t c = 1; c <= max_c && c <= 4096; c++) {
             const double cost = (double)((c * m + slots - 1) / slots) / (double)c;
             if (cost < best * 0.95) {
@@ -214,7 +258,7 @@ int oproj_q8_0(const sf37kv_oproj_layer *layers, uint32_t n, uint32_t in_dim, ui
             P.job[i] = OprojJob{(const uint8_t *)L.weights, L.x, L.out, i * P.ctas_per_job};
         }
         const unsigned grid = m * P.ctas_per_job;
-        oproj_q8_0_kernel<<<grid, kWarps * 32, smem, stream>>>(P);
+        cfg->kernel<<<grid, cfg->warps * 32, smem, stream>>>(P);
         g_launches++;
         if (int rc = check_cuda(cudaGetLastError(), "oproj launch")) return rc;
     }

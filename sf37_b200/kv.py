@@ -201,3 +201,8 @@ def launch_count() -> int:
 def device_error(clear=False) -> int:
     """The device error flag (0 = none, 2 = a bounded wait timed out); syncs."""
     return lib().sf37kv_device_error(int(bool(clear)))
+
+
+def oproj(layers, in_dim, out_dim, stream=None):
+    """Q8_0 o_proj matvec of every layer in one launch (sf37kv_oproj_q8_0)."""
+    check(lib().sf37kv_oproj_q8_0(layers, len(layers), in_dim, out_dim, _sp(stream)), "sf37kv_oproj_q8_0")
