@@ -491,14 +491,22 @@ def run_ours(args, rank, world):
     h_gate = torch.empty_like(gate, device="cpu").pin_memory()
     h_kn = torch.empty_like(kn, device="cpu").pin_memory()
     h_vn = torch.empty_like(vn, device="cpu").pin_memory()
-    h_outs = [(torch.empty(LAYERS, QH, HD) if world > 1 else torch.empty_like(out, device="cpu")).pin_memory()
-              for _ in range(2)]
+    h_outs = [(torch.empty(LAYERS, EMBD) if op_arr is not None else torch.empty(LAYERS, QH, HD) if world > 1
+               else torch.empty_like(out, device="cpu")).pin_memory() for _ in range(2)]
     for t_ in (h_q, h_gate, h_kn, h_vn):
         t_.normal_()
     h2d = sum(t_.numel() * t_.element_size() for t_ in (h_q, h_gate, h_kn, h_vn))
     d2h = h_outs[0].numel() * h_outs[0].element_size()
     bufs = [dict(q=q, gate=gate, kn=kn, vn=vn, out=out, gathered=gathered)]
     bufs.append({k_: v_.clone() for k_, v_ in bufs[0].items()})
+    op_arrs = None
+    if op_arr is not None:
+        from sf37_b200 import _lib
+        for B in bufs:
+            B["op_out"] = torch.empty(LAYERS, EMBD, device=dev)
+        op_arrs = [(_lib.OprojLayer * LAYERS)(*[_lib.OprojLayer(op_w[l].data_ptr(), B["out"][l].data_ptr(),
+                                                                B["op_out"][l].data_ptr()) for l in range(LAYERS)])
+                   for B in bufs]
 
     def descs_b(pos, B):
         return kv.decode_layers_desc([
@@ -531,13 +539,20 @@ def run_ours(args, rank, world):
             pg.step(e2e_desc[i % 4][bb], kv.F16, stream)
             B["gathered"].copy_(pg.gathered[pg.epoch & 1])
         else:
-            kv.decode(e2e_desc[i % 4][bb], qh_l, kvh_l, HD, kv.F16, stream)
+            if prep_arr is not None:
+                kv.decode_prep(e2e_desc[i % 4][bb], prep_arr, qh_l, kvh_l, HD, kv.F16, stream)
+            else:
+                kv.decode(e2e_desc[i % 4][bb], qh_l, kvh_l, HD, kv.F16, stream)
+            if op_arrs is not None:
+                kv.oproj(op_arrs[bb], QH * HD, EMBD, stream)
             if world > 1:
                 dist.all_gather_into_tensor(B["gathered"], B["out"])
         ev_done[bb].record(stream)
         out_s.wait_event(ev_done[bb])
         with torch.cuda.stream(out_s):
-            if world > 1:
+            if op_arrs is not None:
+                h_outs[bb].copy_(B["op_out"], non_blocking=True)
+            elif world > 1:
                 h_outs[bb].view(LAYERS, world, qh_l, HD).copy_(B["gathered"].permute(1, 0, 2, 3), non_blocking=True)
             else:
                 h_outs[bb].copy_(B["out"], non_blocking=True)
