@@ -261,6 +261,21 @@ int sf37kv_decode_gather(const sf37kv_decode_layer *layers, uint32_t n_layers,
  * on timeout the device error flag is set to 2 (sf37kv_device_error). */
 int sf37kv_gather_wait(const sf37kv_peer_gather *g, uint32_t epoch, void *stream);
 
+/* Row-parallel o_proj across the KV-head shards: rank r passes its query
+ * heads' slice of x (in_dim = 8192/N elements) and the matching column
+ * slice of every weight row (weights = row start + r * in_dim/32 * 34
+ * bytes, row_stride = the full row's bytes).  Each rank's partial rows are
+ * stored into every rank's buffer of g (f32 [2][world][n_layers][out_dim],
+ * half epoch & 1, slot rank; layers[i].out is ignored) and its epoch flag
+ * is raised after the last store; sf37kv_oproj_reduce then waits (bounded,
+ * about 2 s; error flag 2 on timeout) and sums the slots in rank order into
+ * out [n_layers][out_dim] (the same bits on every rank).  1..64 layers. */
+int sf37kv_oproj_q8_0_shard(const sf37kv_oproj_layer *layers, uint32_t n_layers, uint32_t in_dim,
+                            uint32_t out_dim, uint64_t row_stride, const sf37kv_peer_gather *g,
+                            uint32_t epoch, void *stream);
+int sf37kv_oproj_reduce(const sf37kv_peer_gather *g, uint32_t n_layers, uint32_t out_dim,
+                        uint32_t epoch, float *out, void *stream);
+
 /* Number of kernel launches this library has issued (process total). */
 uint64_t sf37kv_launch_count(void);
 

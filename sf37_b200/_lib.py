@@ -124,6 +124,9 @@ SIGNATURES = {
     "sf37kv_decode_prep": (c_int, [ctypes.POINTER(DecodeLayer), ctypes.POINTER(QkPrep), c_u32, c_u32, c_u32,
                                    c_u32, c_int, c_vp]),
     "sf37kv_oproj_q8_0": (c_int, [ctypes.POINTER(OprojLayer), c_u32, c_u32, c_u32, c_vp]),
+    "sf37kv_oproj_q8_0_shard": (c_int, [ctypes.POINTER(OprojLayer), c_u32, c_u32, c_u32, c_u64,
+                                        ctypes.POINTER(PeerGather), c_u32, c_vp]),
+    "sf37kv_oproj_reduce": (c_int, [ctypes.POINTER(PeerGather), c_u32, c_u32, c_u32, c_vp, c_vp]),
     "sf37kv_q8_0_quantize": (c_int, [c_vp, c_vp, c_vp, c_u64, c_vp]),
     "sf37kv_decode_gather": (c_int, [ctypes.POINTER(DecodeLayer), c_u32, c_u32, c_u32, c_u32, c_int,
                                      ctypes.POINTER(PeerGather), c_u32, c_vp]),

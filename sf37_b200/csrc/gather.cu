@@ -12,6 +12,7 @@
 // of any other (it waits for everyone's flag of the previous epoch), so the
 // half it writes was consumed by every reader before that reader's own
 // previous decode launch (stream order).
+#include <algorithm>
 #include <cstring>
 
 #include "kv_internal.cuh"
@@ -76,7 +77,8 @@ extern "C" void sf37kv_ipc_close(void *p) {
     if (p) cudaIpcCloseMemHandle(p);
 }
 
-static int gather_dev(const sf37kv_peer_gather *g, uint32_t epoch, GatherDev *d) {
+namespace sf37kv {
+int gather_dev(const sf37kv_peer_gather *g, uint32_t epoch, GatherDev *d) {
     if (!g || g->world < 1 || g->world > 8 || g->rank >= g->world)
         return set_error(SF37KV_EINVAL, "gather: world must be 1..8 and rank < world");
     memset(d, 0, sizeof(*d));
@@ -93,6 +95,7 @@ static int gather_dev(const sf37kv_peer_gather *g, uint32_t epoch, GatherDev *d)
     if (!d->done) return set_error(SF37KV_EINVAL, "gather: done_counter is NULL");
     return SF37KV_OK;
 }
+}  // namespace sf37kv
 
 extern "C" int sf37kv_decode_gather(const sf37kv_decode_layer *layers, uint32_t n_layers, uint32_t q_heads,
                                     uint32_t kv_heads, uint32_t head_dim, int dtype,
@@ -127,4 +130,71 @@ extern "C" int sf37kv_gather_wait(const sf37kv_peer_gather *g, uint32_t epoch, v
     gather_wait_kernel<<<1, 32, 0, s>>>((const uint32_t *)g->my_flags, g->world, epoch, err);
     g_launches++;
     return check_cuda(cudaGetLastError(), "gather wait launch");
+}
+
+// ---------------------------------------------------------------- reduce
+// Sum of the world partial vectors that sf37kv_oproj_q8_0_shard stored into
+// this rank's buffer half: every CTA first waits (bounded, as
+// gather_wait_kernel) for all ranks' epoch flags, then adds the slots in rank
+// order 0..world-1, so every rank gets the same bits.
+namespace sf37kv {
+__global__ void reduce_slots_kernel(const float *half_base, const uint32_t *flags, uint32_t world, uint32_t epoch,
+                                    uint64_t n4, float *out, int *err) {
+    __shared__ int ok;
+    if (threadIdx.x < 32) {
+        bool fine = true;
+        if (threadIdx.x < world) {
+            const long long t0 = clock64();
+            for (;;) {
+                uint32_t v;
+                asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(flags + threadIdx.x) : "memory");
+                if ((int32_t)(v - epoch) >= 0) break;
+                if (clock64() - t0 > 4000000000ll) {
+                    fine = false;
+                    break;
+                }
+                __nanosleep(200);
+            }
+        }
+        fine = __all_sync(0xffffffffu, fine);
+        if (threadIdx.x == 0) ok = fine;
+    }
+    __syncthreads();
+    if (!ok) {
+        if (threadIdx.x == 0) atomicExch(err, 2);
+        return;
+    }
+    const float4 *src = reinterpret_cast<const float4 *>(half_base);
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (uint64_t)gridDim.x * blockDim.x) {
+        float4 s = src[i];
+        for (uint32_t p = 1; p < world; p++) {
+            const float4 v = src[p * n4 + i];
+            s.x += v.x;
+            s.y += v.y;
+            s.z += v.z;
+            s.w += v.w;
+        }
+        reinterpret_cast<float4 *>(out)[i] = s;
+    }
+}
+}  // namespace sf37kv
+
+extern "C" int sf37kv_oproj_reduce(const sf37kv_peer_gather *g, uint32_t n_layers, uint32_t out_dim, uint32_t epoch,
+                                   float *out, void *stream) {
+    GatherDev d;
+    if (int rc = gather_dev(g, epoch, &d)) return rc;
+    if (!out || !g->my_flags) return set_error(SF37KV_EINVAL, "oproj_reduce: NULL output or flags");
+    if (out_dim % 4u || ((uintptr_t)out & 15u))
+        return set_error(SF37KV_EINVAL, "oproj_reduce: out_dim must be a multiple of 4 and out 16-byte aligned");
+    int *err = device_error_flag();
+    if (!err) return set_error(SF37KV_ECUDA, "oproj_reduce: no device error flag");
+    const uint64_t n = (uint64_t)n_layers * out_dim;
+    const float *half = (const float *)g->peer_buf[g->rank] + (uint64_t)(epoch & 1u) * g->world * n;
+    cudaStream_t s = stream ? (cudaStream_t)stream : current_stream();
+    const uint64_t n4 = n / 4u;
+    unsigned grid = (unsigned)std::min<uint64_t>((n4 + 255u) / 256u, (uint64_t)num_sms() * 2u);
+    if (grid == 0) grid = 1;
+    reduce_slots_kernel<<<grid, 256, 0, s>>>(half, (const uint32_t *)g->my_flags, g->world, epoch, n4, out, err);
+    g_launches++;
+    return check_cuda(cudaGetLastError(), "oproj reduce launch");
 }

@@ -92,6 +92,9 @@ struct GatherDev {
     uint32_t *done;  // groups finished in this launch (self-resetting)
 };
 
+// Validates a peer descriptor and fills the device form (gather.cu).
+int gather_dev(const sf37kv_peer_gather *g, uint32_t epoch, GatherDev *d);
+
 int attention_jobs_gather(const AttnJob *jobs, uint32_t n, uint32_t q_heads, uint32_t kv_heads,
                           uint32_t head_dim, int dtype, cudaStream_t stream, const GatherDev *gat,
                           const uint64_t *offsets);

@@ -33,6 +33,7 @@ struct OprojJob {
     const float *x;
     float *out;
     uint32_t cta_begin;  // first CTA of this job
+    uint64_t red_off;    // float offset of this layer's partial in the peers' buffers
 };
 
 struct OprojParams {
@@ -40,7 +41,11 @@ struct OprojParams {
     uint32_t n_jobs;
     uint32_t in_dim, blocks, row_bytes, out_dim;
     uint32_t rows_per_cta, ctas_per_job;
+    uint64_t row_stride;  // bytes between weight rows (>= row_bytes: a column slice)
+    GatherDev red;        // world > 0: partial sums go to every rank (sf37kv_oproj_q8_0_shard)
 };
+
+constexpr uint32_t kMaxRowsPerCta = 1024;
 
 __device__ __forceinline__ void cp_async16(uint32_t saddr, const void *g) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(saddr), "l"(g) : "memory");
@@ -62,6 +67,7 @@ __global__ void __launch_bounds__(kWarps * 32) oproj_q8_0_kernel(const __grid_co
     int8_t *xq = reinterpret_cast<int8_t *>(smem);                        // [blocks/2][80]
     float *xs = reinterpret_cast<float *>(smem + blocks * 40u);           // [blocks]
     uint8_t *stage0 = smem + blocks * 44u;                                // [warps][stages][row_bytes]
+    float *osm = reinterpret_cast<float *>(stage0 + (uint32_t)kWarps * kStages * row_bytes);  // [rows]
 
     const uint32_t j = blockIdx.x / P.ctas_per_job;
     const OprojJob &J = P.job[j];
@@ -78,7 +84,7 @@ __global__ void __launch_bounds__(kWarps * 32) oproj_q8_0_kernel(const __grid_co
     auto issue = [&](uint32_t k) {
         if (k < n_mine) {
             const uint32_t row = r0 + warp + k * kWarps;
-            const uint8_t *src = J.w + (uint64_t)row * row_bytes;
+            const uint8_t *src = J.w + (uint64_t)row * P.row_stride;
             const uint32_t dst = stage_addr + (k % kStages) * row_bytes;
             for (uint32_t c = lane; c < chunks16; c += 32u) cp_async16(dst + c * 16u, src + c * 16u);
         }
@@ -172,13 +178,39 @@ __global__ void __launch_bounds__(kWarps * 32) oproj_q8_0_kernel(const __grid_co
         }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-        if (lane == 0) J.out[r0 + warp + k * kWarps] = acc;
+        if (lane == 0) {
+            if (P.red.world) osm[warp + k * kWarps] = acc;
+            else J.out[r0 + warp + k * kWarps] = acc;
+        }
     }
     cp_async_wait<0>();
+    if (P.red.world) {
+        // Row-parallel layers: this CTA's partial rows go to every rank's
+        // buffer (coalesced NVLink stores); the last CTA of the launch raises
+        // this rank's epoch flag everywhere (as the decode gather does).
+        __syncthreads();
+        const uint32_t nr = r1 - r0;
+        for (uint32_t i = threadIdx.x; i < nr; i += blockDim.x) {
+            const float v = osm[i];
+            J.out[r0 + i] = v;
+            for (uint32_t p = 0; p < P.red.world; p++)
+                if (p != P.red.rank) P.red.peer[p][J.red_off + r0 + i] = v;
+        }
+        __threadfence_system();
+        __syncthreads();
+        if (threadIdx.x == 0 && atomicAdd(P.red.done, 1u) == P.red.total_groups - 1u) {
+            __threadfence_system();
+            for (uint32_t p = 0; p < P.red.world; p++) {
+                uint32_t *f = P.red.peer_flags[p] + P.red.rank;
+                asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(f), "r"(P.red.epoch) : "memory");
+            }
+            *P.red.done = 0u;
+        }
+    }
 }
 
 size_t oproj_smem(uint32_t blocks, uint32_t row_bytes, int warps, int stages) {
-    return (size_t)blocks * 44u + (size_t)warps * stages * row_bytes;
+    return (size_t)blocks * 44u + (size_t)warps * stages * row_bytes + kMaxRowsPerCta * 4u;
 }
 
 struct OprojConfig {
@@ -191,14 +223,22 @@ const OprojConfig kConfigs[] = {{8, 3, oproj_q8_0_kernel<8, 3>},
 
 }  // namespace
 
-// One launch for n layers sharing in_dim / out_dim.
+// One launch per 64 layers sharing in_dim / out_dim.  row_stride: bytes
+// between weight rows; red / red_off: row-parallel partial sums to peers.
 int oproj_q8_0(const sf37kv_oproj_layer *layers, uint32_t n, uint32_t in_dim, uint32_t out_dim,
-               cudaStream_t stream) {
+               cudaStream_t stream, uint64_t row_stride = 0, const GatherDev *red = nullptr,
+               const uint64_t *red_off = nullptr) {
     if (n == 0) return SF37KV_OK;
     if (!layers) return set_error(SF37KV_EINVAL, "oproj: layers is NULL");
     if (in_dim == 0 || in_dim % 256u || out_dim == 0)
         return set_error(SF37KV_EUNSUPPORTED, "oproj: in_dim %u must be a positive multiple of 256", in_dim);
     const uint32_t blocks = in_dim / 32u, row_bytes = blocks * 34u;
+    if (row_stride == 0) row_stride = row_bytes;
+    if (row_stride < row_bytes || row_stride % 16u)
+        return set_error(SF37KV_EINVAL, "oproj: row stride %llu must be >= %u and a multiple of 16",
+                         (unsigned long long)row_stride, row_bytes);
+    if (red && n > (uint32_t)kMaxJobs)
+        return set_error(SF37KV_EINVAL, "oproj: at most %d layers per row-parallel call", kMaxJobs);
     const OprojConfig *cfg = nullptr;
     size_t smem = 0;
     for (const OprojConfig &c : kConfigs) {
@@ -230,10 +270,11 @@ int oproj_q8_0(const sf37kv_oproj_layer *layers, uint32_t n, uint32_t in_dim, ui
     for (uint32_t base = 0; base < n; base += kMaxJobs) {
         const uint32_t m = std::min<uint32_t>(n - base, kMaxJobs);
         const uint64_t slots = (uint64_t)num_sms() * per_sm;
-        uint64_t best_c = 1;
+        uint64_t best_c = (out_dim + kMaxRowsPerCta - 1) / kMaxRowsPerCta;
         double best = 1e30;
         const uint64_t max_c = std::max<uint64_t>(1, out_dim / cfg->warps);
-        for (uint64_t c = 1; c <= max_c && c <= 4096; c++) {
+        const uint64_t min_c = (out_dim + kMaxRowsPerCta - 1) / kMaxRowsPerCta;
+        for (uint64_t c = min_c; c <= std::max(max_c, min_c) && c <= 4096; c++) {
             const double cost = (double)((c * m + slots - 1) / slots) / (double)c;
             if (cost < best * 0.95) {
                 best = cost;
@@ -249,13 +290,19 @@ int oproj_q8_0(const sf37kv_oproj_layer *layers, uint32_t n, uint32_t in_dim, ui
         P.out_dim = out_dim;
         P.rows_per_cta = (uint32_t)((out_dim + best_c - 1) / best_c);
         P.ctas_per_job = (out_dim + P.rows_per_cta - 1) / P.rows_per_cta;
+        P.row_stride = row_stride;
+        if (red) {
+            P.red = *red;
+            P.red.total_groups = m * P.ctas_per_job;
+        }
         for (uint32_t i = 0; i < m; i++) {
             const sf37kv_oproj_layer &L = layers[base + i];
             if (!L.weights || !L.x || !L.out)
                 return set_error(SF37KV_EINVAL, "oproj: layer %u has a NULL pointer", base + i);
             if (((uintptr_t)L.weights | (uintptr_t)L.x) & 15u)
                 return set_error(SF37KV_EINVAL, "oproj: layer %u weights and x must be 16-byte aligned", base + i);
-            P.job[i] = OprojJob{(const uint8_t *)L.weights, L.x, L.out, i * P.ctas_per_job};
+            P.job[i] = OprojJob{(const uint8_t *)L.weights, L.x, L.out, i * P.ctas_per_job,
+                                red_off ? red_off[base + i] : 0};
         }
         const unsigned grid = m * P.ctas_per_job;
         cfg->kernel<<<grid, cfg->warps * 32, smem, stream>>>(P);
@@ -294,6 +341,25 @@ using namespace sf37kv;
 extern "C" int sf37kv_oproj_q8_0(const sf37kv_oproj_layer *layers, uint32_t n_layers, uint32_t in_dim,
                                  uint32_t out_dim, void *stream) {
     return oproj_q8_0(layers, n_layers, in_dim, out_dim, stream ? (cudaStream_t)stream : current_stream());
+}
+
+extern "C" int sf37kv_oproj_q8_0_shard(const sf37kv_oproj_layer *layers, uint32_t n_layers, uint32_t in_dim,
+                                       uint32_t out_dim, uint64_t row_stride, const sf37kv_peer_gather *g,
+                                       uint32_t epoch, void *stream) {
+    GatherDev d;
+    if (int rc = gather_dev(g, epoch, &d)) return rc;
+    if (n_layers == 0 || n_layers > (uint32_t)kMaxJobs)
+        return set_error(SF37KV_EINVAL, "oproj_shard: 1..%d layers per call", kMaxJobs);
+    sf37kv_oproj_layer L[kMaxJobs];
+    uint64_t off[kMaxJobs];
+    const uint64_t n = (uint64_t)n_layers * out_dim;
+    for (uint32_t i = 0; i < n_layers; i++) {
+        off[i] = ((uint64_t)(epoch & 1u) * g->world + g->rank) * n + (uint64_t)i * out_dim;
+        L[i] = layers[i];
+        L[i].out = (float *)g->peer_buf[g->rank] + off[i];
+    }
+    return oproj_q8_0(L, n_layers, in_dim, out_dim, stream ? (cudaStream_t)stream : current_stream(), row_stride,
+                      &d, off);
 }
 
 extern "C" int sf37kv_q8_0_quantize(const float *x, int8_t *xq, float *xscale, uint64_t n, void *stream) {

@@ -74,19 +74,18 @@ class _CudaArray:
                                          "data": (int(ptr), False), "version": 2}
 
 
-class PeerGather:
-    """Output gather over peer memory for sf37kv_decode_gather (see
-    include/sf37kv.h): one zero-filled device buffer per rank holding
-    [world][n_layers][q_local][head_dim] f32 outputs followed by the rank flag
-    array and a done counter, shared with the other ranks by CUDA IPC."""
+class _PeerBuffer:
+    """One zero-filled device buffer per rank (sf37kv_dev_alloc): `floats`
+    f32 of payload, then the ranks' epoch flags and a done counter; mapped
+    into every other rank by CUDA IPC.  `struct` is the sf37kv_peer_gather
+    descriptor the library calls take."""
 
-    def __init__(self, plan: ShardPlan, n_layers: int, group=None):
+    def __init__(self, world, rank, floats, group=None):
         import ctypes
         from ._lib import PeerGather as PG, lib
-        self.plan, self.n_layers = plan, n_layers
         L = lib()
         self._lib = L
-        floats = 2 * plan.world * n_layers * plan.q_local * plan.head_dim
+        self.world, self.rank = world, rank
         self.off_flags = (floats * 4 + 255) // 256 * 256
         self.off_done = self.off_flags + 256
         self.base = L.sf37kv_dev_alloc(self.off_done + 256)
@@ -96,12 +95,12 @@ class PeerGather:
         if L.sf37kv_ipc_handle(self.base, h):
             raise RuntimeError("sf37kv_ipc_handle failed")
         torch.cuda.synchronize()
-        handles = [None] * plan.world
+        handles = [None] * world
         dist.all_gather_object(handles, bytes(h.raw), group=group)
         self.peers = []
         st = PG()
-        for p in range(plan.world):
-            if p == plan.rank:
+        for p in range(world):
+            if p == rank:
                 ptr = self.base
             else:
                 ptr = L.sf37kv_ipc_open(ctypes.create_string_buffer(handles[p], 64))
@@ -112,12 +111,32 @@ class PeerGather:
             st.peer_flags[p] = ptr + self.off_flags
         st.my_flags = self.base + self.off_flags
         st.done_counter = self.base + self.off_done
-        st.world, st.rank = plan.world, plan.rank
+        st.world, st.rank = world, rank
         self.struct = st
         self.epoch = 0
-        self.gathered = torch.as_tensor(
-            _CudaArray(self.base, (2, plan.world, n_layers, plan.q_local, plan.head_dim)), device="cuda")
         dist.barrier(group=group)
+
+    def view(self, shape):
+        return torch.as_tensor(_CudaArray(self.base, shape), device="cuda")
+
+    def close(self):
+        for p in self.peers:
+            self._lib.sf37kv_ipc_close(p)
+        self.peers = []
+        if self.base:
+            self._lib.sf37kv_dev_free(self.base)
+            self.base = None
+
+
+class PeerGather(_PeerBuffer):
+    """Output gather over peer memory for sf37kv_decode_gather (see
+    include/sf37kv.h): [2][world][n_layers][q_local][head_dim] f32 outputs,
+    the half selected by the step's epoch parity."""
+
+    def __init__(self, plan: ShardPlan, n_layers: int, group=None):
+        self.plan, self.n_layers = plan, n_layers
+        super().__init__(plan.world, plan.rank, 2 * plan.world * n_layers * plan.q_local * plan.head_dim, group)
+        self.gathered = self.view((2, plan.world, n_layers, plan.q_local, plan.head_dim))
 
     def heads(self) -> torch.Tensor:
         """[n_layers, q_heads, head_dim] outputs of the last completed step
@@ -142,10 +161,32 @@ class PeerGather:
                                              self.epoch, sp), "sf37kv_decode_gather")
         check(self._lib.sf37kv_gather_wait(ctypes.byref(self.struct), self.epoch, sp), "sf37kv_gather_wait")
 
-    def close(self):
-        for p in self.peers:
-            self._lib.sf37kv_ipc_close(p)
-        self.peers = []
-        if self.base:
-            self._lib.sf37kv_dev_free(self.base)
-            self.base = None
+
+class PeerReduce(_PeerBuffer):
+    """Row-parallel o_proj (sf37kv_oproj_q8_0_shard + sf37kv_oproj_reduce):
+    each rank multiplies its heads' columns and the partial [n_layers][out_dim]
+    vectors are summed across ranks over peer memory."""
+
+    def __init__(self, world, rank, n_layers, out_dim, group=None):
+        self.n_layers, self.out_dim = n_layers, out_dim
+        super().__init__(world, rank, 2 * world * n_layers * out_dim, group)
+
+    @staticmethod
+    def weight_slice(w_rows: torch.Tensor, world: int, rank: int):
+        """(pointer offset in bytes, row stride) of rank's column slice of
+        Q8_0 rows w_rows [out_dim][in_dim/32*34]."""
+        row_bytes = w_rows.shape[-1]
+        return rank * row_bytes // world, row_bytes
+
+    def step(self, layers, in_dim_local, row_stride, out, stream=None):
+        """layers: ctypes OprojLayer array (x = this rank's heads, weights =
+        its column slice); out: [n_layers][out_dim] f32, the summed result."""
+        import ctypes
+        from ._lib import check
+        self.epoch += 1
+        sp = None if stream is None else ctypes.c_void_p(stream.cuda_stream)
+        check(self._lib.sf37kv_oproj_q8_0_shard(layers, len(layers), in_dim_local, self.out_dim, row_stride,
+                                                ctypes.byref(self.struct), self.epoch, sp),
+              "sf37kv_oproj_q8_0_shard")
+        check(self._lib.sf37kv_oproj_reduce(ctypes.byref(self.struct), self.n_layers, self.out_dim, self.epoch,
+                                            out.data_ptr(), sp), "sf37kv_oproj_reduce")

@@ -82,3 +82,62 @@ def test_sharded_decode_2gpu(mode):
         for step, pos in enumerate(positions):
             want = oracle.attention_decode_at(synth.normal(30 + l, (64, 128)), k, v, None, pos, 5000, 64, 8, 128)
             assert_close(got[step][l], want)
+
+
+def _oproj_worker(rank, world, port, result):
+    import torch.distributed as dist
+    from sf37_b200 import _lib, synth
+    from sf37_b200.shard import PeerReduce
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world)
+    layers, in_dim, out_dim = 3, 8192, 4096
+    local = in_dim // world
+    pr = PeerReduce(world, rank, layers, out_dim)
+    got = []
+    for step in range(3):  # both buffer halves
+        ws, xs = [], []
+        for l in range(layers):
+            w = torch.from_numpy(synth.q8_0_weights(10 * step + l, out_dim, in_dim)).cuda()
+            x = torch.from_numpy(synth.normal(100 * step + l, (in_dim,)) * (l + 1)).cuda()
+            off, stride = PeerReduce.weight_slice(w, world, rank)
+            ws.append((w, off, stride))
+            xs.append(x[rank * local:(rank + 1) * local].contiguous())
+        arr = (_lib.OprojLayer * layers)(*[_lib.OprojLayer(w.data_ptr() + off, xs[l].data_ptr(), 0)
+                                          for l, (w, off, stride) in enumerate(ws)])
+        out = torch.empty(layers, out_dim, device="cuda")
+        pr.step(arr, local, ws[0][2], out)
+        got.append(out.cpu().numpy())
+    assert _lib.lib().sf37kv_device_error(1) == 0
+    dist.barrier()
+    torch.cuda.synchronize()
+    pr.close()
+    result.put((rank, got))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_row_parallel_oproj_2gpu():
+    import oracle
+    from sf37_b200 import synth
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    ps = [ctx.Process(target=_oproj_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    res = dict(q.get(timeout=300) for _ in range(2))
+    for p in ps:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    for step in range(3):
+        assert np.array_equal(res[0][step], res[1][step])  # same bits on every rank
+        for l in range(3):
+            w = synth.q8_0_weights(10 * step + l, 4096, 8192)
+            x = synth.normal(100 * step + l, (8192,)) * (l + 1)
+            want = oracle.q8_0_matvec(w, x, 4096)
+            bound = 4e-6 * oracle.q8_0_abs_terms(w, x, 4096) + 1e-30
+            assert np.all(np.abs(res[0][step][l] - want) <= bound)
