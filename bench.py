@@ -377,7 +377,7 @@ def run_ours(args, rank, world):
     # output head straight into all ranks' buffers over NVLink (PeerGather);
     # --gather nccl runs the decode and then an NCCL all-gather instead.
     pg = None
-    if world > 1 and args.gather == "peer":
+    if world > 1 and args.gather == "peer" and not args.oproj:
         from sf37_b200.shard import PeerGather, ShardPlan
         pg = PeerGather(ShardPlan(world, rank, KVH, QH, HD), LAYERS)
 
@@ -394,18 +394,30 @@ def run_ours(args, rank, world):
 
     # --oproj: the step continues with each layer's attention output
     # projection (Q8_0 weights [4096][8192], sf37.c:3367): one more launch.
-    op_arr = None
+    # With N GPUs the projection is row-parallel: rank r keeps the weight
+    # columns of its own heads (1/N of each row), multiplies its heads, and
+    # the partial outputs are summed across ranks over peer memory
+    # (PeerReduce); the heads themselves are never gathered.
+    op_arr = pr = None
+    in_local = QH * HD // world
     if args.oproj:
-        if world > 1:
-            raise SystemExit("--oproj runs on one GPU")
         from sf37_b200 import _lib
-        op_w = torch.randint(0, 256, (LAYERS, EMBD, (QH * HD // 32) * 34), dtype=torch.uint8, device=dev,
+        op_w = torch.randint(0, 256, (LAYERS, EMBD, (in_local // 32) * 34), dtype=torch.uint8, device=dev,
                              generator=g)
-        op_w.view(LAYERS, EMBD, QH * HD // 32, 34)[..., 0:2] = torch.tensor([0x1f, 0x22], dtype=torch.uint8,
-                                                                             device=dev)  # f16 scales ~0.004
+        op_w.view(LAYERS, EMBD, in_local // 32, 34)[..., 0:2] = torch.tensor([0x1f, 0x22], dtype=torch.uint8,
+                                                                              device=dev)  # f16 scales ~0.004
         op_out = torch.empty(LAYERS, EMBD, device=dev)
         op_arr = (_lib.OprojLayer * LAYERS)(*[_lib.OprojLayer(op_w[l].data_ptr(), out[l].data_ptr(),
                                                               op_out[l].data_ptr()) for l in range(LAYERS)])
+        if world > 1:
+            from sf37_b200.shard import PeerReduce
+            pr = PeerReduce(world, rank, LAYERS, EMBD)
+
+    def run_oproj(arr, dst):
+        if pr is not None:
+            pr.step(arr, in_local, (in_local // 32) * 34, dst, stream)
+        else:
+            kv.oproj(arr, in_local, EMBD, stream)
 
     def step(i):
         if pg is not None:
@@ -416,7 +428,8 @@ def run_ours(args, rank, world):
         else:
             kv.decode(all_desc[i], qh_l, kvh_l, HD, kv.F16, stream)
         if op_arr is not None:
-            kv.oproj(op_arr, QH * HD, EMBD, stream)
+            run_oproj(op_arr, op_out)
+            return
         if world > 1:
             dist.all_gather_into_tensor(gathered, out)
 
@@ -476,7 +489,8 @@ def run_ours(args, rank, world):
                     for l in range(LAYERS))
     peak, peak_kind = _peaks()
     achieved = att_bytes / (att_ms * 1e-3) / 1e9
-    op_line = oproj_leg(dev, stream, op_arr, op_w, out, op_out, steps, peak) if op_arr is not None else None
+    op_line = oproj_leg(dev, stream, op_arr, op_w, out, op_out, steps, peak) if (op_arr is not None and
+                                                                                  world == 1) else None
     # ncu DRAM bytes of the full 8-KV-head launch; a rank's launch reads
     # kvh_l/8 of the same rows, so the capture scales by that share
     traffic = _traffic_from_profiles("decode_f16_pipe_cfg2.md") if (LAYERS == 48 and wl == "decode") else None
@@ -544,8 +558,8 @@ def run_ours(args, rank, world):
             else:
                 kv.decode(e2e_desc[i % 4][bb], qh_l, kvh_l, HD, kv.F16, stream)
             if op_arrs is not None:
-                kv.oproj(op_arrs[bb], QH * HD, EMBD, stream)
-            if world > 1:
+                run_oproj(op_arrs[bb], B["op_out"])
+            elif world > 1:
                 dist.all_gather_into_tensor(B["gathered"], B["out"])
         ev_done[bb].record(stream)
         out_s.wait_event(ev_done[bb])
@@ -574,12 +588,13 @@ def run_ours(args, rank, world):
         t = torch.tensor([e2e_ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_ms = float(t.item())
-    if pg is not None:
-        if kv.device_error(1):
-            raise RuntimeError("peer gather: a bounded wait timed out")
-        dist.barrier()
-        torch.cuda.synchronize(dev)
-        pg.close()
+    for peer in (pg, pr):
+        if peer is not None:
+            if kv.device_error(1):
+                raise RuntimeError("peer gather/reduce: a bounded wait timed out")
+            dist.barrier()
+            torch.cuda.synchronize(dev)
+            peer.close()
 
     ref_gpu = None
     if world == 1 and wl == "decode" and not args.no_ref_gpu:
@@ -606,7 +621,8 @@ def run_ours(args, rank, world):
                    "qk_prep_fused": bool(args.prep),
                    "oproj_q8_0": bool(args.oproj),
                    "parallelism": f"kv-head shard x{world}" + (
-                       "" if world == 1 else " + NCCL all-gather" if pg is None
+                       "" if world == 1 else " + row-parallel o_proj, partial sums reduced over peer memory"
+                       if pr is not None else " + NCCL all-gather" if pg is None
                        else " + output gather by peer-memory stores from the decode kernels"),
                    "l2": "no flush needed: 6.4 GB of KV per step >> 126 MB L2"},
         "kv_read_GBps": kv_bytes_step / (ms * 1e-3) / 1e9,
