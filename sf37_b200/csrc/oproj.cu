@@ -261,12 +261,21 @@ int oproj_q8_0(const sf37kv_oproj_layer *layers, uint32_t n, uint32_t in_dim, ui
     }
     // Rows per CTA: the split of each layer that fills whole waves best
     // (fewest waves per unit of work), as the decode planning does.
-    int per_sm = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, cfg->kernel, cfg->warps * 32, smem) != cudaSuccess ||
-        per_sm < 1) {
-        (void)cudaGetLastError();
-        per_sm = 1;
+    // (occupancy cached per config and shared-memory size: the query costs
+    // host time on every call otherwise)
+    static size_t occ_smem[3] = {0, 0, 0};
+    static int occ[3] = {0, 0, 0};
+    if (occ_smem[ci] != smem) {
+        int per = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, cfg->kernel, cfg->warps * 32, smem) != cudaSuccess ||
+            per < 1) {
+            (void)cudaGetLastError();
+            per = 1;
+        }
+        occ[ci] = per;
+        occ_smem[ci] = smem;
     }
+    const int per_sm = occ[ci];
     for (uint32_t base = 0; base < n; base += kMaxJobs) {
         const uint32_t m = std::min<uint32_t>(n - base, kMaxJobs);
         const uint64_t slots = (uint64_t)num_sms() * per_sm;
