@@ -178,7 +178,18 @@ struct DecodeParams {
     float qscale;          // log2(e) / sqrt(head_dim)
     GatherDev gat;
     float rope[kMaxRope][128];  // q/k preparation tables (JobDev::rope_idx)
+    uint32_t pdl;               // launched with programmatic stream serialization
 };
+
+// Programmatic dependent launch (sm_90+): a kernel launched with
+// programmatic stream serialization may start while the previous kernel on
+// the stream is still running; griddepcontrol.wait blocks until that kernel
+// has completed and its writes are visible.  Without the attribute both are
+// no-ops.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
 
 __device__ __forceinline__ void gather_store(const DecodeParams &P, const JobDev &J, uint64_t idx, float v) {
     for (uint32_t p = 0; p < P.gat.world; p++)
@@ -674,7 +685,12 @@ __global__ void __launch_bounds__(NW * 32, 1) decode_f16_pipe_kernel(const __gri
     float *Qf = reinterpret_cast<float *>(smem_raw + NW * S * kStage + 2 * 8 * 32 * 16), *Kf = Qf + 16 * 128;
     const bool prep = PREP && J.qn != nullptr;
     const bool appender = J.k_new && split + 1u == J.n_splits;
-    const bool early = prep && !appender;
+    // Under PDL nothing may be read before griddepcontrol.wait: the previous
+    // kernel's writes (to these caches too) are not yet guaranteed visible.
+    griddep_wait();
+    griddep_launch_dependents();
+    // A CTA that does not append starts its first loads before preparing q.
+    const bool early = !appender && prep;
     if (early) {
 #pragma unroll
         for (int s = 0; s < S - 1; s++) issue(s);
@@ -910,7 +926,12 @@ __global__ void __launch_bounds__(NW * 32, 1) decode_f32_pipe_kernel(const __gri
     float *Qf = reinterpret_cast<float *>(smem_raw + NW * S * kStage + 2 * 8 * 32 * 16), *Kf = Qf + 16 * 128;
     const bool prep = PREP && J.qn != nullptr;
     const bool appender = J.k_new && split + 1u == J.n_splits;
-    const bool early = prep && !appender;
+    // Under PDL nothing may be read before griddepcontrol.wait: the previous
+    // kernel's writes (to these caches too) are not yet guaranteed visible.
+    griddep_wait();
+    griddep_launch_dependents();
+    // A CTA that does not append starts its first loads before preparing q.
+    const bool early = !appender && prep;
     if (early) {
 #pragma unroll
         for (int s = 0; s < S - 1; s++) issue(s);
@@ -1337,6 +1358,39 @@ static void rope_table(float *t, const RopeKey &k) {
     }
 }
 
+// SF37KV_PDL=0 turns programmatic dependent launch off (default on).
+static bool pdl_enabled() {
+    static int on = -1;
+    if (on < 0) {
+        const char *e = getenv("SF37KV_PDL");
+        on = (e && !strcmp(e, "0")) ? 0 : 1;
+    }
+    return on != 0;
+}
+
+// Launches a pipelined decode kernel; with P.pdl set, with programmatic
+// stream serialization so that its CTAs start (and prefetch cached rows)
+// while the previous kernel on the stream drains.
+template <typename Kernel>
+static void launch_pipe(Kernel kernel, unsigned grid, unsigned block, size_t smem, cudaStream_t s,
+                        const DecodeParams &P) {
+    if (!P.pdl) {
+        kernel<<<grid, block, smem, s>>>(P);
+        return;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(block);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    (void)cudaLaunchKernelEx(&cfg, kernel, P);
+}
+
 constexpr size_t kPrepSmem = (16 * 128 + 128) * 4;  // prepared q heads + K head (PREP kernels)
 static size_t smem_pipe(int nw, int stages) { return (size_t)nw * stages * 8192 + 2 * 8 * 32 * 16; }
 static size_t smem_pipe32(int nw, int stages) { return (size_t)nw * stages * 16384 + 2 * 8 * 32 * 16; }
@@ -1485,6 +1539,7 @@ int attention_jobs(const AttnJob *jobs, uint32_t n, uint32_t q_heads, uint32_t k
         }
         if (const char *e = getenv("SF37KV_SPLIT_ROWS")) per = strtoull(e, nullptr, 10) ? strtoull(e, nullptr, 10) : per;
         DecodeParams P;
+        P.pdl = 0;
         P.n_jobs = m;
         P.q_heads = q_heads;
         P.kv_heads = kv_heads;
@@ -1556,12 +1611,13 @@ int attention_jobs(const AttnJob *jobs, uint32_t n, uint32_t q_heads, uint32_t k
                                      (int)(smem_pipe(4, 3) + kPrepSmem));
                 prep_attr = true;
             }
-            if (any_prep) decode_f16_pipe_kernel<4, 3, true><<<ctas, 128, smem_pipe(4, 3) + kPrepSmem, stream>>>(P);
+            P.pdl = pdl_enabled() && (any_prep || variant == 1 || variant == 0);
+            if (any_prep) launch_pipe(decode_f16_pipe_kernel<4, 3, true>, ctas, 128, smem_pipe(4, 3) + kPrepSmem, stream, P);
             else switch (variant) {
-                case 1: decode_f16_pipe_kernel<4, 3><<<ctas, 128, smem_pipe(4, 3), stream>>>(P); break;
+                case 1: launch_pipe(decode_f16_pipe_kernel<4, 3>, ctas, 128, smem_pipe(4, 3), stream, P); break;
                 case 2: decode_f16_kernel<kNW, 2><<<ctas, kNW * 32, smem_f16(), stream>>>(P); break;
                 case 3: decode_f16_kernel<kNW, 3><<<ctas, kNW * 32, smem_f16(), stream>>>(P); break;
-                default: decode_f16_pipe_kernel<8, 3><<<ctas, 256, smem_pipe(8, 3), stream>>>(P); break;
+                default: launch_pipe(decode_f16_pipe_kernel<8, 3>, ctas, 256, smem_pipe(8, 3), stream, P); break;
             }
         } else {
             // SF37KV_DECODE_F32=cuda selects the CUDA-core fp32 kernel (comparison runs).
@@ -1578,10 +1634,11 @@ int attention_jobs(const AttnJob *jobs, uint32_t n, uint32_t q_heads, uint32_t k
                                      (int)(smem_pipe32(4, 3) + kPrepSmem));
                 prep_attr = true;
             }
+            P.pdl = pdl_enabled() && (any_prep || !f32_cuda);
             if (any_prep) {
-                decode_f32_pipe_kernel<4, 3, true><<<ctas, 128, smem_pipe32(4, 3) + kPrepSmem, stream>>>(P);
+                launch_pipe(decode_f32_pipe_kernel<4, 3, true>, ctas, 128, smem_pipe32(4, 3) + kPrepSmem, stream, P);
             } else if (!f32_cuda) {
-                decode_f32_pipe_kernel<4, 3><<<ctas, 128, smem_pipe32(4, 3), stream>>>(P);
+                launch_pipe(decode_f32_pipe_kernel<4, 3>, ctas, 128, smem_pipe32(4, 3), stream, P);
             } else {
                 switch (G) {
                     case 1: launch_f32<1, 8>(P, ctas, stream); break;
@@ -1780,6 +1837,7 @@ int attention_jobs_prealloc(const AttnJob *jobs, uint32_t n, uint32_t q_heads, u
     uint64_t per = (total + target - 1) / target;
     if (per < 256) per = 256;
     DecodeParams P;
+    P.pdl = 0;
     for (;;) {
         P.n_jobs = n;
         P.q_heads = q_heads;

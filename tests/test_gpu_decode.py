@@ -142,3 +142,34 @@ def test_gqa_single_token():
     assert kv.gqa_single_token_heads(out, dev(v), dev(g), 64, 8, 128)
     want = v.reshape(8, 1, 128).repeat(8, axis=1).reshape(64, 128) * (1 / (1 + np.exp(-g)))[:, None]
     assert_close(host(out), want, atol=1e-6, rtol=1e-6)
+
+
+@pytest.mark.parametrize("f16", [True, False])
+def test_back_to_back_steps_on_one_cache(f16):
+    # Consecutive decode launches on the same stream, each appending the row
+    # the next one reads (the programmatic-dependent-launch case: a kernel may
+    # start before the previous one finished, and must not read early).
+    cap, pos0, steps = 3000, 2500, 6
+    k = synth.normal(71, (cap, 1024))
+    v = synth.normal(72, (cap, 1024))
+    kn = synth.normal(73, (steps, 1024))
+    vn = synth.normal(74, (steps, 1024))
+    qs = synth.normal(75, (steps, 64, 128))
+    if f16:
+        kb, vb = oracle.f32_to_f16_bits(k), oracle.f32_to_f16_bits(v)
+        kd = torch.from_numpy(kb.view(np.float16)).cuda()
+        vd = torch.from_numpy(vb.view(np.float16)).cuda()
+        ke, ve = kb.copy(), vb.copy()
+    else:
+        kd, vd = dev(k), dev(v)
+        ke, ve = k.copy(), v.copy()
+    outs = [torch.empty(64, 128, device="cuda") for _ in range(steps)]
+    qd, knd, vnd = dev(qs), dev(kn), dev(vn)
+    for s in range(steps):
+        kv.decode([dict(k_cache=kd, v_cache=vd, cap=cap, pos=pos0 + s, q=qd[s], out=outs[s],
+                        k_new=knd[s], v_new=vnd[s])], 64, 8, 128, kv.F16 if f16 else kv.F32)
+    torch.cuda.synchronize()
+    for s in range(steps):
+        oracle.store_kv_rows(ke, ve, kn[s:s + 1], vn[s:s + 1], pos0 + s, 1, cap, 1024)
+        want = oracle.attention_decode_at(qs[s], ke, ve, None, pos0 + s, cap, 64, 8, 128)
+        assert_close(host(outs[s]), want, what=f"step {s}")
