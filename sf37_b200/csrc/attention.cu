@@ -1535,6 +1535,14 @@ int attention_jobs(const AttnJob *jobs, uint32_t n, uint32_t q_heads, uint32_t k
                 for (uint32_t i = 0; i < m; i++) longest = std::max<uint64_t>(longest, jobs[base + i].end - jobs[base + i].start);
                 per = ((longest + ns - 1) / ns + 127) / 128 * 128;
                 if (per < 128) per = 128;
+            } else if (per > 8192) {
+                // More (layer, head) groups than one wave holds, with a few
+                // long jobs among many short ones (config 3: 12 full layers of
+                // 65K rows and 36 sliding layers of 512): one-wave sizing makes
+                // the long jobs' CTAs huge, and their tail cannot overlap the
+                // next launch.  Measured on config 3: 21.6K rows per CTA 1682
+                // tok/s, 8192 rows 2002 tok/s.
+                per = 8192;
             }
         }
         if (const char *e = getenv("SF37KV_SPLIT_ROWS")) per = strtoull(e, nullptr, 10) ? strtoull(e, nullptr, 10) : per;
