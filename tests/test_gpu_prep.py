@@ -21,9 +21,11 @@ def _bf16(seed):
     return (w.view(np.uint32) >> 16).astype(np.uint16)
 
 
-@pytest.mark.parametrize("f16", [True, False])
-@pytest.mark.parametrize("pos", [0, 700, 4999])
-def test_decode_prep_matches_oracle(f16, pos):
+@pytest.mark.parametrize("f16,pos,qh", [(True, 0, 64), (True, 700, 64), (True, 4999, 64), (False, 0, 64),
+                                         (False, 700, 64), (False, 4999, 64), (True, 3000, 96), (False, 600, 96)])
+def test_decode_prep_matches_oracle(f16, pos, qh):
+    # qh 96: the real model's sliding layers (group 12)
+    QH = qh
     layers = 4
     caps = [5000, 512, 512, 512]
     params = [FULL, SLIDING, SLIDING, SLIDING]

@@ -163,3 +163,24 @@ def test_loads_reference_payload_golden():
     for il in range(C.LAYERS):
         assert np.array_equal(rk[il].cpu().numpy(), ok_k[il])
         assert np.array_equal(rv[il].cpu().numpy(), ok_v[il])
+
+
+def test_empty_session_roundtrip():
+    # no tokens: header, row counts (all 0), logits and hidden only
+    ctx = 16
+    caps = [ctx] * C.LAYERS
+    toks, lg, hd, kc, vc = C.state(17, ctx, 0, caps)
+    s, _, _ = _session(ctx, caps, kc, vc, False, toks, lg, hd)
+    snap = s.save_snapshot().numpy().tobytes()
+    assert snap == S.save(0, ctx, toks, lg, hd, kc, vc, caps)
+    with tempfile.TemporaryFile() as f:
+        nb = s.save_payload(f)
+        f.seek(0)
+        pay = f.read()
+        assert pay == S.save(1, ctx, toks, lg, hd, kc, vc, caps) and nb == len(pay)
+        r, _, _ = _session(ctx, caps, kc, vc, False)
+        f.seek(0)
+        r.load_payload(f.fileno(), nb)
+        assert r.n_tokens == 0 and np.array_equal(r.logits, lg)
+    r.load_snapshot(snap)
+    assert r.n_tokens == 0 and np.array_equal(r.hidden, hd)
