@@ -99,6 +99,7 @@ int main(void) {
     L.n_layers = 1;
     L.vocab = 16;
     L.embd = 8;
+    L.full_every = 0; /* the one layer is a sliding ring of 600 slots, not a full layer */
     sf37kv_cache cache = {tk->ptr, tv->ptr, CAP, 1, 512, 0};
     int32_t toks[POS + 1];
     for (int i = 0; i <= POS; i++) toks[i] = i % 16;
