@@ -239,6 +239,13 @@ int oproj_q8_0(const sf37kv_oproj_layer *layers, uint32_t n, uint32_t in_dim, ui
                          (unsigned long long)row_stride, row_bytes);
     if (red && n > (uint32_t)kMaxJobs)
         return set_error(SF37KV_EINVAL, "oproj: at most %d layers per row-parallel call", kMaxJobs);
+    for (uint32_t i = 0; i < n; i++) {  // every argument check before any CUDA call
+        const sf37kv_oproj_layer &L = layers[i];
+        if (!L.weights || !L.x || !L.out)
+            return set_error(SF37KV_EINVAL, "oproj: layer %u has a NULL pointer", i);
+        if (((uintptr_t)L.weights | (uintptr_t)L.x) & 15u)
+            return set_error(SF37KV_EINVAL, "oproj: layer %u weights and x must be 16-byte aligned", i);
+    }
     const OprojConfig *cfg = nullptr;
     size_t smem = 0;
     for (const OprojConfig &c : kConfigs) {
@@ -306,10 +313,6 @@ int oproj_q8_0(const sf37kv_oproj_layer *layers, uint32_t n, uint32_t in_dim, ui
         }
         for (uint32_t i = 0; i < m; i++) {
             const sf37kv_oproj_layer &L = layers[base + i];
-            if (!L.weights || !L.x || !L.out)
-                return set_error(SF37KV_EINVAL, "oproj: layer %u has a NULL pointer", base + i);
-            if (((uintptr_t)L.weights | (uintptr_t)L.x) & 15u)
-                return set_error(SF37KV_EINVAL, "oproj: layer %u weights and x must be 16-byte aligned", base + i);
             P.job[i] = OprojJob{(const uint8_t *)L.weights, L.x, L.out, i * P.ctas_per_job,
                                 red_off ? red_off[base + i] : 0};
         }

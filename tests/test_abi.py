@@ -106,3 +106,29 @@ def test_gather_rejects_bad_descriptors_without_launching():
     # head_dim 64 has no gather kernel
     assert L.sf37kv_decode_gather(lay, 1, 8, 1, 64, 2, ctypes.byref(g), 1, None) == 4
     assert L.sf37kv_gather_wait(None, 1, None) == 1
+
+
+def test_prep_and_oproj_reject_bad_arguments_without_launching():
+    L = _lib.lib()
+    lay = (_lib.DecodeLayer * 1)()
+    lay[0].cache.cap = 16
+    lay[0].cache.k_cache = lay[0].cache.v_cache = lay[0].q = lay[0].out = 256
+    prep = (_lib.QkPrep * 1)()
+    assert L.sf37kv_decode_prep(lay, None, 1, 64, 8, 128, 2, None) == 1  # prep NULL
+    prep[0].q_norm = prep[0].k_norm = 512
+    prep[0].rotary_dim = 63
+    assert L.sf37kv_decode_prep(lay, prep, 1, 64, 8, 128, 2, None) == 1
+    assert "rotary_dim" in _lib.last_error()
+    prep[0].rotary_dim = 64
+    prep[0].q_norm = 0
+    assert L.sf37kv_decode_prep(lay, prep, 1, 64, 8, 128, 2, None) == 1
+    assert L.sf37kv_decode_prep(lay, prep, 1, 64, 8, 64, 2, None) == 4  # head_dim 64
+    # o_proj
+    op = (_lib.OprojLayer * 1)(_lib.OprojLayer(256, 256, 256))
+    assert L.sf37kv_oproj_q8_0(op, 1, 100, 8, None) == 4  # in_dim % 256
+    op[0].x = 260
+    assert L.sf37kv_oproj_q8_0(op, 1, 256, 8, None) == 1  # alignment
+    g = _lib.PeerGather()
+    g.world, g.rank = 0, 0
+    assert L.sf37kv_oproj_q8_0_shard(op, 1, 256, 8, 272, ctypes.byref(g), 1, None) == 1
+    assert L.sf37kv_oproj_reduce(ctypes.byref(g), 1, 8, 1, None, None) == 1
