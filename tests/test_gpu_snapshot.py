@@ -117,3 +117,35 @@ def test_dropin_pack_rows(fmt):
     hv = np.zeros_like(vf)
     oracle.unpack_layer(hbuf, hk, hv, first, rows, cap, 1024, fmt)
     assert np.array_equal(host(dk), hk) and np.array_equal(host(dv), hv)
+
+
+@pytest.mark.parametrize("dtype", [kv.F32, kv.F16])
+def test_pack_i8_special_values(dtype):
+    # all-zero groups, +-inf / NaN (skipped by the max, encoded as 0), huge
+    # and tiny magnitudes, exact .5 ties: bit-exact with the oracle
+    cap, kd = 40, 1024
+    rng = np.random.default_rng(3)
+    k = (rng.standard_normal((cap, kd)) * 3).astype(np.float32)
+    v = (rng.standard_normal((cap, kd)) * 0.01).astype(np.float32)
+    k[0, :64] = 0
+    k[1, 5] = np.inf
+    k[1, 70] = -np.inf
+    k[2, 3] = np.nan
+    k[2, 64:128] = np.nan
+    k[3, :] = 60000.0 * np.sign(rng.standard_normal(kd))
+    k[4, :] = 1e-6
+    v[5, :64] = np.arange(64) * 0.5 - 16  # many exact halves
+    v[6, :] = -0.0
+    if dtype == kv.F16:
+        hk, hv = oracle.f32_to_f16_bits(k), oracle.f32_to_f16_bits(v)
+        kc = torch.from_numpy(hk.view(np.float16)).cuda()
+        vc = torch.from_numpy(hv.view(np.float16)).cuda()
+    else:
+        hk, hv = k, v
+        kc, vc = dev(k), dev(v)
+    L = [dict(k_cache=kc, v_cache=vc, cap=cap, first_pos=0, rows=cap)]
+    arr, total = kv.pack_layers_desc(L, kd, kv.FMT_I8G)
+    buf = torch.empty(total, dtype=torch.uint8, device="cuda")
+    kv.pack(buf, arr, kd, dtype, kv.FMT_I8G)
+    want = oracle.pack_layer(hk, hv, 0, cap, cap, kd, kv.FMT_I8G)
+    assert np.array_equal(host(buf), want)
