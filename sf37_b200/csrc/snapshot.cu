@@ -218,15 +218,29 @@ __global__ void __launch_bounds__(128) pack_kernel(uint8_t *dst, const __grid_co
     advance(P, row0, ref);
     const uint32_t e0 = threadIdx.x * 8u;
     if (blockDim.x * 8u >= P.kv_dim) {
+        // The CTA's rows are consecutive, so the ring slot advances by one
+        // every second row (K, V); one modulo per CTA and per job switch.
         const bool act = e0 < P.kv_dim;
+        uint32_t slot = (P.job[ref.j].first_pos + (ref.local >> 1)) % P.job[ref.j].cap;
+        auto src_of = [&](const RowRef &c, uint32_t s) {
+            const PackJob &J = P.job[c.j];
+            return reinterpret_cast<const T *>((c.local & 1u) ? J.v : J.k) + (uint64_t)s * P.kv_dim;
+        };
         float x[8];
-        if (act) load8<T>(row_src<T>(P, ref) + e0, x);
+        if (act) load8<T>(src_of(ref, slot) + e0, x);
         for (uint32_t row = row0; row < row1; row++) {
             const RowRef cur = ref;
             float xn[8];
             if (row + 1 < row1) {
-                advance(P, row + 1, ref);
-                if (act) load8<T>(row_src<T>(P, ref) + e0, xn);
+                ref.local++;
+                if (ref.local == 2u * P.job[ref.j].rows) {  // next layer section
+                    ref.j++;
+                    ref.local = 0;
+                    slot = P.job[ref.j].first_pos % P.job[ref.j].cap;
+                } else if ((ref.local & 1u) == 0) {
+                    slot = slot + 1u == P.job[ref.j].cap ? 0u : slot + 1u;
+                }
+                if (act) load8<T>(src_of(ref, slot) + e0, xn);
             }
             if (act)
                 encode8<FMT>(P, x, dst + P.job[cur.j].offset + (uint64_t)cur.local * P.row_bytes, e0);
