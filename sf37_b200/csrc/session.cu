@@ -200,6 +200,7 @@ struct FdIo {
     uint64_t *remaining;  // loader: bytes of the record not yet read
     char *err;
     size_t errlen;
+    bool io_failed = false;  // a callback reported a short read / failed write (message in err)
     uint8_t *map = nullptr;  // writer: mapping of [map_base, map_base + map_len)
     int64_t map_base = 0;
     uint64_t map_len = 0;
@@ -296,7 +297,10 @@ int par_io(FdIo &io, void *p, uint64_t n, bool wr) {
 
 int sink_fd(const void *p, uint64_t n, void *ctx) {
     FdIo *S = (FdIo *)ctx;
-    if (par_io(*S, const_cast<void *>(p), n, true)) return fail(S->err, S->errlen, "failed to write session payload");
+    if (par_io(*S, const_cast<void *>(p), n, true)) {
+        S->io_failed = true;
+        return fail(S->err, S->errlen, "failed to write session payload");
+    }
     return 0;
 }
 
@@ -304,7 +308,10 @@ int sink_fd(const void *p, uint64_t n, void *ctx) {
 // record's byte budget is exhausted.
 int source_fd(void *p, uint64_t n, void *ctx) {
     FdIo *S = (FdIo *)ctx;
-    if (n > *S->remaining || par_io(*S, p, n, false)) return fail(S->err, S->errlen, "truncated session payload");
+    if (n > *S->remaining || par_io(*S, p, n, false)) {
+        S->io_failed = true;
+        return fail(S->err, S->errlen, "truncated session payload");
+    }
     *S->remaining -= n;
     return 0;
 }
@@ -417,7 +424,7 @@ extern "C" int sf37kv_session_save_payload(const sf37kv_session *s, int fd, char
     const int rc = pack_stream(sec.data(), L.n_layers, kv_row(L), s->dtype, SF37KV_FMT_I8_GROUPED, L.payload_group,
                                sink_fd, &io);
     fd_done(io);
-    if (rc == SF37KV_EINVAL && err && errlen && err[0]) return 1;  // the sink's message
+    if (rc && io.io_failed) return 1;  // the sink's message
     if (rc) return fail_last(err, errlen, "failed to read CUDA K cache for payload");
     return 0;
 }
@@ -450,7 +457,7 @@ int load_payload_body(sf37kv_session *s, FdIo &src, uint64_t payload_bytes, char
     const auto sec = kv_sections(s, rows.data(), token_count, rb);
     const int rc = unpack_stream(sec.data(), L.n_layers, kv_row(L), s->dtype, SF37KV_FMT_I8_GROUPED,
                                  L.payload_group, source_fd, &src);
-    if (rc == SF37KV_EINVAL && err && errlen && err[0]) return 1;  // the source's message
+    if (rc && src.io_failed) return 1;  // the source's message
     if (rc) return fail_last(err, errlen, "failed to restore CUDA K cache from payload");
     if (remaining != 0) return fail(err, errlen, "session payload has trailing bytes");
     for (uint32_t i = 0; i < token_count; i++) s->tokens[i] = (int32_t)toks[i];
