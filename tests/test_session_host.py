@@ -88,3 +88,56 @@ def test_payload_write_error_reports_reference_message():
     finally:
         signal.signal(signal.SIGPIPE, old)
         os.close(w)
+
+
+@pytest.mark.parametrize("kind", [0, 1])
+def test_random_header_corruptions_agree_with_oracle(kind):
+    # Random single-word corruptions of the reference's golden records
+    # (header, row counts, tokens) and random truncations / extensions: every
+    # one the oracle loader rejects, the library rejects with the same words,
+    # before touching a cache.
+    from oracle import session as S
+    g = np.load(GOLD)
+    buf = g["snapshot" if kind == 0 else "payload"].tobytes()
+    nf = 11 if kind == 0 else 15
+    n_words = nf + C.LAYERS + 2
+    rng = np.random.default_rng(40 + kind)
+    L = _lib.lib()
+    checked = 0
+    for trial in range(300):
+        b = bytearray(buf)
+        op = rng.integers(0, 3)
+        if op == 0:
+            w = int(rng.integers(0, n_words))
+            val = int(rng.choice([0, 1, 2, 3, 4, 511, 512, 513, 2**31, 2**32 - 1, int(rng.integers(0, 2**32))]))
+            b[4 * w:4 * w + 4] = np.array([val], "<u4").tobytes()
+        elif op == 1:
+            b = b[:int(rng.integers(0, len(b)))]
+        else:
+            b = b + bytes(int(rng.integers(1, 64)))
+        b = bytes(b)
+        if not b:
+            continue
+        try:
+            kc = [np.zeros((3, C.KV), np.float32) for _ in range(C.LAYERS)]
+            S.load(kind, b, 3, [3] * C.LAYERS, kc, [k.copy() for k in kc])
+            continue  # accepted by the oracle: restoring needs the GPU
+        except S.LoadError as e:
+            want = str(e)
+        except (ValueError, IndexError):
+            continue
+        s, keep = _session(3)
+        err = ctypes.create_string_buffer(512)
+        if kind == 0:
+            arr = np.frombuffer(b, np.uint8)
+            rc = L.sf37kv_session_load_snapshot(ctypes.byref(s), arr.ctypes.data, arr.size, err, 512)
+        else:
+            with tempfile.TemporaryFile() as f:
+                f.write(b)
+                f.flush()
+                f.seek(0)
+                rc = L.sf37kv_session_load_payload(ctypes.byref(s), f.fileno(), len(b), err, 512)
+        assert rc == 1
+        assert err.value.decode() == want, (trial, op, want)
+        checked += 1
+    assert checked > 100
