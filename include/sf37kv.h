@@ -215,9 +215,9 @@ int sf37kv_unpack_from_host(const void *host_src, const sf37kv_pack_layer *layer
                             uint32_t group);
 
 /* Synchronizes the device and returns the library's device error flag: 1
- * when a kernel's bounded wait gave up (the kernel then stopped early and
- * its output is invalid), 0 otherwise, -1 if it cannot be read.  clear != 0
- * resets the flag. */
+ * when a prefill kernel's bounded wait gave up, 2 when a multi-GPU gather or
+ * reduce wait did (the kernel then stopped early and its output is
+ * invalid), 0 otherwise, -1 if it cannot be read.  clear != 0 resets it. */
 int sf37kv_device_error(int clear);
 
 /* ---- multi-GPU output gather over peer memory (KV-head sharding) ----
