@@ -272,8 +272,8 @@ __device__ __forceinline__ uint32_t ring_slot(uint32_t sb, uint32_t x, uint32_t 
 // output (single split) or to scratch followed by the last-CTA reduction.
 template <int NT>
 __device__ void finish_cta(const DecodeParams &P, const JobDev &J, uint32_t j, uint32_t kvh,
-                           uint32_t split, uint32_t cta, uint32_t n_streams,
-                           uint32_t heads_per_part, float *Os, float *Ms, float *Ls) {
+                           uint32_t split, uint32_t cta, uint32_t n_streams, float *Os, float *Ms,
+                           float *Ls) {
     const uint32_t G = P.group;
     const uint32_t tid = threadIdx.x;
     __syncthreads();
@@ -306,7 +306,6 @@ __device__ void finish_cta(const DecodeParams &P, const JobDev &J, uint32_t j, u
             }
         }
     }
-    (void)heads_per_part;
     if (single) {
         gather_group_done(P);
         return;
@@ -381,13 +380,11 @@ __device__ void finish_cta(const DecodeParams &P, const JobDev &J, uint32_t j, u
         const uint32_t qh = kvh * G + h;
         const float L = Lh[h];
         const float g = J.gate ? sigmoid_dev(J.gate[qh]) : 1.0f;
-        const float f = L > 0.f ? g / L : 0.f;
         float4 r;
         r.x = L > 0.f ? acc.x / L * g : 0.f;
         r.y = L > 0.f ? acc.y / L * g : 0.f;
         r.z = L > 0.f ? acc.z / L * g : 0.f;
         r.w = L > 0.f ? acc.w / L * g : 0.f;
-        (void)f;
         *reinterpret_cast<float4 *>(J.out + (uint64_t)qh * 128u + d4) = r;
         if (P.gat.world) gather_store4(P, J, (uint64_t)qh * 128u + d4, r);
     }
@@ -593,7 +590,7 @@ __global__ void __launch_bounds__(NW * 32, MINB) decode_f16_kernel(const __grid_
             Ls[stream * 16u + hrow] = l_run;
         }
     }
-    finish_cta<NW * 32>(P, J, j, kvh, split, cta, n_streams, 8, Os, Ms, Ls);
+    finish_cta<NW * 32>(P, J, j, kvh, split, cta, n_streams, Os, Ms, Ls);
 }
 
 // ------------------------------------------------------------ f16 kernel, cp.async pipeline
@@ -834,7 +831,7 @@ __global__ void __launch_bounds__(NW * 32, 1) decode_f16_pipe_kernel(const __gri
             Ls[stream * 16u + hrow] = l_run;
         }
     }
-    finish_cta<NW * 32>(P, J, j, kvh, split, cta, n_streams, 8, Os, Ms, Ls);
+    finish_cta<NW * 32>(P, J, j, kvh, split, cta, n_streams, Os, Ms, Ls);
 }
 
 // ------------------------------------------------------------ f32 kernel, tensor cores
@@ -1067,7 +1064,7 @@ __global__ void __launch_bounds__(NW * 32, 1) decode_f32_pipe_kernel(const __gri
             Ls[stream * 16u + hrow] = l_run;
         }
     }
-    finish_cta<NW * 32>(P, J, j, kvh, split, cta, n_streams, 8, Os, Ms, Ls);
+    finish_cta<NW * 32>(P, J, j, kvh, split, cta, n_streams, Os, Ms, Ls);
 }
 
 // ------------------------------------------------------------ f32 kernel
@@ -1237,7 +1234,7 @@ __global__ void __launch_bounds__(NW * 32) decode_f32_kernel(const __grid_consta
             Ls[stream * 16u + hrow] = l[h];
         }
     }
-    finish_cta<NW * 32>(P, J, j, kvh, split, cta, n_streams, GP, Os, Ms, Ls);
+    finish_cta<NW * 32>(P, J, j, kvh, split, cta, n_streams, Os, Ms, Ls);
 }
 
 // ------------------------------------------------------------ generic kernel
