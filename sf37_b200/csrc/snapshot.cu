@@ -261,6 +261,105 @@ __global__ void __launch_bounds__(128) pack_kernel(uint8_t *dst, const __grid_co
     }
 }
 
+// Payload rows of the SF37 shape (kv_dim 1024): a thread encodes 16
+// elements, so the per-row work (group max, the scale and its IEEE
+// reciprocal, addresses) is spread over twice the bytes of pack_kernel.
+// A CTA pass handles one position: threads 0-63 its K row, 64-127 its V row
+// (a CTA's first row and every section start are even, so the two rows of a
+// pass are always the K / V pair of one position).  Same bytes as encode8.
+template <typename T>
+__device__ __forceinline__ void load16(const T *p, float (&x)[16]) {
+    float a[8], b[8];
+    load8<T>(p, a);
+    load8<T>(p + 8, b);
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        x[i] = a[i];
+        x[8 + i] = b[i];
+    }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(128) pack_i8x16_kernel(uint8_t *dst, const __grid_constant__ PackParams P) {
+    const uint32_t row0 = blockIdx.x * kRowsPerCta;
+    const uint32_t row1 = min(row0 + kRowsPerCta, P.total_rows);
+    const uint32_t half = threadIdx.x >> 6, t = threadIdx.x & 63u, e0 = t * 16u;
+    const uint32_t tpg = P.group >> 4;  // threads per group
+    RowRef ref{0, 0};
+    advance(P, row0, ref);
+    uint32_t slot = (P.job[ref.j].first_pos + (ref.local >> 1)) % P.job[ref.j].cap;
+    auto src_of = [&](uint32_t j, uint32_t s) {
+        const PackJob &J = P.job[j];
+        return reinterpret_cast<const T *>(half ? J.v : J.k) + (uint64_t)s * 1024u + e0;
+    };
+    float x[16];
+    const bool act0 = row0 + half < row1;
+    if (act0) load16<T>(src_of(ref.j, slot), x);
+    for (uint32_t row = row0; row < row1; row += 2) {
+        const uint32_t cj = ref.j, clocal = ref.local;
+        const bool act = row + half < row1;
+        float xn[16];
+        if (row + 2 < row1) {
+            ref.local += 2;
+            if (ref.local == 2u * P.job[ref.j].rows) {
+                ref.j++;
+                ref.local = 0;
+                slot = P.job[ref.j].first_pos % P.job[ref.j].cap;
+            } else {
+                slot = slot + 1u == P.job[ref.j].cap ? 0u : slot + 1u;
+            }
+            if (row + 2 + half < row1) load16<T>(src_of(ref.j, slot), xn);
+        }
+        if (act) {
+            uint8_t *out = dst + P.job[cj].offset + (uint64_t)(clocal + half) * P.row_bytes;
+            float m = 0.f;
+#pragma unroll
+            for (int i = 0; i < 16; i++) {
+                const float av = fabsf(x[i]);
+                m = fmaxf(m, av < INFINITY ? av : 0.f);
+            }
+            // a half's 64 threads are two whole warps, active together
+            for (uint32_t s = 1; s < tpg; s <<= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, s));
+            float scale, inv;
+            if (m > 0.f) {
+                if (P.variant == 1) {
+                    scale = __fmul_rn(m, 1.0f / 127.0f);
+                    inv = __frcp_rn(scale);
+                } else {
+                    scale = __fdiv_rn(m, 127.0f);
+                    inv = 0.f;
+                }
+            } else {
+                scale = 1.0f;
+                inv = 1.0f;
+            }
+            if ((t & (tpg - 1u)) == 0) *reinterpret_cast<float *>(out + (e0 / P.group) * 4u) = scale;
+            // as encode8: the reference's [-127, 127] clamp never fires
+            uint32_t q[16];
+#pragma unroll
+            for (int i = 0; i < 16; i++) {
+                const float v = fabsf(x[i]) < INFINITY ? x[i] : 0.f;
+                const float y = (P.variant == 1 || m <= 0.f) ? __fmul_rn(v, inv) : __fdiv_rn(v, scale);
+                q[i] = (uint32_t)__float2int_rn(y);
+            }
+            uint32_t w[4];
+#pragma unroll
+            for (int k = 0; k < 4; k++)
+                w[k] = __byte_perm(__byte_perm(q[4 * k], q[4 * k + 1], 0x0040u),
+                                   __byte_perm(q[4 * k + 2], q[4 * k + 3], 0x0040u), 0x5410u);
+            uint8_t *qo = out + (uint64_t)P.groups * 4u + e0;
+            if (((uintptr_t)qo & 15u) == 0) {
+                *reinterpret_cast<uint4 *>(qo) = make_uint4(w[0], w[1], w[2], w[3]);
+            } else {
+                store_bytes8(qo, w[0], w[1]);
+                store_bytes8(qo + 8, w[2], w[3]);
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < 16; i++) x[i] = xn[i];
+    }
+}
+
 template <typename T, int FMT>
 __global__ void __launch_bounds__(128) unpack_kernel(const uint8_t *src, const __grid_constant__ PackParams P) {
     const uint32_t row0 = blockIdx.x * kRowsPerCta;
@@ -340,7 +439,15 @@ static int launch_layers(void *buf, const sf37kv_pack_layer *layers, uint32_t n,
         if (dir == 0) pack_kernel<T, F><<<grid, threads, 0, stream>>>(b, P);          \
         else unpack_kernel<T, F><<<grid, threads, 0, stream>>>(b, P);                 \
     } while (0)
-        if (dtype == SF37KV_F32) {
+        // the SF37 shape (1024 elements per row, groups of 16..256) packs
+        // payload rows with 16 elements per thread
+        bool x16 = dir == 0 && fmt == SF37KV_FMT_I8_GROUPED && kv_dim == 1024u && group >= 16u &&
+                   ((uintptr_t)b & 3u) == 0 && P.row_bytes % 4u == 0;
+        for (uint32_t i = 0; i < P.n_jobs; i++) x16 = x16 && P.job[i].offset % 4u == 0;
+        if (x16) {
+            if (dtype == SF37KV_F32) pack_i8x16_kernel<float><<<grid, 128, 0, stream>>>(b, P);
+            else pack_i8x16_kernel<__half><<<grid, 128, 0, stream>>>(b, P);
+        } else if (dtype == SF37KV_F32) {
             if (fmt == SF37KV_FMT_RAW_F32) SF37_PACK_LAUNCH(float, SF37KV_FMT_RAW_F32);
             else SF37_PACK_LAUNCH(float, SF37KV_FMT_I8_GROUPED);
         } else {
