@@ -214,6 +214,21 @@ int sf37kv_unpack_from_host(const void *host_src, const sf37kv_pack_layer *layer
                             uint32_t n_layers, uint32_t kv_dim, int dtype, int fmt,
                             uint32_t group);
 
+/* One GPU's KV-head slice of a multi-GPU record (sharded by KV head): the
+ * caches hold elements [col0, col0 + kv_dim) of each full_kv_dim-element
+ * row, and only those bytes of the full-width record rows are written
+ * (read): raw, 4 kv_dim bytes at 4 col0 of each row; payload, the slice's
+ * group scales and int8 codes in place (col0 and kv_dim multiples of
+ * group; 64-element groups align with 128-element heads).  layers[i].offset
+ * is the section's offset in the FULL layout.  Several GPUs can fill one
+ * host buffer this way, each touching only its own columns.  Synchronous. */
+int sf37kv_pack_slice_to_host(void *host_dst, const sf37kv_pack_layer *layers, uint32_t n_layers,
+                              uint32_t kv_dim, uint32_t full_kv_dim, uint32_t col0, int dtype,
+                              int fmt, uint32_t group, int variant);
+int sf37kv_unpack_slice_from_host(const void *host_src, const sf37kv_pack_layer *layers,
+                                  uint32_t n_layers, uint32_t kv_dim, uint32_t full_kv_dim,
+                                  uint32_t col0, int dtype, int fmt, uint32_t group);
+
 /* Synchronizes the device and returns the library's device error flag: 1
  * when a prefill kernel's bounded wait gave up, 2 when a multi-GPU gather or
  * reduce wait did (the kernel then stopped early and its output is

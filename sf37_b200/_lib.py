@@ -123,6 +123,10 @@ SIGNATURES = {
     "sf37kv_ipc_close": (None, [c_vp]),
     "sf37kv_decode_prep": (c_int, [ctypes.POINTER(DecodeLayer), ctypes.POINTER(QkPrep), c_u32, c_u32, c_u32,
                                    c_u32, c_int, c_vp]),
+    "sf37kv_pack_slice_to_host": (c_int, [c_vp, ctypes.POINTER(PackLayer), c_u32, c_u32, c_u32, c_u32, c_int,
+                                          c_int, c_u32, c_int]),
+    "sf37kv_unpack_slice_from_host": (c_int, [c_vp, ctypes.POINTER(PackLayer), c_u32, c_u32, c_u32, c_u32, c_int,
+                                              c_int, c_u32]),
     "sf37kv_oproj_q8_0": (c_int, [ctypes.POINTER(OprojLayer), c_u32, c_u32, c_u32, c_vp]),
     "sf37kv_oproj_q8_0_shard": (c_int, [ctypes.POINTER(OprojLayer), c_u32, c_u32, c_u32, c_u64,
                                         ctypes.POINTER(PeerGather), c_u32, c_vp]),

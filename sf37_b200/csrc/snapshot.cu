@@ -14,6 +14,8 @@
 // These kernels are HBM- (device buffer) or link- (mapped host buffer) bound.
 #include <cstdio>
 #include <cstring>
+#include <thread>
+#include <vector>
 
 #include "kv_internal.cuh"
 #include "../../include/sf37_cuda_kv.h"
@@ -569,6 +571,8 @@ static int host_buffers_init() {
 namespace {
 struct Chunk {
     sf37kv_pack_layer piece[kMaxJobs];
+    uint32_t layer[kMaxJobs];   // index of the piece's layer section
+    uint32_t row0[kMaxJobs];    // its first row within that section
     uint32_t n = 0;
     uint64_t bytes = 0;
 };
@@ -595,6 +599,8 @@ struct Chunker {
             p.first_pos = L.first_pos + (uint32_t)r0;
             p.rows = (uint32_t)take;
             p.offset = c->bytes;
+            c->layer[c->n] = li;
+            c->row0[c->n] = (uint32_t)r0;
             c->piece[c->n++] = p;
             c->bytes += 2ull * take * rb;
             room -= take;
@@ -671,6 +677,123 @@ int unpack_stream(const sf37kv_pack_layer *layers, uint32_t n, uint32_t kv_dim, 
     return rc ? rc : rs;
 }
 
+// ---------------------------------------------------------------- KV-head slices
+// A GPU that holds KV heads [h0, h0 + n) of every layer writes (reads) only
+// its columns of the full-width record rows: elements [col0, col0 + kv_dim)
+// of each full_kv_dim-element row.  The device packs the slice compactly
+// (kv_dim-wide rows) into the staging buffer; the host then scatters each
+// row's pieces into the full layout (raw: one run of 4 kv_dim bytes; payload:
+// the slice's group scales and its codes), so no byte of another slice is
+// touched and several GPUs can fill one record buffer.
+namespace {
+struct SliceGeom {
+    uint32_t kv_dim, full, col0, group;
+    int fmt;
+    uint64_t rb, rbf;  // compact and full row bytes
+    // (offset, length) of the slice's pieces within a compact / full row
+    uint32_t n_pieces() const { return fmt == SF37KV_FMT_RAW_F32 ? 1u : 2u; }
+    void piece(uint32_t k, uint64_t &src, uint64_t &dst, uint64_t &len) const {
+        if (fmt == SF37KV_FMT_RAW_F32) {
+            src = 0;
+            dst = (uint64_t)col0 * 4u;
+            len = (uint64_t)kv_dim * 4u;
+        } else if (k == 0) {  // group scales
+            src = 0;
+            dst = (uint64_t)(col0 / group) * 4u;
+            len = (uint64_t)(kv_dim / group) * 4u;
+        } else {  // int8 codes
+            src = (uint64_t)(kv_dim / group) * 4u;
+            dst = (uint64_t)(full / group) * 4u + col0;
+            len = kv_dim;
+        }
+    }
+};
+
+// Copies the pieces of every row of chunk c between the compact staging
+// image `compact` and the full-layout host buffer, with a few threads.
+void scatter_gather(const Chunk &c, const sf37kv_pack_layer *layers, const SliceGeom &G, uint8_t *compact,
+                    uint8_t *host, bool to_host) {
+    uint64_t total_rows = 0;
+    for (uint32_t i = 0; i < c.n; i++) total_rows += 2ull * c.piece[i].rows;
+    auto work = [&](uint64_t lo, uint64_t hi) {
+        uint64_t base = 0;
+        for (uint32_t i = 0; i < c.n && base < hi; i++) {
+            const uint64_t nr = 2ull * c.piece[i].rows;
+            const uint64_t a = lo > base ? lo - base : 0, b = hi - base < nr ? hi - base : nr;
+            for (uint64_t r = a; r < b; r++) {
+                uint8_t *cr = compact + c.piece[i].offset + r * G.rb;
+                uint8_t *hr = host + layers[c.layer[i]].offset + (2ull * c.row0[i] + r) * G.rbf;
+                for (uint32_t k = 0; k < G.n_pieces(); k++) {
+                    uint64_t so, dof, len;
+                    G.piece(k, so, dof, len);
+                    if (to_host) memcpy(hr + dof, cr + so, len);
+                    else memcpy(cr + so, hr + dof, len);
+                }
+            }
+            base += nr;
+        }
+    };
+    unsigned nt = std::thread::hardware_concurrency();
+    nt = nt < 1 ? 1 : nt > 8 ? 8 : nt;
+    if (total_rows < 4096) nt = 1;
+    std::vector<std::thread> th;
+    for (unsigned t = 1; t < nt; t++)
+        th.emplace_back(work, total_rows * t / nt, total_rows * (t + 1) / nt);
+    work(0, total_rows / nt);
+    for (auto &x : th) x.join();
+}
+}  // namespace
+
+static int slice_pipeline(void *host, const sf37kv_pack_layer *layers, uint32_t n, uint32_t kv_dim,
+                          uint32_t full_kv_dim, uint32_t col0, int dtype, int fmt, uint32_t group, int variant,
+                          int dir) {
+    if (int rc = validate(kv_dim, dtype, fmt, group)) return rc;
+    if (int rc = validate(full_kv_dim, dtype, fmt, group)) return rc;
+    if (!host && n) return set_error(SF37KV_EINVAL, "pack slice: host buffer is NULL");
+    if (col0 % 8u || (uint64_t)col0 + kv_dim > full_kv_dim ||
+        (fmt == SF37KV_FMT_I8_GROUPED && col0 % group))
+        return set_error(SF37KV_EINVAL, "pack slice: columns [%u, %u) do not fit %u (payload: group-aligned)", col0,
+                         col0 + kv_dim, full_kv_dim);
+    if (int rc = host_buffers_init()) return rc;
+    SliceGeom G{kv_dim, full_kv_dim, col0, group, fmt, row_bytes_of(kv_dim, fmt, group),
+                row_bytes_of(full_kv_dim, fmt, group)};
+    Chunker ck{layers, n, 0, 0, G.rb, kStageBytes / (2 * G.rb)};
+    cudaEventRecord(g_ev_start, current_stream());
+    cudaStreamWaitEvent(g_work_stream, g_ev_start, 0);
+    uint8_t *h = (uint8_t *)host;
+    Chunk c[2];
+    int b = 0, rc = SF37KV_OK;
+    bool have_prev = false, used[2] = {false, false};
+    while (rc == SF37KV_OK && ck.next(&c[b])) {
+        if (dir == 0) {
+            rc = launch_layers(g_stage[b], c[b].piece, c[b].n, kv_dim, dtype, fmt, group, variant, 0, g_work_stream);
+            if (!rc) rc = check_cuda(cudaMemcpyAsync(g_hbuf[b], g_stage[b], c[b].bytes, cudaMemcpyDeviceToHost,
+                                                     g_work_stream), "slice D2H");
+            if (!rc) rc = check_cuda(cudaEventRecord(g_ev_host[b], g_work_stream), "event");
+            if (!rc && have_prev) {  // scatter the previous chunk while this one packs
+                rc = check_cuda(cudaEventSynchronize(g_ev_host[b ^ 1]), "slice sync");
+                if (!rc) scatter_gather(c[b ^ 1], layers, G, (uint8_t *)g_hbuf[b ^ 1], h, true);
+            }
+        } else {
+            if (used[b]) rc = check_cuda(cudaEventSynchronize(g_ev_host[b]), "slice sync");
+            if (!rc) scatter_gather(c[b], layers, G, (uint8_t *)g_hbuf[b], h, false);
+            if (!rc) rc = check_cuda(cudaMemcpyAsync(g_stage[b], g_hbuf[b], c[b].bytes, cudaMemcpyHostToDevice,
+                                                     g_work_stream), "slice H2D");
+            if (!rc) rc = check_cuda(cudaEventRecord(g_ev_host[b], g_work_stream), "event");
+            if (!rc) rc = launch_layers(g_stage[b], c[b].piece, c[b].n, kv_dim, dtype, fmt, group, 1, 1, g_work_stream);
+            used[b] = true;
+        }
+        have_prev = true;
+        b ^= 1;
+    }
+    if (!rc && dir == 0 && have_prev) {
+        rc = check_cuda(cudaEventSynchronize(g_ev_host[b ^ 1]), "slice sync");
+        if (!rc) scatter_gather(c[b ^ 1], layers, G, (uint8_t *)g_hbuf[b ^ 1], h, true);
+    }
+    const int rs = check_cuda(cudaStreamSynchronize(g_work_stream), "slice sync");
+    return rc ? rc : rs;
+}
+
 void staging_release() {
     for (int i = 0; i < 2; i++) {
         if (g_stage[i]) {
@@ -709,6 +832,19 @@ extern "C" int sf37kv_unpack(const void *src, const sf37kv_pack_layer *layers, u
 extern "C" int sf37kv_pack_to_host(void *host_dst, const sf37kv_pack_layer *layers, uint32_t n_layers,
                                    uint32_t kv_dim, int dtype, int fmt, uint32_t group, int variant) {
     return host_pipeline(host_dst, layers, n_layers, kv_dim, dtype, fmt, group, variant, 0);
+}
+
+extern "C" int sf37kv_pack_slice_to_host(void *host_dst, const sf37kv_pack_layer *layers, uint32_t n_layers,
+                                         uint32_t kv_dim, uint32_t full_kv_dim, uint32_t col0, int dtype, int fmt,
+                                         uint32_t group, int variant) {
+    return slice_pipeline(host_dst, layers, n_layers, kv_dim, full_kv_dim, col0, dtype, fmt, group, variant, 0);
+}
+
+extern "C" int sf37kv_unpack_slice_from_host(const void *host_src, const sf37kv_pack_layer *layers,
+                                             uint32_t n_layers, uint32_t kv_dim, uint32_t full_kv_dim, uint32_t col0,
+                                             int dtype, int fmt, uint32_t group) {
+    return slice_pipeline(const_cast<void *>(host_src), layers, n_layers, kv_dim, full_kv_dim, col0, dtype, fmt,
+                          group, 1, 1);
 }
 
 extern "C" int sf37kv_unpack_from_host(const void *host_src, const sf37kv_pack_layer *layers,

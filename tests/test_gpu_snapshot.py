@@ -149,3 +149,48 @@ def test_pack_i8_special_values(dtype):
     kv.pack(buf, arr, kd, dtype, kv.FMT_I8G)
     want = oracle.pack_layer(hk, hv, 0, cap, cap, kd, kv.FMT_I8G)
     assert np.array_equal(host(buf), want)
+
+
+@pytest.mark.parametrize("dtype", [kv.F16, kv.F32])
+@pytest.mark.parametrize("fmt", [kv.FMT_RAW, kv.FMT_I8G])
+def test_kv_head_slices_fill_one_record(dtype, fmt):
+    # N GPUs' KV-head slices written into one full-layout record equal the
+    # record packed from the full caches; restoring each slice from the
+    # record equals restoring the full caches and taking its columns.
+    from sf37_b200 import _lib
+    Ls = _layers(dtype, [(300, 1000, 300), (64, 0, 40), (90, 17, 90)])
+    arr, total = kv.pack_layers_desc(Ls, 1024, fmt)
+    whole = np.empty(total, np.uint8)
+    kv.pack_to_host(whole.ctypes.data, arr, 1024, dtype, fmt)
+    for n in (2, 4, 8):
+        kd = 1024 // n
+        rec = np.full(total, 0xAB, np.uint8)
+        for r in range(n):
+            sl = [dict(k_cache=L["k_cache"][:, r * kd:(r + 1) * kd].contiguous(),
+                       v_cache=L["v_cache"][:, r * kd:(r + 1) * kd].contiguous()) for L in Ls]
+            sarr = (_lib.PackLayer * len(Ls))()
+            for i, L in enumerate(Ls):
+                sarr[i] = _lib.PackLayer(kv.cache_desc(sl[i]["k_cache"], sl[i]["v_cache"], L["cap"]), L["first_pos"],
+                                         L["rows"], arr[i].offset)
+            assert _lib.lib().sf37kv_pack_slice_to_host(rec.ctypes.data, sarr, len(Ls), kd, 1024, r * kd, dtype,
+                                                        fmt, 64, 1) == 0, _lib.last_error()
+            if r == n - 1:
+                assert np.array_equal(rec, whole), n
+            # restore this slice from the full record into zeroed slice caches
+            for s in sl:
+                s["k_cache"].zero_()
+                s["v_cache"].zero_()
+            assert _lib.lib().sf37kv_unpack_slice_from_host(whole.ctypes.data, sarr, len(Ls), kd, 1024, r * kd,
+                                                            dtype, fmt, 64) == 0, _lib.last_error()
+            torch.cuda.synchronize()
+            for i, L in enumerate(Ls):
+                full_k = torch.zeros_like(L["k_cache"])
+                full_v = torch.zeros_like(L["v_cache"])
+                one = [dict(k_cache=full_k, v_cache=full_v, cap=L["cap"], first_pos=L["first_pos"], rows=L["rows"])]
+                oarr, _ = kv.pack_layers_desc(one, 1024, fmt)
+                sec = 2 * L["rows"] * kv.row_bytes(1024, fmt)
+                part = np.ascontiguousarray(whole[arr[i].offset:arr[i].offset + sec])
+                kv.unpack_from_host(part.ctypes.data, oarr, 1024, dtype, fmt)
+                torch.cuda.synchronize()
+                assert torch.equal(sl[i]["k_cache"], full_k[:, r * kd:(r + 1) * kd])
+                assert torch.equal(sl[i]["v_cache"], full_v[:, r * kd:(r + 1) * kd])
