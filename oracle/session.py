@@ -225,3 +225,14 @@ def ref_session_load(kind, buf, ctx):
     if rc != 0:
         raise LoadError(err.value.decode())
     return (toks[:ntok.value].copy(), lg, hd, [ks[i][:nr[i]] for i in range(n)], [vs[i][:nr[i]] for i in range(n)])
+
+
+def slice_columns(kind, kv=1024, group=64, col0=0, width=1024):
+    """Byte ranges of a KV-head slice (elements [col0, col0 + width)) within
+    one full-width record row: [(start, length), ...].  Raw rows are f32
+    elements; payload rows are the group scales then the int8 codes
+    (payload_encode_kv_row_i8_grouped, sf37.c:6633-6659)."""
+    if kind == 0:
+        return [(4 * col0, 4 * width)]
+    groups = kv // group
+    return [(4 * (col0 // group), 4 * (width // group)), (4 * groups + col0, width)]

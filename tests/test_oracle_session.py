@@ -131,3 +131,29 @@ def test_oracle_ring_session_matches_live_reference(kind):
         for il in (0, 1, 44):
             assert np.array_equal(kk[il], C.live_rows_in_order(k2[il], n, rows[il], caps[il]))
             assert np.array_equal(vv[il], C.live_rows_in_order(v2[il], n, rows[il], caps[il]))
+
+
+@pytest.mark.parametrize("kind", [0, 1])
+def test_head_slices_tile_the_record_rows(kind):
+    # The N slices' byte ranges of a row are disjoint and cover it, and the
+    # bytes a slice's own (narrower) row encodes are the record row's bytes
+    # at those ranges: packing per KV-head slice needs no exchange.
+    rng = np.random.default_rng(4)
+    k = rng.standard_normal((6, 1024)).astype(np.float32)
+    v = rng.standard_normal((6, 1024)).astype(np.float32)
+    full = oracle.pack_layer(k, v, 0, 6, 6, 1024, fmt=kind).reshape(12, -1)
+    rb = full.shape[1]
+    for n in (1, 2, 4, 8):
+        w = 1024 // n
+        cover = np.zeros(rb, np.int32)
+        for r in range(n):
+            rngs = S.slice_columns(kind, col0=r * w, width=w)
+            part = oracle.pack_layer(np.ascontiguousarray(k[:, r * w:(r + 1) * w]),
+                                     np.ascontiguousarray(v[:, r * w:(r + 1) * w]), 0, 6, 6, w, fmt=kind).reshape(12, -1)
+            pos = 0
+            for start, length in rngs:
+                cover[start:start + length] += 1
+                assert np.array_equal(full[:, start:start + length], part[:, pos:pos + length])
+                pos += length
+            assert pos == part.shape[1]
+        assert np.all(cover == 1)
