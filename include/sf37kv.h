@@ -91,10 +91,13 @@ int sf37kv_decode(const sf37kv_decode_layer *layers, uint32_t n_layers,
  * first-use allocation): the split-K partials and counters live in a fixed
  * device array of SF37KV_NOALLOC_SCRATCH_BYTES compiled into the library,
  * which every GPU that loads the library holds until exit.  Same arguments
- * and results as sf37kv_decode(), with these limits: head_dim 128,
- * q_heads/kv_heads <= 16 (f32 caches: 1, 2, 4, 8, 12 or 16), at most 64
- * layers per call, layers x kv_heads <= 4096; other sizes are rejected with
- * SF37KV_EINVAL / SF37KV_EUNSUPPORTED and nothing is launched.  The first
+ * as sf37kv_decode() and the same kernels (the appended row is stored by the
+ * attention kernel); the split plan may be coarser, so outputs agree with
+ * sf37kv_decode() within the attention tolerance, not bit for bit, while the
+ * appended cache rows are identical.  Limits: head_dim 128,
+ * q_heads/kv_heads <= 16, at most 64 layers per call, layers x kv_heads <=
+ * 4096; other sizes are rejected with SF37KV_EINVAL / SF37KV_EUNSUPPORTED
+ * before anything is launched (the caches are left untouched).  The first
  * call on a device looks up the array's address (make it before any stream
  * capture).  All calls share the array: calls that overlap on the GPU race,
  * so serialize them. */

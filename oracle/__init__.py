@@ -21,7 +21,9 @@ import subprocess
 import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-REF_DIR_DEFAULT = "/root/reference"
+# The reference source tree: $SF37_REF_DIR, else a "reference" directory next
+# to this repository's root.
+REF_DIR_DEFAULT = os.path.normpath(os.path.join(HERE, "..", "..", "reference"))
 
 _f32p = ctypes.POINTER(ctypes.c_float)
 _u8p = ctypes.POINTER(ctypes.c_uint8)

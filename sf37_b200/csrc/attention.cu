@@ -392,7 +392,7 @@ __device__ void finish_cta(const DecodeParams &P, const JobDev &J, uint32_t j, u
     gather_group_done(P);
 }
 
-// ------------------------------------------------------------ f16 kernel
+// ------------------------------------------------------------ f16 kernel: register fragments
 // NW warps; warp w handles M-tile (w % n_mt) (query heads 8*mt .. 8*mt+7 of
 // the group) and row stream (w / n_mt).  Thread (g = lane/4, t = lane%4).
 //
@@ -407,194 +407,8 @@ __device__ void finish_cta(const DecodeParams &P, const JobDev &J, uint32_t j, u
 //    thread (g,t) loads rows b+2t, b+2t+1, b+2t+8, b+2t+9, chunks g and g+8,
 //    and interleaves the two rows of each B register with one PRMT.
 //    Output dim of (n-tile jt, column c) = jt<8 ? 8c+jt : 64+8c+jt-8.
-template <int NW, int MINB>
-__global__ void __launch_bounds__(NW * 32, MINB) decode_f16_kernel(const __grid_constant__ DecodeParams P) {
-    extern __shared__ __align__(16) float smem[];
-    float *Os = smem;                                  // [NW streams][16 heads][128]
-    float *Ms = Os + NW * 16 * 128;                    // 16*NW
-    float *Ls = Ms + 16 * NW;                          // 16*NW
-    uint4 *Qs = reinterpret_cast<uint4 *>(Ls + 16 * NW);  // [n_mt][8 kk][32 lanes]
-
-    const uint32_t cta = blockIdx.x;
-    const uint32_t j = locate_job(P, cta);
-    const JobDev &J = P.job[j];
-    const uint32_t local = cta - J.cta_begin;
-    const uint32_t kvh = local / J.n_splits, split = local - kvh * J.n_splits;
-    const uint32_t G = P.group;
-    const uint32_t n_mt = (G + 7u) >> 3;
-    const uint32_t n_streams = NW / n_mt;
-    const uint32_t lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;
-    const uint32_t g = lane >> 2, t = lane & 3u;
-    const uint32_t mt = warp % n_mt, stream = warp / n_mt;
-
-    // Q fragments -> shared memory (one warp per M-tile builds them).
-    if (warp < n_mt) {
-        const uint32_t hg = warp * 8u + g;
-        const bool valid = hg < G;
-        const float *qp = J.q + (uint64_t)(kvh * G + (valid ? hg : 0u)) * 128u;
-#pragma unroll
-        for (int kk = 0; kk < 8; kk++) {
-            uint32_t r[4];
-#pragma unroll
-            for (int half = 0; half < 2; half++) {
-                const int w = 2 * kk + half;
-                const uint32_t dim = (4u * (w >> 2) + t) * 8u + 2u * (w & 3);
-                float2 x = valid ? *reinterpret_cast<const float2 *>(qp + dim) : make_float2(0.f, 0.f);
-                x.x *= P.qscale;
-                x.y *= P.qscale;
-                const __half2 hi = __floats2half2_rn(x.x, x.y);
-                const float2 hf = __half22float2(hi);
-                const __half2 lo = __floats2half2_rn(x.x - hf.x, x.y - hf.y);
-                r[half * 2] = h2_as_u32(hi);
-                r[half * 2 + 1] = h2_as_u32(lo);
-            }
-            Qs[(warp * 8 + kk) * 32 + lane] = make_uint4(r[0], r[1], r[2], r[3]);
-        }
-    }
-    __syncthreads();
-
-    const uint32_t row0 = J.start + split * J.split_rows;
-    const uint32_t row1 = min(row0 + J.split_rows, J.end);
-    const uint32_t cap = J.cap;
-    const uint64_t row_bytes = (uint64_t)P.kv_heads * 256u;
-    const char *kbase = reinterpret_cast<const char *>(J.k) + kvh * 256u;
-    const char *vbase = reinterpret_cast<const char *>(J.v) + kvh * 256u;
-    const uint4 *qs = Qs + mt * 8 * 32 + lane;
-
-    float o[16][4];
-#pragma unroll
-    for (int i = 0; i < 16; i++) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
-    float m_run = -INFINITY, l_run = 0.f;
-
-    const uint32_t bstep = n_streams * 16u;
-    uint32_t b = row0 + stream * 16u;
-    uint4 kr[2][4], vr[4][2];
-
-    auto load_k = [&](uint32_t bb) {
-        const uint32_t sb = bb % cap;
-#pragma unroll
-        for (int i = 0; i < 2; i++) {
-            const uint32_t r = bb + 8u * i + g;
-            const uint32_t slot = r < row1 ? ring_slot(sb, 8u * i + g, cap) : sb;
-            const char *p = kbase + (uint64_t)slot * row_bytes + t * 16u;
-#pragma unroll
-            for (int c = 0; c < 4; c++) kr[i][c] = ld_stream16(p + c * 64);
-        }
-    };
-    auto load_v = [&](uint32_t bb) {
-        const uint32_t sb = bb % cap;
-#pragma unroll
-        for (int x = 0; x < 4; x++) {
-            const uint32_t off = 2u * t + (x & 1) + (x >> 1) * 8u;
-            const uint32_t r = bb + off;
-            const uint32_t slot = r < row1 ? ring_slot(sb, off, cap) : sb;
-            const char *p = vbase + (uint64_t)slot * row_bytes + g * 16u;
-            vr[x][0] = ld_stream16(p);
-            vr[x][1] = ld_stream16(p + 128);
-        }
-    };
-
-    if (b < row1) {
-        load_k(b);
-        load_v(b);
-    }
-    for (; b < row1; b += bstep) {
-        // S = q K^T for rows b .. b+15 (two n-tiles of 8 keys).
-        float s[2][4];
-#pragma unroll
-        for (int i = 0; i < 2; i++) s[i][0] = s[i][1] = s[i][2] = s[i][3] = 0.f;
-#pragma unroll
-        for (int kk = 0; kk < 8; kk++) {
-            const uint4 a = qs[kk * 32];
-#pragma unroll
-            for (int i = 0; i < 2; i++) {
-                const uint4 &u = kr[i][kk >> 1];
-                const uint32_t b0 = (kk & 1) ? u.z : u.x;
-                const uint32_t b1 = (kk & 1) ? u.w : u.y;
-                mma16816(s[i], a.x, a.y, a.z, a.w, b0, b1);
-            }
-        }
-        const uint32_t nb = b + bstep;
-        if (nb < row1) load_k(nb);
-
-        // Online softmax (log2 domain) for head row g.
-        float sc[2][2];
-#pragma unroll
-        for (int i = 0; i < 2; i++)
-#pragma unroll
-            for (int e = 0; e < 2; e++) {
-                const uint32_t r = b + 8u * i + 2u * t + e;
-                sc[i][e] = r < row1 ? s[i][e] + s[i][e + 2] : -INFINITY;
-            }
-        float mx = fmaxf(fmaxf(sc[0][0], sc[0][1]), fmaxf(sc[1][0], sc[1][1]));
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-        if (__any_sync(0xffffffffu, mx > m_run + kRescaleSlack)) {
-            const float m_new = fmaxf(m_run, mx);
-            const float alpha = fast_exp2(m_run - m_new);
-            l_run *= alpha;
-#pragma unroll
-            for (int i = 0; i < 16; i++) {
-                o[i][0] *= alpha;
-                o[i][1] *= alpha;
-                o[i][2] *= alpha;
-                o[i][3] *= alpha;
-            }
-            m_run = m_new;
-        }
-        float p[2][2];
-#pragma unroll
-        for (int i = 0; i < 2; i++)
-#pragma unroll
-            for (int e = 0; e < 2; e++) {
-                p[i][e] = fast_exp2(sc[i][e] - m_run);
-                l_run += p[i][e];
-            }
-        uint32_t pa[4];
-#pragma unroll
-        for (int i = 0; i < 2; i++) {
-            const __half2 hi = __floats2half2_rn(p[i][0], p[i][1]);
-            const float2 hf = __half22float2(hi);
-            const __half2 lo = __floats2half2_rn(p[i][0] - hf.x, p[i][1] - hf.y);
-            pa[2 * i] = h2_as_u32(hi);
-            pa[2 * i + 1] = h2_as_u32(lo);
-        }
-        // O += P V over 16 n-tiles of 8 (permuted) dims.
-#pragma unroll
-        for (int jt = 0; jt < 16; jt++) {
-            const int u = jt >> 3, e = jt & 7, w = e >> 1;
-            const uint32_t sel = (e & 1) ? 0x7632u : 0x5410u;
-            const uint32_t b0 = prmt(word_of(vr[0][u], w), word_of(vr[1][u], w), sel);
-            const uint32_t b1 = prmt(word_of(vr[2][u], w), word_of(vr[3][u], w), sel);
-            mma16816(o[jt], pa[0], pa[1], pa[2], pa[3], b0, b1);
-        }
-        if (nb < row1) load_v(nb);
-    }
-
-    // Per-warp state -> shared memory.
-    l_run += __shfl_xor_sync(0xffffffffu, l_run, 1);
-    l_run += __shfl_xor_sync(0xffffffffu, l_run, 2);
-    const uint32_t hrow = mt * 8u + g;
-    float *Ow = Os + (stream * 16u + hrow) * 128u;
-    if (hrow < G) {
-#pragma unroll
-        for (int jt = 0; jt < 16; jt++)
-#pragma unroll
-            for (int e = 0; e < 2; e++) {
-                const uint32_t c = 2u * t + e;
-                const uint32_t dim = jt < 8 ? 8u * c + jt : 64u + 8u * c + (jt - 8);
-                Ow[dim] = o[jt][e] + o[jt][e + 2];
-            }
-        if (t == 0) {
-            Ms[stream * 16u + hrow] = m_run;
-            Ls[stream * 16u + hrow] = l_run;
-        }
-    }
-    finish_cta<NW * 32>(P, J, j, kvh, split, cta, n_streams, Os, Ms, Ls);
-}
-
 // ------------------------------------------------------------ f16 kernel, cp.async pipeline
-// Same math and register fragments as decode_f16_kernel, but K/V blocks are
+// The math and register fragments above; K/V blocks are
 // staged through a per-warp ring of S shared-memory stages filled with
 // 16-byte cp.async copies, so S-1 blocks (8 KB each) per warp are in flight
 // without holding registers.  Warps never wait on each other inside the
@@ -1067,176 +881,6 @@ __global__ void __launch_bounds__(NW * 32, 1) decode_f32_pipe_kernel(const __gri
     finish_cta<NW * 32>(P, J, j, kvh, split, cta, n_streams, Os, Ms, Ls);
 }
 
-// ------------------------------------------------------------ f32 kernel
-// Warp = (part, stream): part p owns heads [p*GP, (p+1)*GP) of the group,
-// stream s takes row blocks s, s+n_streams, ...  Lane holds dims 4*lane..+3.
-template <int NW, int GP, int R>
-__global__ void __launch_bounds__(NW * 32) decode_f32_kernel(const __grid_constant__ DecodeParams P) {
-    extern __shared__ __align__(16) float smem[];
-    float *Os = smem;                          // 16 streams*16 heads*128 max
-    float *Ms = Os + NW * 16 * 128;
-    float *Ls = Ms + 16 * NW;
-    float *Sx = Ls + 16 * NW;                  // [NW][R*GP] scores / probabilities
-
-    constexpr int N = R * GP;  // partial dot products per lane per block
-    const uint32_t cta = blockIdx.x;
-    const uint32_t j = locate_job(P, cta);
-    const JobDev &J = P.job[j];
-    const uint32_t local = cta - J.cta_begin;
-    const uint32_t kvh = local / J.n_splits, split = local - kvh * J.n_splits;
-    const uint32_t G = P.group;
-    const uint32_t parts = G / GP;
-    const uint32_t n_streams = NW / parts;
-    const uint32_t lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;
-    const uint32_t part = warp % parts, stream = warp / parts;
-    float *sx = Sx + warp * N;
-
-    float4 q[GP];
-#pragma unroll
-    for (int h = 0; h < GP; h++) {
-        const float4 x = *reinterpret_cast<const float4 *>(
-            J.q + (uint64_t)(kvh * G + part * GP + h) * 128u + lane * 4u);
-        q[h] = make_float4(x.x * P.qscale, x.y * P.qscale, x.z * P.qscale, x.w * P.qscale);
-    }
-    float4 o[GP];
-    float m[GP], l[GP];
-#pragma unroll
-    for (int h = 0; h < GP; h++) {
-        o[h] = make_float4(0.f, 0.f, 0.f, 0.f);
-        m[h] = -INFINITY;
-        l[h] = 0.f;
-    }
-
-    const uint32_t row0 = J.start + split * J.split_rows;
-    const uint32_t row1 = min(row0 + J.split_rows, J.end);
-    const uint32_t cap = J.cap;
-    const uint64_t row_elems = (uint64_t)P.kv_heads * 128u;
-    const float *kb = reinterpret_cast<const float *>(J.k) + kvh * 128u + lane * 4u;
-    const float *vb = reinterpret_cast<const float *>(J.v) + kvh * 128u + lane * 4u;
-
-    for (uint32_t b = row0 + stream * R; b < row1; b += n_streams * R) {
-        const uint32_t sb = b % cap;
-        float4 kf[R], vf[R];
-#pragma unroll
-        for (int r = 0; r < R; r++) {
-            const uint32_t slot = b + r < row1 ? ring_slot(sb, r, cap) : sb;
-            kf[r] = ld_stream_f4(kb + slot * row_elems);
-            vf[r] = ld_stream_f4(vb + slot * row_elems);
-        }
-        float d[N];
-#pragma unroll
-        for (int r = 0; r < R; r++)
-#pragma unroll
-            for (int h = 0; h < GP; h++)
-                d[r * GP + h] = q[h].x * kf[r].x + q[h].y * kf[r].y + q[h].z * kf[r].z +
-                                q[h].w * kf[r].w;
-        // Transposing butterfly: after it, lane holds cnt values whose
-        // original indices are idx0 .. idx0+cnt-1.
-        int cnt = N;
-        uint32_t idx0 = 0;
-#pragma unroll
-        for (int msk = 16; msk >= 1; msk >>= 1) {
-            if ((cnt & 1) == 0) {
-                const int half = cnt >> 1;
-                const bool upper = (lane & msk) != 0;
-#pragma unroll
-                for (int i = 0; i < N / 2; i++) {
-                    if (i < half) {
-                        const float send = upper ? d[i] : d[i + half];
-                        const float keep = upper ? d[i + half] : d[i];
-                        d[i] = keep + __shfl_xor_sync(0xffffffffu, send, msk);
-                    }
-                }
-                if (upper) idx0 += half;
-                cnt = half;
-            } else {
-#pragma unroll
-                for (int i = 0; i < N; i++)
-                    if (i < cnt) d[i] += __shfl_xor_sync(0xffffffffu, d[i], msk);
-            }
-        }
-        // Own scores -> shared, then every lane reads all of them.
-#pragma unroll
-        for (int i = 0; i < N; i++)
-            if (i < cnt) sx[idx0 + i] = d[i];
-        __syncwarp();
-        float sc[N];
-#pragma unroll
-        for (int i = 0; i < N; i += 4) {
-            const float4 x = *reinterpret_cast<const float4 *>(sx + i);
-            sc[i] = x.x;
-            sc[i + 1] = x.y;
-            sc[i + 2] = x.z;
-            sc[i + 3] = x.w;
-        }
-        const uint32_t nvalid = row1 - b;
-#pragma unroll
-        for (int r = 0; r < R; r++)
-            if ((uint32_t)r >= nvalid)
-#pragma unroll
-                for (int h = 0; h < GP; h++) sc[r * GP + h] = -INFINITY;
-#pragma unroll
-        for (int h = 0; h < GP; h++) {
-            float bm = sc[h];
-#pragma unroll
-            for (int r = 1; r < R; r++) bm = fmaxf(bm, sc[r * GP + h]);
-            if (bm > m[h] + kRescaleSlack) {  // uniform across the warp
-                const float alpha = fast_exp2(m[h] - bm);
-                l[h] *= alpha;
-                o[h].x *= alpha;
-                o[h].y *= alpha;
-                o[h].z *= alpha;
-                o[h].w *= alpha;
-                m[h] = bm;
-            }
-        }
-        __syncwarp();
-        // Own probabilities -> shared, then every lane reads all of them.
-#pragma unroll
-        for (int i = 0; i < N; i++)
-            if (i < cnt) {
-                const uint32_t id = idx0 + i;
-                const uint32_t h = id % GP, r = id / GP;
-                float mh = m[0];
-#pragma unroll
-                for (int hh = 1; hh < GP; hh++)
-                    if (h == (uint32_t)hh) mh = m[hh];
-                sx[id] = r < nvalid ? fast_exp2(d[i] - mh) : 0.f;
-            }
-        __syncwarp();
-#pragma unroll
-        for (int i = 0; i < N; i += 4) {
-            const float4 x = *reinterpret_cast<const float4 *>(sx + i);
-            sc[i] = x.x;
-            sc[i + 1] = x.y;
-            sc[i + 2] = x.z;
-            sc[i + 3] = x.w;
-        }
-        __syncwarp();
-#pragma unroll
-        for (int r = 0; r < R; r++)
-#pragma unroll
-            for (int h = 0; h < GP; h++) {
-                const float pv = sc[r * GP + h];
-                l[h] += pv;
-                o[h].x += pv * vf[r].x;
-                o[h].y += pv * vf[r].y;
-                o[h].z += pv * vf[r].z;
-                o[h].w += pv * vf[r].w;
-            }
-    }
-#pragma unroll
-    for (int h = 0; h < GP; h++) {
-        const uint32_t hrow = part * GP + h;
-        *reinterpret_cast<float4 *>(Os + (stream * 16u + hrow) * 128u + lane * 4u) = o[h];
-        if (lane == 0) {
-            Ms[stream * 16u + hrow] = m[h];
-            Ls[stream * 16u + hrow] = l[h];
-        }
-    }
-    finish_cta<NW * 32>(P, J, j, kvh, split, cta, n_streams, Os, Ms, Ls);
-}
-
 // ------------------------------------------------------------ generic kernel
 // Any head_dim <= 256 and any group: one warp per (job, query head), one
 // pass over the rows with an online softmax.  Lane holds dims lane + 32*i.
@@ -1303,23 +947,6 @@ __global__ void __launch_bounds__(256) decode_generic_kernel(const __grid_consta
 }
 
 // ------------------------------------------------------------ host side
-static int f32_gp(uint32_t G) {
-    switch (G) {
-        case 1: return 1;
-        case 2: return 2;
-        case 4: return 4;
-        case 8: return 8;
-        case 12: return 6;
-        case 16: return 8;
-        default: return 0;
-    }
-}
-
-constexpr int kNW = 4;  // warps per CTA of the fast kernels
-
-static size_t smem_f16() {
-    return (size_t)(kNW * 16 * 128 + 32 * kNW) * 4 + 2 * 8 * 32 * 16;
-}
 // inv_freq of RoPE pair `pair`: sf37_inv_freq (sf37.c:1995-2013), double.
 static double rope_inv_freq(uint32_t pair, uint32_t dim, double theta, uint32_t llama3) {
     const double inv = 1.0 / pow(theta, (double)(pair * 2u) / (double)dim);
@@ -1355,16 +982,6 @@ static void rope_table(float *t, const RopeKey &k) {
     }
 }
 
-// SF37KV_PDL=0 turns programmatic dependent launch off (default on).
-static bool pdl_enabled() {
-    static int on = -1;
-    if (on < 0) {
-        const char *e = getenv("SF37KV_PDL");
-        on = (e && !strcmp(e, "0")) ? 0 : 1;
-    }
-    return on != 0;
-}
-
 // Launches a pipelined decode kernel; with P.pdl set, with programmatic
 // stream serialization so that its CTAs start (and prefetch cached rows)
 // while the previous kernel on the stream drains.
@@ -1391,11 +1008,6 @@ static void launch_pipe(Kernel kernel, unsigned grid, unsigned block, size_t sme
 constexpr size_t kPrepSmem = (16 * 128 + 128) * 4;  // prepared q heads + K head (PREP kernels)
 static size_t smem_pipe(int nw, int stages) { return (size_t)nw * stages * 8192 + 2 * 8 * 32 * 16; }
 static size_t smem_pipe32(int nw, int stages) { return (size_t)nw * stages * 16384 + 2 * 8 * 32 * 16; }
-template <int GP, int R>
-static size_t smem_f32() {
-    return (size_t)(kNW * 16 * 128 + 32 * kNW + kNW * R * GP) * 4;
-}
-
 static int launch_generic(const AttnJob *jobs, uint32_t n, uint32_t q_heads, uint32_t kv_heads,
                           uint32_t head_dim, int dtype, cudaStream_t stream) {
     if (head_dim > 256)
@@ -1422,18 +1034,6 @@ static int launch_generic(const AttnJob *jobs, uint32_t n, uint32_t q_heads, uin
     return SF37KV_OK;
 }
 
-template <int GP, int R>
-static void launch_f32(const DecodeParams &P, unsigned grid, cudaStream_t stream) {
-    static bool attr = false;
-    const size_t sm = smem_f32<GP, R>();
-    if (!attr) {
-        cudaFuncSetAttribute(decode_f32_kernel<kNW, GP, R>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
-        attr = true;
-    }
-    decode_f32_kernel<kNW, GP, R><<<grid, kNW * 32, sm, stream>>>(P);
-}
-
 int attention_jobs(const AttnJob *jobs, uint32_t n, uint32_t q_heads, uint32_t kv_heads,
                    uint32_t head_dim, int dtype, cudaStream_t stream) {
     if (dtype != SF37KV_F32 && dtype != SF37KV_F16)
@@ -1447,19 +1047,15 @@ int attention_jobs(const AttnJob *jobs, uint32_t n, uint32_t q_heads, uint32_t k
             return set_error(SF37KV_EINVAL, "attention: job %u is invalid", i);
     }
     const uint32_t G = q_heads / kv_heads;
-    // Kernels that store appended rows themselves: the f16 cp.async pipeline
-    // (default variant) and the fp32 tensor-core pipeline (default); for the
-    // others the rows are appended by a separate launch first.
-    const char *ef = getenv("SF37KV_DECODE_F32");
-    const char *ek = getenv("SF37KV_DECODE_KERNEL");
-    const bool fuses = head_dim == 128 && G <= 16 &&
-                       ((dtype == SF37KV_F16 && !(ek && (!strcmp(ek, "reg2") || !strcmp(ek, "reg3")))) ||
-                        (dtype == SF37KV_F32 && !(ef && !strcmp(ef, "cuda"))));
+    // The pipelined kernels (head_dim 128, group <= 16) store the appended
+    // rows themselves; for the generic kernel they are appended by a
+    // separate launch first.
+    const bool fuses = head_dim == 128 && G <= 16;
     bool any_prep = false;
     for (uint32_t i = 0; i < n; i++) any_prep |= jobs[i].prep != nullptr;
     if (any_prep && !fuses)
         return set_error(SF37KV_EUNSUPPORTED,
-                         "decode_prep: needs head_dim 128, group <= 16 and the default pipelined kernels");
+                         "decode_prep: needs head_dim 128 and group <= 16");
     if (!fuses) {
         AppendJob aj[kMaxJobs];
         for (uint32_t base = 0; base < n; base += kMaxJobs) {
@@ -1472,9 +1068,7 @@ int attention_jobs(const AttnJob *jobs, uint32_t n, uint32_t q_heads, uint32_t k
                 if (int rc = append_jobs(aj, na, kv_heads * head_dim, dtype, stream)) return rc;
         }
     }
-    const bool fast = head_dim == 128 && G <= 16 &&
-                      (dtype == SF37KV_F16 || f32_gp(G) != 0 || !getenv("SF37KV_DECODE_F32"));
-    if (!fast) return launch_generic(jobs, n, q_heads, kv_heads, head_dim, dtype, stream);
+    if (!fuses) return launch_generic(jobs, n, q_heads, kv_heads, head_dim, dtype, stream);
 
     const int sms = num_sms();
     for (uint32_t base = 0, m = 0; base < n; base += m) {
@@ -1542,7 +1136,6 @@ int attention_jobs(const AttnJob *jobs, uint32_t n, uint32_t q_heads, uint32_t k
                 per = 8192;
             }
         }
-        if (const char *e = getenv("SF37KV_SPLIT_ROWS")) per = strtoull(e, nullptr, 10) ? strtoull(e, nullptr, 10) : per;
         DecodeParams P;
         P.pdl = 0;
         P.n_jobs = m;
@@ -1591,69 +1184,31 @@ int attention_jobs(const AttnJob *jobs, uint32_t n, uint32_t q_heads, uint32_t k
         }
         P.part = S.part;
         P.counters = S.counters;
+        // Pipelined kernels, 4 warps x 3 cp.async stages; launched with
+        // programmatic dependent launch (PDL).
+        P.pdl = 1;
         if (dtype == SF37KV_F16) {
-            // SF37KV_DECODE_KERNEL selects a variant for tuning runs:
-            // pipe4 (default: 4 warps x 3 cp.async stages, two CTAs per SM),
-            // pipe8 (8 warps x 3 stages, one CTA per SM), reg2 / reg3 (register
-            // prefetch, 2 or 3 CTAs per SM).  Measured on B200 (48 layers, 32K
-            // rows): pipe4 6.25 TB/s, pipe8 5.97, reg2 5.09.
-            static int variant = -1;
-            if (variant < 0) {
-                const char *e = getenv("SF37KV_DECODE_KERNEL");
-                variant = !e ? 1 : !strcmp(e, "pipe8") ? 0 : !strcmp(e, "reg2") ? 2 : !strcmp(e, "reg3") ? 3 : 1;
-                cudaFuncSetAttribute(decode_f16_kernel<kNW, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     (int)smem_f16());
-                cudaFuncSetAttribute(decode_f16_kernel<kNW, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     (int)smem_f16());
-                cudaFuncSetAttribute(decode_f16_pipe_kernel<8, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     (int)smem_pipe(8, 3));
+            static bool attr = false;
+            if (!attr) {
                 cudaFuncSetAttribute(decode_f16_pipe_kernel<4, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      (int)smem_pipe(4, 3));
-            }
-            static bool prep_attr = false;
-            if (any_prep && !prep_attr) {
                 cudaFuncSetAttribute(decode_f16_pipe_kernel<4, 3, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      (int)(smem_pipe(4, 3) + kPrepSmem));
-                prep_attr = true;
+                attr = true;
             }
-            P.pdl = pdl_enabled() && (any_prep || variant == 1 || variant == 0);
             if (any_prep) launch_pipe(decode_f16_pipe_kernel<4, 3, true>, ctas, 128, smem_pipe(4, 3) + kPrepSmem, stream, P);
-            else switch (variant) {
-                case 1: launch_pipe(decode_f16_pipe_kernel<4, 3>, ctas, 128, smem_pipe(4, 3), stream, P); break;
-                case 2: decode_f16_kernel<kNW, 2><<<ctas, kNW * 32, smem_f16(), stream>>>(P); break;
-                case 3: decode_f16_kernel<kNW, 3><<<ctas, kNW * 32, smem_f16(), stream>>>(P); break;
-                default: launch_pipe(decode_f16_pipe_kernel<8, 3>, ctas, 256, smem_pipe(8, 3), stream, P); break;
-            }
+            else launch_pipe(decode_f16_pipe_kernel<4, 3>, ctas, 128, smem_pipe(4, 3), stream, P);
         } else {
-            // SF37KV_DECODE_F32=cuda selects the CUDA-core fp32 kernel (comparison runs).
-            static int f32_cuda = -1;
-            if (f32_cuda < 0) {
-                const char *e = getenv("SF37KV_DECODE_F32");
-                f32_cuda = (e && !strcmp(e, "cuda")) ? 1 : 0;
+            static bool attr = false;
+            if (!attr) {
                 cudaFuncSetAttribute(decode_f32_pipe_kernel<4, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      (int)smem_pipe32(4, 3));
-            }
-            static bool prep_attr = false;
-            if (any_prep && !prep_attr) {
                 cudaFuncSetAttribute(decode_f32_pipe_kernel<4, 3, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      (int)(smem_pipe32(4, 3) + kPrepSmem));
-                prep_attr = true;
+                attr = true;
             }
-            P.pdl = pdl_enabled() && (any_prep || !f32_cuda);
-            if (any_prep) {
-                launch_pipe(decode_f32_pipe_kernel<4, 3, true>, ctas, 128, smem_pipe32(4, 3) + kPrepSmem, stream, P);
-            } else if (!f32_cuda) {
-                launch_pipe(decode_f32_pipe_kernel<4, 3>, ctas, 128, smem_pipe32(4, 3), stream, P);
-            } else {
-                switch (G) {
-                    case 1: launch_f32<1, 8>(P, ctas, stream); break;
-                    case 2: launch_f32<2, 8>(P, ctas, stream); break;
-                    case 4: launch_f32<4, 8>(P, ctas, stream); break;
-                    case 8: launch_f32<8, 4>(P, ctas, stream); break;
-                    case 12: launch_f32<6, 4>(P, ctas, stream); break;
-                    default: launch_f32<8, 4>(P, ctas, stream); break;  // 16
-                }
-            }
+            if (any_prep) launch_pipe(decode_f32_pipe_kernel<4, 3, true>, ctas, 128, smem_pipe32(4, 3) + kPrepSmem, stream, P);
+            else launch_pipe(decode_f32_pipe_kernel<4, 3>, ctas, 128, smem_pipe32(4, 3), stream, P);
         }
         g_launches++;
         if (int rc = check_cuda(cudaGetLastError(), "attention launch")) return rc;
@@ -1811,10 +1366,9 @@ int attention_jobs_prealloc(const AttnJob *jobs, uint32_t n, uint32_t q_heads, u
         return set_error(SF37KV_EINVAL, "decode_noalloc: bad head configuration q=%u kv=%u", q_heads,
                          kv_heads);
     const uint32_t G = q_heads / kv_heads;
-    if (head_dim != 128 || G > 16 || (dtype == SF37KV_F32 && f32_gp(G) == 0))
+    if (head_dim != 128 || G > 16)
         return set_error(SF37KV_EUNSUPPORTED,
-                         "decode_noalloc: needs head_dim 128 and q_heads/kv_heads in {1,2,4,8,12,16} "
-                         "(f32) or <= 16 (f16); got head_dim %u, group %u",
+                         "decode_noalloc: needs head_dim 128 and q_heads/kv_heads <= 16; got head_dim %u, group %u",
                          head_dim, G);
     if (n > (uint32_t)kMaxJobs)
         return set_error(SF37KV_EINVAL, "decode_noalloc: %u layers exceed the maximum of %d per call", n,
@@ -1865,7 +1419,7 @@ int attention_jobs_prealloc(const AttnJob *jobs, uint32_t n, uint32_t q_heads, u
             if (ns < 1) ns = 1;
             if (ns > 1) any_split = true;
             P.job[i] = JobDev{A.k, A.v, A.q, A.gate, A.out, A.start, A.end, A.cap, sr, (uint32_t)ns, ctas,
-                              nullptr, nullptr, 0};
+                              A.k_new, A.v_new, 0};
             ctas += (uint32_t)ns * kv_heads;
         }
         P.total_ctas = ctas;
@@ -1880,19 +1434,16 @@ int attention_jobs_prealloc(const AttnJob *jobs, uint32_t n, uint32_t q_heads, u
     if (int rc = check_cuda(cudaMemsetAsync(counters, 0, (size_t)n * kv_heads * 4u, stream),
                             "decode_noalloc counter clear"))
         return rc;
+    // The same pipelined kernels as sf37kv_decode's defaults (f16: 4 warps x
+    // 3 stages; f32: the bf16 hi/lo tensor-core kernel), without PDL.
     if (dtype == SF37KV_F16) {
         cudaFuncSetAttribute(decode_f16_pipe_kernel<4, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)smem_pipe(4, 3));
         decode_f16_pipe_kernel<4, 3><<<P.total_ctas, 128, smem_pipe(4, 3), stream>>>(P);
     } else {
-        switch (G) {
-            case 1: launch_f32<1, 8>(P, P.total_ctas, stream); break;
-            case 2: launch_f32<2, 8>(P, P.total_ctas, stream); break;
-            case 4: launch_f32<4, 8>(P, P.total_ctas, stream); break;
-            case 8: launch_f32<8, 4>(P, P.total_ctas, stream); break;
-            case 12: launch_f32<6, 4>(P, P.total_ctas, stream); break;
-            default: launch_f32<8, 4>(P, P.total_ctas, stream); break;
-        }
+        cudaFuncSetAttribute(decode_f32_pipe_kernel<4, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)smem_pipe32(4, 3));
+        decode_f32_pipe_kernel<4, 3><<<P.total_ctas, 128, smem_pipe32(4, 3), stream>>>(P);
     }
     g_launches++;
     return check_cuda(cudaGetLastError(), "decode_noalloc launch");
@@ -1908,8 +1459,8 @@ int attention_jobs_gather(const AttnJob *jobs, uint32_t n, uint32_t q_heads, uin
     if (n > (uint32_t)kMaxJobs)
         return set_error(SF37KV_EINVAL, "decode_gather: at most %d layers per call", kMaxJobs);
     const uint32_t G = kv_heads ? q_heads / kv_heads : 0;
-    if (head_dim != 128 || G == 0 || G > 16 || (dtype == SF37KV_F32 && f32_gp(G) == 0 && getenv("SF37KV_DECODE_F32")))
-        return set_error(SF37KV_EUNSUPPORTED, "decode_gather: needs head_dim 128, group <= 16 and a fast kernel");
+    if (head_dim != 128 || G == 0 || G > 16)
+        return set_error(SF37KV_EUNSUPPORTED, "decode_gather: needs head_dim 128 and group <= 16");
     if (n == 0) return set_error(SF37KV_EINVAL, "decode_gather: no layers (the epoch flag would never rise)");
     for (uint32_t i = 0; i < n; i++) g_gather_off[i] = offsets[i];
     g_gather_cur = gat;

@@ -59,25 +59,24 @@ extern "C" int sf37kv_decode_noalloc(const sf37kv_decode_layer *layers, uint32_t
         return set_error(SF37KV_EINVAL, "decode_noalloc: %u layers exceed the maximum of %d per call",
                          n_layers, kMaxJobs);
     cudaStream_t s = stream ? (cudaStream_t)stream : current_stream();
-    void *scratch = nullptr;
-    if (int rc = noalloc_scratch(&scratch)) return rc;
-    AppendJob aj[kMaxJobs];
+    // Every check runs before the first launch, so a rejected call leaves
+    // the caches untouched.  The appended row is stored by the attention
+    // kernel itself (the same pipelined kernels sf37kv_decode uses), so a
+    // call is one counter clear plus one launch.
     AttnJob jobs[kMaxJobs];
-    uint32_t na = 0;
     for (uint32_t i = 0; i < n_layers; i++) {
         const sf37kv_decode_layer &L = layers[i];
         if (L.cache.cap == 0) return set_error(SF37KV_EINVAL, "decode_noalloc: layer %u cap 0", i);
-        if (L.k_new || L.v_new) {
-            if (!L.k_new || !L.v_new)
-                return set_error(SF37KV_EINVAL, "decode_noalloc: layer %u has only one of k_new/v_new", i);
-            aj[na++] = AppendJob{L.cache.k_cache, L.cache.v_cache, L.k_new, L.v_new, L.pos, 1, L.cache.cap};
-        }
+        if ((L.k_new != nullptr) != (L.v_new != nullptr))
+            return set_error(SF37KV_EINVAL, "decode_noalloc: layer %u has only one of k_new/v_new", i);
+        if (L.k_new && (((uintptr_t)L.k_new | (uintptr_t)L.v_new) & 15u))
+            return set_error(SF37KV_EINVAL, "decode_noalloc: layer %u k_new/v_new must be 16-byte aligned", i);
         jobs[i] = AttnJob{L.cache.k_cache, L.cache.v_cache, L.q, L.gate, L.out,
                           start_at(L.pos, L.cache.cap, L.cache.sliding, L.cache.window), L.pos + 1u,
-                          L.cache.cap};
+                          L.cache.cap, L.k_new, L.v_new};
     }
-    if (na)
-        if (int rc = append_jobs(aj, na, kv_heads * head_dim, dtype, s)) return rc;
+    void *scratch = nullptr;
+    if (int rc = noalloc_scratch(&scratch)) return rc;
     unsigned char *base = static_cast<unsigned char *>(scratch);
     return attention_jobs_prealloc(jobs, n_layers, q_heads, kv_heads, head_dim, dtype, s,
                                    reinterpret_cast<float *>(base + kCounterBytes),

@@ -65,9 +65,7 @@ extern "C" int sf37kv_prefill(const sf37kv_cache *cache, const void *q, int q_ty
     cudaStream_t s = stream ? (cudaStream_t)stream : current_stream();
     if (dtype == SF37KV_F16 && head_dim == 128) {
         bool handled = false;
-        // SF37KV_PREFILL=mma selects the mma.sync kernel; default tcgen05.
-        const char *e = getenv("SF37KV_PREFILL");
-        if (q_type == SF37KV_Q_BF16 && !(e && !strcmp(e, "mma")))
+        if (q_type == SF37KV_Q_BF16)
             if (int rc = prefill_tc05(cache, q, gate, out, pos0, n_tok, q_heads, kv_heads, s, &handled))
                 return rc;
         if (!handled)

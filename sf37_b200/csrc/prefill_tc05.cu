@@ -58,8 +58,6 @@ struct Tc05Params {
     uint32_t pos0, n_tok, cap, sliding, window;
     uint32_t q_heads, kv_heads, group, tpt;  // tpt = 128 / group tokens per Q tile
     float qscale;
-    long long *trace;  // per-stage clock64 stamps of CTA (0,0) when dbg & 8
-    uint32_t dbg;  // timing experiments only (SF37KV_TC05_DBG): 1 no softmax math, 2 no PV, 4 no TMA
 };
 
 namespace tc05 {
@@ -217,12 +215,6 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map
 
 }  // namespace tc05
 
-#define TC05_TRACE(slot, j)                                                                         \
-    do {                                                                                            \
-        if ((P.dbg & 8) && blockIdx.x == 0 && blockIdx.y == 0 && (j) < 16)                          \
-            P.trace[(slot) * 16 + (j)] = clock64();                                                 \
-    } while (0)
-
 // POLY: one in POLY exp2 evaluations of a row uses the FMA polynomial
 // (exp2_fma), the others the MUFU unit (0 = MUFU only); balances the MUFU
 // and issue limits of the softmax warps.
@@ -315,7 +307,6 @@ __global__ void __launch_bounds__(576, 1) prefill_tc05_kernel(const __grid_const
                 const uint32_t full = bar((which ? B_VFULL : B_KFULL) + b);
                 const uint32_t dst = tile((which ? T_V : T_K) + b);
                 const CUtensorMap *map = which ? &P.vmap : &P.kmap;
-                if (P.dbg & 4) { bar_arrive(full); return; }
                 bar_expect_tx(full, kTile);
                 tma_load_2d(dst, map, x0, y, full);
                 tma_load_2d(dst + kHalf, map, x0 + 64, y, full);
@@ -351,7 +342,6 @@ __global__ void __launch_bounds__(576, 1) prefill_tc05_kernel(const __grid_const
             auto issue_pv = [&](uint32_t t, uint32_t j) {
                 const uint32_t vt = tile(T_V + (j & 1u));
                 fence_after();
-                if (!(P.dbg & 2))
 #pragma unroll
                 for (uint32_t kk = 0; kk < 8; kk++)
                     mma_ts(tmem + 256u + t * 128u, tmem + t * 128u + kk * 8u, sdesc(vt + kk * 2048u, kHalf, 1024),
@@ -372,15 +362,12 @@ __global__ void __launch_bounds__(576, 1) prefill_tc05_kernel(const __grid_const
                     commit(bar(B_KEMPTY));
                 }
                 if (!wait_bar(bar(B_VFULL + vb), vph)) { bad = true; break; }
-                TC05_TRACE(2, j);
                 issue_pv(0, j);
                 if (more) {
                     if (!wait_bar(bar(B_KFULL + ((j + 1) & 1u)), ((j + 1) >> 1) & 1u)) { bad = true; break; }
-                    TC05_TRACE(3, j);
                     issue_s(0, j + 1);
                 }
                 if (!wait_bar(bar(B_PFULL + 1), j & 1u)) { bad = true; break; }
-                TC05_TRACE(4, j);
                 issue_pv(1, j);
                 commit(bar(B_VEMPTY + vb));
                 if (more) {
@@ -461,11 +448,9 @@ __global__ void __launch_bounds__(576, 1) prefill_tc05_kernel(const __grid_const
         };
         for (uint32_t j = 0; j < ntiles; j++) {
             const uint32_t k0 = kbeg + j * 128u;
-            if (r == 0 && hh == 0) TC05_TRACE(5 + 4 * t_id, j);
             __syncwarp();
             const bool got_s = !abort_sh && wait_bar_warp(bar(B_SFULL + t_id), j & 1u);
             fence_after();
-            if (r == 0 && hh == 0) TC05_TRACE(6 + 4 * t_id, j);
             // s_full(j) follows every earlier MMA of the issuing thread, so
             // PV_t(j-1) is complete: O_t is stable and P_t may be rewritten.
             const bool full = k0 >= full_lo && k0 + 127u <= full_hi;
@@ -478,7 +463,6 @@ __global__ void __launch_bounds__(576, 1) prefill_tc05_kernel(const __grid_const
             // the first tile); then the row max is exchanged with the partner
             // half, O and l are rescaled and P is recomputed.
             const bool need = m == -INFINITY || xm > 8.0f;
-            if (r == 0 && hh == 0) TC05_TRACE(7 + 4 * t_id, j);
             if (pair_any(need)) {
                 xch[j & 1u][t_id][hh][r] = xm + mu0;
                 pair_any(false);
@@ -512,7 +496,6 @@ __global__ void __launch_bounds__(576, 1) prefill_tc05_kernel(const __grid_const
             tmem_st16u(t_s + cb / 2u + 16u, w[1]);
             tmem_wait_st();
             fence_before();
-            if (r == 0 && hh == 0) TC05_TRACE(8 + 4 * t_id, j);
             bar_arrive(bar(B_PFULL + t_id));  // P_t ready (S_t fully consumed)
         }
         const bool got_e = ok && !abort_sh && wait_bar_warp(bar(B_ODONE + t_id), (ntiles - 1) & 1u);
@@ -603,50 +586,15 @@ int prefill_tc05(const sf37kv_cache *cache, const void *q, const float *gate, fl
     P.group = G;
     P.tpt = 128u / G;
     P.qscale = 1.4426950408889634f / sqrtf(128.0f);
-    {
-        const char *e = getenv("SF37KV_TC05_DBG");
-        P.dbg = e ? (uint32_t)atoi(e) : 0u;
-    }
     const size_t sm = 6 * tc05::kTile + 1024;
-    static int poly = -1;
-    if (poly < 0) {
-        const char *e = getenv("SF37KV_TC05_POLY");
-        poly = e ? atoi(e) : 0;
+    static bool attr = false;
+    if (!attr) {
         cudaFuncSetAttribute(prefill_tc05_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
-        cudaFuncSetAttribute(prefill_tc05_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
-        cudaFuncSetAttribute(prefill_tc05_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
-        cudaFuncSetAttribute(prefill_tc05_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
-        cudaFuncSetAttribute(prefill_tc05_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+        attr = true;
     }
     dim3 grid((n_tok + 2 * P.tpt - 1) / (2 * P.tpt), kv_heads);
-    static long long *trace = nullptr;
-    P.trace = nullptr;
-    if (P.dbg & 8) {
-        if (!trace) cudaMalloc(&trace, 16 * 16 * sizeof(long long));
-        cudaMemset(trace, 0, 16 * 16 * sizeof(long long));
-        P.trace = trace;
-    }
-    switch (poly) {
-        case 0: prefill_tc05_kernel<0><<<grid, 576, sm, stream>>>(P); break;
-        case 1: prefill_tc05_kernel<1><<<grid, 576, sm, stream>>>(P); break;
-        case 2: prefill_tc05_kernel<2><<<grid, 576, sm, stream>>>(P); break;
-        case 8: prefill_tc05_kernel<8><<<grid, 576, sm, stream>>>(P); break;
-        case 4: prefill_tc05_kernel<4><<<grid, 576, sm, stream>>>(P); break;
-        default: prefill_tc05_kernel<0><<<grid, 576, sm, stream>>>(P); break;
-    }
+    prefill_tc05_kernel<0><<<grid, 576, sm, stream>>>(P);
     g_launches++;
-    if (P.dbg & 8) {
-        long long h[256];
-        cudaMemcpy(h, trace, sizeof(h), cudaMemcpyDeviceToHost);
-        const long long t0 = h[5 * 16];
-        const char *names[15] = {"mma:top", "mma:vfull", "mma:pA", "mma:kfull", "mma:pB", "A:wait", "A:sfull",
-                                 "A:pass1", "A:arrive", "B:wait", "B:sfull", "B:pass1", "B:arrive", "A:j1sub", "B:j1sub"};
-        for (int sl = 0; sl < 15; sl++) {
-            fprintf(stderr, "%-10s", names[sl]);
-            for (int j = 0; j < 12; j++) fprintf(stderr, " %7lld", h[sl * 16 + j] ? h[sl * 16 + j] - t0 : -1);
-            fprintf(stderr, "\n");
-        }
-    }
     if (int rc = check_cuda(cudaGetLastError(), "prefill tcgen05 launch")) return rc;
     *handled = true;
     return SF37KV_OK;
