@@ -1,20 +1,30 @@
 #!/usr/bin/env python
 """Benchmark of the SF37 KV-cache hot path on B200.
 
-Default workload: one decode step of a synthetic
-48-layer stack, 64 query heads / 8 KV heads, head_dim 128, f16 KV caches with
-32768 cached positions, batch 1.  Per layer and step: append one K/V row,
-then GQA attention over 32769+ positions (the position advances every
-step).  One step = one sf37kv_decode() call over all 48 layers.
+Headline: one decode step of a synthetic 48-layer stack,
+64 query heads / 8 KV heads, head_dim 128, f16 KV caches with 32768 cached
+positions, batch 1.  Per layer and step: append one K/V row, then GQA
+attention over 32769+ positions (the position advances every step).  One
+step = one sf37kv_decode() call over all 48 layers.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
 
-N > 1 (under torchrun): KV heads sharded 8/N per GPU, per-head attention
-outputs all-gathered over NCCL every step; total work is fixed (strong).
+N > 1 (under torchrun): KV heads sharded 8/N per GPU; every rank's decode
+kernels store their output heads into all ranks' buffers over NVLink (peer
+memory); total work is fixed (strong scaling).  After the timed region the
+gathered outputs are checked (bit-equal to an NCCL all-gather of the local
+outputs, and within the north-star tolerance of the CPU oracle) and the line
+carries "parity"; a mismatch exits non-zero.
+
+The default line also carries, after the headline's timed region, one
+compact object per other BASELINE config ("configs": cfg1, cfg3, cfg4,
+cfg5a, cfg5b) and the engine's per-layer call pattern ("per_layer"), each
+with its own timing, roofline fraction and clock record.
 
 Output: one JSON line on rank 0 (see the repository's build contract).
 """
 import argparse
+import ctypes
 import json
 import os
 import statistics
@@ -32,6 +42,15 @@ METRIC = "decode-attn KV-read GB/s (% of 8 TB/s) and tokens/s at 32K ctx, 1/2/4/
 QH, KVH, HD, CTX = 64, 8, 128, 32768
 EMBD = 4096  # model width: o_proj output (sf37.c:36)
 LAYERS = 48  # --layers overrides (profiling runs use a small stack)
+WORKLOADS = {
+    "decode": "cfg2: 48-layer decode step (append + GQA attention) at 32768 cached tokens, 64 Q / 8 KV heads, "
+              "d 128, batch 1",
+    "long": "cfg5a: 48-layer decode step at 131072 cached tokens, KV heads sharded across GPUs",
+    "hybrid": "cfg3: 48 layers, 12 full (il%4==0) + 36 sliding (window 512, 512-row ring), decode after a "
+              "65536-token prefix",
+}
+# north-star tolerance for attention outputs (elementwise: abs or rel)
+ATOL, RTOL = 2e-3, 1e-2
 
 
 def _peaks():
@@ -40,6 +59,13 @@ def _peaks():
         d = json.load(open(p))
         return float(d["hbm_gbs"]), "measured"
     return 6650.0, "fallback"
+
+
+def _tensor_peak():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        return float(json.load(open(p)).get("bf16_tflops_sustained", 1400.0)), "measured sustained"
+    return 1400.0, "fallback sustained"
 
 
 def _traffic_from_profiles(name):
@@ -58,7 +84,7 @@ def _traffic_from_profiles(name):
 
 
 class ClockSampler:
-    """nvidia-smi sampling during the timed region."""
+    """nvidia-smi sampling during a timed region."""
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
          "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
@@ -76,6 +102,7 @@ class ClockSampler:
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
+            time.sleep(0.3)  # let nvidia-smi start before the timed region
         except Exception:
             self.proc = None
         return self
@@ -91,6 +118,7 @@ class ClockSampler:
                 self.proc.wait(timeout=5)
             except Exception:
                 self.proc.kill()
+            self.proc = None
 
     def summary(self):
         sm, mx, reasons = [], None, set()
@@ -113,32 +141,72 @@ class ClockSampler:
                 "samples": len(sm)}
 
 
+def _dev():
+    import torch
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(dev)
+    return dev
+
+
+def _max_over_ranks(x, world, dev):
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], device=dev, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def _barrier(world, dev):
+    import torch
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+
+
+def decode_config(wl, world, prep=False, oproj=False, gather="peer"):
+    """The `config` object of a decode line; the reference arm prints the
+    same object for the same workload and N."""
+    return {"workload": WORKLOADS[wl], "layers": LAYERS,
+            "ctx": {"decode": CTX, "long": 131072, "hybrid": 65536}[wl],
+            "q_heads": QH, "kv_heads": KVH, "head_dim": HD, "kv_heads_per_gpu": KVH // world,
+            "qk_prep_fused": bool(prep), "oproj_q8_0": bool(oproj),
+            "parallelism": f"kv-head shard x{world}" + (
+                "" if world == 1 else " + row-parallel o_proj, partial sums reduced over peer memory" if oproj
+                else " + NCCL all-gather" if gather == "nccl"
+                else " + output gather by peer-memory stores from the decode kernels"),
+            "l2": "no flush needed: every step reads >= 3.4 GB of KV, far more than the 126 MB L2"}
+
+
 # ---------------------------------------------------------------- CPU legs
 _CPU_DATA = {}
 
 
-def cpu_reference_step_time(threads, layers_sample, rows):
-    """One decode step of `layers_sample` layers through the reference's own
-    CPU code (kv_cache_push + attention_decode + gate, oracle/_ref), spread
-    over `threads` threads (one layer per thread at a time).  Each layer has
-    its own fp32 cache holding f16-valued N(0,1) data.  Returns seconds."""
-    import ctypes
+def cpu_reference_step_time(threads, n_layers, rows):
+    """One decode step of `n_layers` layers through the reference's own CPU
+    code (kv_cache_push + attention_decode + gate, oracle/_ref), spread over
+    `threads` threads (contiguous blocks of layers per thread).  Each layer
+    has its own fp32 cache (the reference's only cache type) holding
+    f16-valued N(0,1) data.  Returns seconds."""
     import oracle
     R = oracle.ref()
     kd = KVH * HD
     cap = rows
-    key = (layers_sample, rows)
+    key = (n_layers, rows)
     if key not in _CPU_DATA:
+        _CPU_DATA.clear()
         rng = np.random.default_rng(0)
         k0 = rng.standard_normal((cap, kd), dtype=np.float32).astype(np.float16).astype(np.float32)
         v0 = rng.standard_normal((cap, kd), dtype=np.float32).astype(np.float16).astype(np.float32)
-        d = dict(k=[k0] + [k0.copy() for _ in range(layers_sample - 1)],
-                 v=[v0] + [v0.copy() for _ in range(layers_sample - 1)],
-                 q=[rng.standard_normal((QH, HD), dtype=np.float32) for _ in range(layers_sample)],
-                 g=[rng.standard_normal((QH,), dtype=np.float32) for _ in range(layers_sample)],
-                 o=[np.zeros((QH, HD), np.float32) for _ in range(layers_sample)],
-                 kn=[rng.standard_normal((kd,), dtype=np.float32) for _ in range(layers_sample)],
-                 vn=[rng.standard_normal((kd,), dtype=np.float32) for _ in range(layers_sample)])
+        d = dict(k=[k0] + [k0.copy() for _ in range(n_layers - 1)],
+                 v=[v0] + [v0.copy() for _ in range(n_layers - 1)],
+                 q=[rng.standard_normal((QH, HD), dtype=np.float32) for _ in range(n_layers)],
+                 g=[rng.standard_normal((QH,), dtype=np.float32) for _ in range(n_layers)],
+                 o=[np.zeros((QH, HD), np.float32) for _ in range(n_layers)],
+                 kn=[rng.standard_normal((kd,), dtype=np.float32) for _ in range(n_layers)],
+                 vn=[rng.standard_normal((kd,), dtype=np.float32) for _ in range(n_layers)])
 
         def parr(lst):
             a = (ctypes.c_void_p * len(lst))()
@@ -146,155 +214,55 @@ def cpu_reference_step_time(threads, layers_sample, rows):
                 a[i] = x.ctypes.data
             return a
         d["p"] = {n: parr(d[n]) for n in ("k", "v", "q", "g", "o", "kn", "vn")}
-        d["sliding"] = (ctypes.c_int * layers_sample)(*([0] * layers_sample))
+        d["sliding"] = (ctypes.c_int * n_layers)(*([0] * n_layers))
         _CPU_DATA[key] = d
     d = _CPU_DATA[key]
     p = d["p"]
     # cap-1 live rows; the push of this step fills the last row
-    n_live = (ctypes.c_uint32 * layers_sample)(*([cap - 1] * layers_sample))
+    n_live = (ctypes.c_uint32 * n_layers)(*([cap - 1] * n_layers))
     t0 = time.perf_counter()
     ok = R.sf37ref_decode_step_layers(p["k"], p["v"], n_live, cap, p["kn"], p["vn"], p["q"], p["g"],
-                                      p["o"], d["sliding"], QH, layers_sample, threads)
+                                      p["o"], d["sliding"], QH, n_layers, threads)
     dt = time.perf_counter() - t0
     assert ok
     return dt
 
 
-def _cpu_plan():
-    threads = os.cpu_count() or 1
-    sample_layers = max(1, min(LAYERS, threads, 16))
-    return min(threads, sample_layers), sample_layers
+def _cpu_layers(rows):
+    """All LAYERS layers if the host has the memory for their fp32 caches
+    (12.9 GB at config 2) with headroom, else the largest count that fits."""
+    need = rows * KVH * HD * 4 * 2
+    try:
+        import psutil
+        avail = psutil.virtual_memory().available
+    except Exception:
+        avail = 64 << 30
+    return max(1, min(LAYERS, int(avail * 0.6 // need)))
 
 
 def cpu_baseline(rows):
+    """The reference CPU decode step of all 48 layers, on all host threads,
+    timed directly (no extrapolation) when the host memory allows."""
     import oracle
     if not oracle.ref_available():
         return None
-    threads, sample_layers = _cpu_plan()
-    cpu_reference_step_time(threads, sample_layers, rows)  # warm (page-in)
-    dt = min(cpu_reference_step_time(threads, sample_layers, rows) for _ in range(3))
-    full = dt * LAYERS / sample_layers
-    return {"value": 1.0 / full, "unit": "tokens/s", "cores": threads,
-            "kind": "reference",
-            "sample": f"{sample_layers} of {LAYERS} layers x {rows} rows (one decode step through the "
-                      f"reference's own kv_cache_push+attention_decode+gate, fp32 cache holding f16 "
-                      f"values), extrapolated linearly to {LAYERS} layers",
-            "kv_read_GBps": sample_layers * rows * KVH * HD * 2 * 4 / dt / 1e9}
-
-
-def oproj_leg(dev, stream, op_arr, op_w, x, op_out, steps, peak):
-    """The o_proj kernel alone over all layers (one launch), timed with CUDA
-    events per launch; and the reference's own quantize + matvec kernels
-    (sf37_cuda_matvec_q8_0 of oracle/_ref/libsf37ref_cuda.so), one call per
-    layer, on the same weights and inputs."""
-    import torch
-    from sf37_b200 import kv
-    n_layers = op_w.shape[0]
-    wbytes = op_w.numel()
-    for _ in range(3):
-        kv.oproj(op_arr, QH * HD, EMBD, stream)
-    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(max(steps, 20))]
-    for a, b_ in evs:
-        a.record(stream)
-        kv.oproj(op_arr, QH * HD, EMBD, stream)
-        b_.record(stream)
-    torch.cuda.synchronize(dev)
-    ms = sum(a.elapsed_time(b_) for a, b_ in evs) / len(evs)
-    alg = wbytes + n_layers * (QH * HD * 4 + EMBD * 4)
-    res = {"kernel": "oproj_q8_0_kernel", "layers": n_layers, "in_dim": QH * HD, "out_dim": EMBD,
-           "launch_ms": ms, "algorithmic_bytes_per_launch": alg,
-           "roofline": {"bound": "hbm", "achieved": alg / (ms * 1e-3) / 1e9, "peak": peak, "unit": "GB/s",
-                        "frac": alg / (ms * 1e-3) / 1e9 / peak}}
-    try:
-        import oracle
-        if not oracle.ref_cuda_available():
-            raise RuntimeError("oracle/_ref/libsf37ref_cuda.so not built")
-        R = oracle.ref_cuda()
-        import ctypes
-        TP = ctypes.POINTER(oracle.RefTensor)
-        R.sf37_cuda_matvec_q8_0.restype = ctypes.c_int
-        R.sf37_cuda_matvec_q8_0.argtypes = [TP, TP, ctypes.c_uint64, ctypes.c_uint64, TP]
-        refout = torch.empty(EMBD, device=dev)
-
-        def rt(t):
-            return oracle.ref_tensor(t.data_ptr(), t.numel() * t.element_size())
-        ts = [(rt(refout), rt(op_w[l]), rt(x[l])) for l in range(n_layers)]
-        for o, w, xx in ts[:3]:
-            R.sf37_cuda_matvec_q8_0(o, w, QH * HD, EMBD, xx)
-        torch.cuda.synchronize(dev)
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-        reps = 5
-        for _ in range(reps):
-            for o, w, xx in ts:
-                if not R.sf37_cuda_matvec_q8_0(o, w, QH * HD, EMBD, xx):
-                    raise RuntimeError("reference matvec failed")
-        e1.record()
-        torch.cuda.synchronize(dev)
-        rms = e0.elapsed_time(e1) / reps
-        res["reference_kernels"] = {"ms_all_layers": rms, "GBps": alg / (rms * 1e-3) / 1e9,
-                                    "calls": f"{n_layers} x sf37_cuda_matvec_q8_0 (quantize + matvec kernels)"}
-    except Exception as e:
-        res["reference_kernels"] = {"unavailable": str(e)}
-    return res
-
-
-def reference_gpu_leg(dev, steps):
-    """Config 2 with fp32 caches, one call per layer through the reference's
-    own entry point sf37_cuda_attention_decode_heads_at: (a) the reference's
-    CUDA kernels (oracle/_ref/libsf37ref_cuda.so, sm_100a build of its
-    sources), (b) this library's drop-in of the same symbol.  Tokens/s of the
-    48 per-layer calls per step (attention only, fp32 KV = 12.9 GB)."""
-    import torch
-    import oracle
-    from sf37_b200 import kv
-    if not oracle.ref_cuda_available():
-        return None
-    R = oracle.ref_cuda()
-    cap = CTX + 1
-    kf = torch.empty(cap, KVH * HD, device=dev)
-    layers = []
-    for _ in range(LAYERS):
-        k = torch.empty(cap, KVH * HD, device=dev).normal_()
-        v = torch.empty(cap, KVH * HD, device=dev).normal_()
-        layers.append((k, v))
-    del kf
-    q = torch.randn(QH, HD, device=dev)
-    gate = torch.randn(QH, device=dev)
-    out = torch.empty(QH, HD, device=dev)
-
-    def rt(t):
-        return oracle.ref_tensor(t.data_ptr(), t.numel() * t.element_size())
-
-    def run(which, n):
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        for rep in range(2):
-            torch.cuda.synchronize(dev)
-            e0.record()
-            for _ in range(n):
-                for k, v in layers:
-                    if which == "ref":
-                        R.sf37_cuda_attention_decode_heads_at(rt(out), rt(q), rt(k), rt(v), rt(gate), CTX, cap,
-                                                              QH, KVH, HD, 0, 512)
-                    else:
-                        kv.attention_decode_heads_at(out, q, k, v, gate, CTX, cap, QH, KVH, HD, 0, 512)
-            e1.record()
-            torch.cuda.synchronize(dev)
-        return e0.elapsed_time(e1) / n
-
-    n = max(2, min(steps, 5))
-    ms_ref = run("ref", n)
-    ms_ours = run("ours", n)
-    b = LAYERS * cap * KVH * HD * 4 * 2
-    del layers
-    torch.cuda.empty_cache()
-    return {"what": "cfg2 attention, fp32 caches, 48 per-layer calls of sf37_cuda_attention_decode_heads_at",
-            "reference_kernels": {"tokens_per_s": 1000.0 / ms_ref, "kv_read_GBps": b / (ms_ref * 1e-3) / 1e9},
-            "dropin_f32": {"tokens_per_s": 1000.0 / ms_ours, "kv_read_GBps": b / (ms_ours * 1e-3) / 1e9}}
+    threads = os.cpu_count() or 1
+    n = _cpu_layers(rows)
+    cpu_reference_step_time(threads, n, rows)  # warm (page-in)
+    dt = min(cpu_reference_step_time(threads, n, rows) for _ in range(2))
+    _CPU_DATA.clear()
+    full = dt * LAYERS / n
+    return {"value": 1.0 / full, "unit": "tokens/s", "cores": threads, "kind": "reference",
+            "sample": (f"one whole decode step, {n} layers x {rows} rows" if n == LAYERS else
+                       f"{n} of {LAYERS} layers x {rows} rows, scaled to {LAYERS} layers") +
+                      " through the reference's own kv_cache_push + attention_decode + gate (fp32 cache "
+                      "holding f16 values); best of 2 after one warm step",
+            "kv_read_GBps": n * rows * KVH * HD * 2 * 4 / dt / 1e9}
 
 
 def run_reference(args, rank, world):
-    """--impl reference: the reference's own CPU implementation of the path."""
+    """--impl reference: the reference's own CPU implementation of the path
+    (config 2), every step a whole 48-layer decode step on the host cores."""
     if rank != 0:
         return
     import oracle
@@ -302,41 +270,108 @@ def run_reference(args, rank, world):
         print(json.dumps({"impl": "reference",
                           "unavailable": "oracle/_ref/libsf37ref.so was not built (needs the reference tree)"}))
         return
-    threads, sample_layers = _cpu_plan()
+    threads = os.cpu_count() or 1
     rows = CTX + 1
+    n = _cpu_layers(rows)
     for _ in range(args.warmup):
-        cpu_reference_step_time(threads, sample_layers, rows)
-    ts = [cpu_reference_step_time(threads, sample_layers, rows) for _ in range(args.steps)]
-    step = sum(ts) / len(ts) * LAYERS / sample_layers
+        cpu_reference_step_time(threads, n, rows)
+    ts = [cpu_reference_step_time(threads, n, rows) for _ in range(args.steps)]
+    step = sum(ts) / len(ts) * LAYERS / n
     val = 1.0 / step
+    sample = (f"every step is a whole decode step: {LAYERS} layers x {rows} rows" if n == LAYERS else
+              f"{n} of {LAYERS} layers per step (host memory), scaled to {LAYERS}")
     line = {"impl": "reference", "metric": METRIC, "value": val, "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": step * 1e3,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic N(0,1) f16-valued K/V, fp32 query (seeded)",
-            "config": {"workload": "cfg2: 48-layer decode step at 32768 cached tokens, 64 Q / 8 KV "
-                                   "heads, d 128, batch 1", "layers": LAYERS, "ctx": CTX},
-            "cpu_baseline": {"value": val, "unit": "tokens/s", "cores": threads,
-                             "kind": "reference",
-                             "sample": f"{sample_layers} of {LAYERS} layers per step, extrapolated"},
-            "e2e": {"value": val, "unit": "tokens/s", "h2d_bytes_per_step": 0,
-                    "d2h_bytes_per_step": 0}}
+            "data": "synthetic N(0,1) f16-valued K/V in fp32 caches (the reference's only cache type), fp32 q",
+            "config": decode_config("decode", world),
+            "cpu_baseline": {"value": val, "unit": "tokens/s", "cores": threads, "kind": "reference",
+                             "sample": sample + " through kv_cache_push + attention_decode + gate "
+                                                "(sf37.c:2054-2101, 2235-2239), layers spread over the threads"},
+            "e2e": {"value": val, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
 
-# ---------------------------------------------------------------- GPU leg
-def run_ours(args, rank, world):
+# ---------------------------------------------------------------- parity
+def _host_f16_bits(t):
+    return t.cpu().view(__import__("torch").int16).numpy().view(np.uint16)
+
+
+def decode_parity(rank, world, dev, stream, kc, vc, caps, sliding, pos, qh_l, kvh_l, pg, gen):
+    """After the timed region: one more decode step (no append) at `pos`
+    with fresh q / gate, twice (both halves of the peer buffer).  Checks
+      * every rank's gathered outputs (peer-memory stores from the decode
+        kernels) bit-equal an NCCL all-gather of the ranks' local outputs;
+      * each rank's local heads of layers 0, 1 and LAYERS-1 against the CPU
+        oracle (the reference's attention restated) on the cache contents,
+        within the north-star tolerance (2e-3 abs or 1e-2 rel).
+    Returns {"max_abs", "bad", "gather_equal", "ok", ...} reduced over ranks."""
+    import torch
+    import torch.distributed as dist
+    import oracle
+    from sf37_b200 import kv
+    n_layers = len(kc)
+    check_layers = sorted({0, min(1, n_layers - 1), n_layers - 1})
+    worst, bad, gather_bad, steps_checked = 0.0, 0, 0, 0
+    for rep in range(2):
+        q = torch.randn(n_layers, qh_l, HD, device=dev, generator=gen)
+        gate = torch.randn(n_layers, qh_l, device=dev, generator=gen)
+        out = torch.full((n_layers, qh_l, HD), float("nan"), device=dev)
+        desc = kv.decode_layers_desc([dict(k_cache=kc[l], v_cache=vc[l], cap=caps[l], sliding=sliding[l],
+                                           window=512, pos=pos, q=q[l], gate=gate[l], out=out[l])
+                                      for l in range(n_layers)])
+        if pg is not None:
+            pg.step(desc, kv.F16, stream)
+            peer = pg.gathered[pg.epoch & 1].clone()
+        else:
+            kv.decode(desc, qh_l, kvh_l, HD, kv.F16, stream)
+        if world > 1:
+            ref = torch.empty(world, n_layers, qh_l, HD, device=dev)
+            dist.all_gather_into_tensor(ref, out)
+            if pg is not None and not torch.equal(peer, ref):
+                gather_bad += 1
+        torch.cuda.synchronize(dev)
+        got = out.cpu().numpy()
+        for l in check_layers:
+            want = oracle.attention_decode_at(q[l].cpu().numpy(), _host_f16_bits(kc[l]), _host_f16_bits(vc[l]),
+                                              gate[l].cpu().numpy(), pos, caps[l], qh_l, kvh_l, HD,
+                                              int(sliding[l]), 512)
+            diff = np.abs(got[l] - want)
+            worst = max(worst, float(diff.max()))
+            bad += int(((diff > ATOL) & (diff > RTOL * np.abs(want))).sum() + (~np.isfinite(got[l])).sum())
+        steps_checked += 1
+    if pg is not None and kv.device_error(1):
+        gather_bad += 1000
+    t = torch.tensor([worst, float(bad), float(gather_bad)], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    worst, bad, gather_bad = float(t[0]), int(t[1]), int(t[2])
+    return {"max_abs": worst, "bad_elements": bad,
+            "gather_equal": (gather_bad == 0) if world > 1 else None,
+            "checked": f"{steps_checked} steps at position {pos}; layers {check_layers} of every rank's heads vs "
+                       f"the CPU oracle (atol {ATOL} or rtol {RTOL})" +
+                       ("; gathered [world][layers][heads][d] bit-equal to an NCCL all-gather of the local "
+                        "outputs" if world > 1 and pg is not None else ""),
+            "ok": bad == 0 and gather_bad == 0}
+
+
+# ---------------------------------------------------------------- decode legs
+def decode_leg(args, rank, world, wl, headline):
+    """Config 2 (decode), 3 (hybrid) or 5a (long).  Returns the line (on
+    every rank; rank 0 prints)."""
     import torch
     import torch.distributed as dist
     from sf37_b200 import kv
 
-    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
-    torch.cuda.set_device(dev)
+    dev = _dev()
     assert KVH % world == 0, "world size must divide the 8 KV heads"
     kvh_l = KVH // world
     qh_l = QH // world
     kd = kvh_l * HD
     steps, warm = args.steps, args.warmup
-    wl = args.workload
+    oproj_on = headline and args.oproj
+    prep_on = headline and args.prep
+    gather = args.gather
     ctx = {"decode": CTX, "long": 131072, "hybrid": 65536}[wl]
     full_cap = ctx + warm + steps + 16
     # hybrid (config 3): layers il % 4 != 0 are sliding-window layers with a
@@ -377,7 +412,7 @@ def run_ours(args, rank, world):
     # output head straight into all ranks' buffers over NVLink (PeerGather);
     # --gather nccl runs the decode and then an NCCL all-gather instead.
     pg = None
-    if world > 1 and args.gather == "peer" and not args.oproj:
+    if world > 1 and gather == "peer" and not oproj_on:
         from sf37_b200.shard import PeerGather, ShardPlan
         pg = PeerGather(ShardPlan(world, rank, KVH, QH, HD), LAYERS)
 
@@ -385,7 +420,7 @@ def run_ours(args, rank, world):
     # the decode kernel (full layers rotary 64 / theta 5e6 / llama3, sliding
     # layers 128 / 1e4, sf37.c:1983-1993).
     prep_arr = None
-    if args.prep:
+    if prep_on:
         qw = torch.randn(LAYERS, HD, device=dev, generator=g).mul_(0.3).to(torch.bfloat16)
         kw = torch.randn(LAYERS, HD, device=dev, generator=g).mul_(0.3).to(torch.bfloat16)
         prep_arr = kv.qk_prep_desc([
@@ -398,9 +433,9 @@ def run_ours(args, rank, world):
     # columns of its own heads (1/N of each row), multiplies its heads, and
     # the partial outputs are summed across ranks over peer memory
     # (PeerReduce); the heads themselves are never gathered.
-    op_arr = pr = None
+    op_arr = pr = op_w = op_out = None
     in_local = QH * HD // world
-    if args.oproj:
+    if oproj_on:
         from sf37_b200 import _lib
         op_w = torch.randint(0, 256, (LAYERS, EMBD, (in_local // 32) * 34), dtype=torch.uint8, device=dev,
                              generator=g)
@@ -433,29 +468,20 @@ def run_ours(args, rank, world):
         if world > 1:
             dist.all_gather_into_tensor(gathered, out)
 
-    def barrier():
-        if world > 1:
-            dist.barrier()
-        torch.cuda.synchronize(dev)
-
     for i in range(warm):
         step(i)
-    barrier()
+    _barrier(world, dev)
     n0 = kv.launch_count()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     clk = ClockSampler(dev.index).__enter__()
-    time.sleep(0.3)  # let nvidia-smi start before the timed region
     ev0.record(stream)
     for i in range(warm, warm + steps):
         step(i)
     ev1.record(stream)
-    barrier()
+    _barrier(world, dev)
     launches = kv.launch_count() - n0
-    ms = ev0.elapsed_time(ev1) / steps
-    if world > 1:
-        t = torch.tensor([ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+    ms = _max_over_ranks(ev0.elapsed_time(ev1) / steps, world, dev)
+
     def rows_at(pos, l):
         return min(pos + 1, 512) if sliding[l] else pos + 1
     kv_bytes_step = sum(rows_at(ctx + i, l) for i in range(warm, warm + steps) for l in range(LAYERS)) \
@@ -467,7 +493,7 @@ def run_ours(args, rank, world):
         if rank == 0:
             print(json.dumps({"quick": True, "layers": LAYERS, "ms_per_step": ms, "value": tok_s,
                               "gpu_launches": launches}), flush=True)
-        return
+        return None
 
     # Roofline leg: the attention kernel alone (no append), one launch per
     # call, CUDA events on the launching stream around each launch.
@@ -484,7 +510,7 @@ def run_ours(args, rank, world):
         kv.decode(att_desc, qh_l, kvh_l, HD, kv.F16, stream)
         b.record(stream)
     torch.cuda.synchronize(dev)
-    att_ms = sum(a.elapsed_time(b) for a, b in evs) / len(evs)
+    att_ms = _max_over_ranks(sum(a.elapsed_time(b) for a, b in evs) / len(evs), world, dev)
     att_bytes = sum(rows_at(ctx + warm + steps - 1, l) * kd * 2 * 2 + qh_l * HD * 4 * 2 + qh_l * 4
                     for l in range(LAYERS))
     peak, peak_kind = _peaks()
@@ -499,7 +525,7 @@ def run_ours(args, rank, world):
 
     # End-to-end leg through the C ABI with host buffers: every step copies its
     # inputs (q, gate, new K/V rows) in from pinned host memory and its
-    # outputs back out.  The copies run on a side stream with double-buffered
+    # outputs back out.  The copies run on side streams with double-buffered
     # device inputs/outputs, so step i's copies overlap steps i-1 / i+1.
     h_q = torch.empty_like(q, device="cpu").pin_memory()
     h_gate = torch.empty_like(gate, device="cpu").pin_memory()
@@ -574,7 +600,7 @@ def run_ours(args, rank, world):
 
     for i in range(3):
         e2e_step(i)
-    barrier()
+    _barrier(world, dev)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     for i in range(steps):
@@ -582,12 +608,19 @@ def run_ours(args, rank, world):
     stream.wait_stream(copy_s)
     stream.wait_stream(out_s)
     e1.record(stream)
-    barrier()
-    e2e_ms = e0.elapsed_time(e1) / steps
-    if world > 1:
-        t = torch.tensor([e2e_ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms = float(t.item())
+    _barrier(world, dev)
+    e2e_ms = _max_over_ranks(e0.elapsed_time(e1) / steps, world, dev)
+    clk.__exit__()
+
+    # Parity of the gathered (or reduced) outputs, after the timed regions.
+    parity = None
+    if not prep_on and not oproj_on:
+        pgen = torch.Generator(device=dev)
+        pgen.manual_seed(4321 + rank)
+        parity = decode_parity(rank, world, dev, stream, kc, vc, caps, sliding, ctx + warm + steps + 2,
+                               qh_l, kvh_l, pg, pgen)
+    elif pr is not None:
+        parity = oproj_reduce_parity(world, dev, stream, pr, op_arr, op_w, out, op_out, in_local)
     for peer in (pg, pr):
         if peer is not None:
             if kv.device_error(1):
@@ -596,35 +629,13 @@ def run_ours(args, rank, world):
             torch.cuda.synchronize(dev)
             peer.close()
 
-    ref_gpu = None
-    if world == 1 and wl == "decode" and not args.no_ref_gpu:
-        ref_gpu = reference_gpu_leg(dev, steps)
-    clk.__exit__()
-    if rank != 0:
-        return
-    cpu = cpu_baseline(CTX + 1) if (world == 1 and not args.no_cpu and wl == "decode") else None
-    clocks = clk.summary()
     line = {
         "metric": METRIC, "value": tok_s, "unit": "tokens/s", "n_gpus": world, "steps": steps,
         "warmup": warm, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "f16",
         "data": "synthetic: N(0,1) f16 K/V caches and fp32 q/gate/new rows from torch's seeded CUDA "
                 "generator",
-        "config": {"workload": {"decode": "cfg2: 48-layer decode step (append + GQA attention) at 32768 "
-                                          "cached tokens, 64 Q / 8 KV heads, d 128, batch 1",
-                                "long": "cfg5a: 48-layer decode step at 131072 cached tokens, KV heads "
-                                        "sharded across GPUs",
-                                "hybrid": "cfg3: 48 layers, 12 full (il%4==0) + 36 sliding (window 512, "
-                                          "512-row ring), decode after a 65536-token prefix"}[wl],
-                   "layers": LAYERS, "ctx": ctx, "q_heads": QH, "kv_heads": KVH, "head_dim": HD,
-                   "kv_heads_per_gpu": kvh_l,
-                   "qk_prep_fused": bool(args.prep),
-                   "oproj_q8_0": bool(args.oproj),
-                   "parallelism": f"kv-head shard x{world}" + (
-                       "" if world == 1 else " + row-parallel o_proj, partial sums reduced over peer memory"
-                       if pr is not None else " + NCCL all-gather" if pg is None
-                       else " + output gather by peer-memory stores from the decode kernels"),
-                   "l2": "no flush needed: 6.4 GB of KV per step >> 126 MB L2"},
+        "config": decode_config(wl, world, prep_on, oproj_on, gather),
         "kv_read_GBps": kv_bytes_step / (ms * 1e-3) / 1e9,
         "kv_read_frac_of_8TBps": kv_bytes_step / (ms * 1e-3) / 8e12,
         "roofline": {"bound": "hbm", "kernel": "decode_f16_pipe_kernel", "achieved": achieved,
@@ -634,26 +645,224 @@ def run_ours(args, rank, world):
         "e2e": {"value": 1000.0 / e2e_ms, "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
         "gpu_launches": launches,
-        "clocks": clocks,
+        "clocks": clk.summary(),
     }
-    if cpu:
-        line["cpu_baseline"] = cpu
-    if ref_gpu:
-        line["reference_gpu"] = ref_gpu
+    if parity is not None:
+        line["parity"] = parity
     if op_line:
         line["oproj"] = op_line
-    print(json.dumps(line), flush=True)
+    del kc, vc, all_desc, e2e_desc, bufs
+    torch.cuda.empty_cache()
+    return line
 
 
-def run_cfg1(args, rank, world):
-    """BASELINE config 1: one layer, 2048 cached f16 rows + the appended row
-    at position 2048, 64 Q / 8 KV heads, d 128.  One step = one
-    sf37kv_decode (append + attention).  The 8.4 MB of K/V would sit in the
-    126 MB L2, so steps rotate over 16 independent cache copies (134 MB)."""
+def oproj_reduce_parity(world, dev, stream, pr, op_arr, op_w, out, op_out, in_local):
+    """Row-parallel o_proj: the peer-memory reduce of the ranks' partial
+    products equals an NCCL all-reduce of the same partials (computed by the
+    plain sf37kv_oproj_q8_0 on this rank's column slice), up to the float
+    summation order."""
+    import torch
+    import torch.distributed as dist
+    from sf37_b200 import _lib, kv
+    out.normal_()
+    pr.step(op_arr, in_local, (in_local // 32) * 34, op_out, stream)
+    got = op_out.clone()
+    part = torch.empty_like(op_out)
+    arr = (_lib.OprojLayer * LAYERS)(*[_lib.OprojLayer(op_w[l].data_ptr(), out[l].data_ptr(), part[l].data_ptr())
+                                       for l in range(LAYERS)])
+    kv.oproj(arr, in_local, EMBD, stream)
+    dist.all_reduce(part)
+    scale = float(part.abs().max())
+    err = float((got - part).abs().max())
+    t = torch.tensor([err / max(scale, 1e-30)], device=dev, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    rel = float(t.item())
+    return {"max_rel_to_max": rel, "checked": "peer-memory reduce vs NCCL all-reduce of the ranks' partials",
+            "ok": rel <= 1e-5}
+
+
+def oproj_leg(dev, stream, op_arr, op_w, x, op_out, steps, peak):
+    """The o_proj kernel alone over all layers (one launch), timed with CUDA
+    events per launch; and the reference's own quantize + matvec kernels
+    (sf37_cuda_matvec_q8_0 of oracle/_ref/libsf37ref_cuda.so), one call per
+    layer, on the same weights and inputs."""
     import torch
     from sf37_b200 import kv
-    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
-    torch.cuda.set_device(dev)
+    n_layers = op_w.shape[0]
+    wbytes = op_w.numel()
+    for _ in range(3):
+        kv.oproj(op_arr, QH * HD, EMBD, stream)
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(max(steps, 20))]
+    for a, b_ in evs:
+        a.record(stream)
+        kv.oproj(op_arr, QH * HD, EMBD, stream)
+        b_.record(stream)
+    torch.cuda.synchronize(dev)
+    ms = sum(a.elapsed_time(b_) for a, b_ in evs) / len(evs)
+    alg = wbytes + n_layers * (QH * HD * 4 + EMBD * 4)
+    res = {"kernel": "oproj_q8_0_kernel", "layers": n_layers, "in_dim": QH * HD, "out_dim": EMBD,
+           "launch_ms": ms, "algorithmic_bytes_per_launch": alg,
+           "roofline": {"bound": "hbm", "achieved": alg / (ms * 1e-3) / 1e9, "peak": peak, "unit": "GB/s",
+                        "frac": alg / (ms * 1e-3) / 1e9 / peak}}
+    try:
+        import oracle
+        if not oracle.ref_cuda_available():
+            raise RuntimeError("oracle/_ref/libsf37ref_cuda.so not built")
+        R = oracle.ref_cuda()
+        TP = ctypes.POINTER(oracle.RefTensor)
+        R.sf37_cuda_matvec_q8_0.restype = ctypes.c_int
+        R.sf37_cuda_matvec_q8_0.argtypes = [TP, TP, ctypes.c_uint64, ctypes.c_uint64, TP]
+        refout = torch.empty(EMBD, device=dev)
+
+        def rt(t):
+            return oracle.ref_tensor(t.data_ptr(), t.numel() * t.element_size())
+        ts = [(rt(refout), rt(op_w[l]), rt(x[l])) for l in range(n_layers)]
+        for o, w, xx in ts[:3]:
+            R.sf37_cuda_matvec_q8_0(o, w, QH * HD, EMBD, xx)
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        reps = 5
+        for _ in range(reps):
+            for o, w, xx in ts:
+                if not R.sf37_cuda_matvec_q8_0(o, w, QH * HD, EMBD, xx):
+                    raise RuntimeError("reference matvec failed")
+        e1.record()
+        torch.cuda.synchronize(dev)
+        rms = e0.elapsed_time(e1) / reps
+        res["reference_kernels"] = {"ms_all_layers": rms, "GBps": alg / (rms * 1e-3) / 1e9,
+                                    "calls": f"{n_layers} x sf37_cuda_matvec_q8_0 (quantize + matvec kernels)"}
+    except Exception as e:
+        res["reference_kernels"] = {"unavailable": str(e)}
+    return res
+
+
+def reference_gpu_leg(dev, steps):
+    """Config 2 with fp32 caches, one call per layer through the reference's
+    own entry point sf37_cuda_attention_decode_heads_at: (a) the reference's
+    CUDA kernels (oracle/_ref/libsf37ref_cuda.so, sm_100a build of its
+    sources), (b) this library's drop-in of the same symbol.  Tokens/s of the
+    48 per-layer calls per step (attention only, fp32 KV = 12.9 GB)."""
+    import torch
+    import oracle
+    from sf37_b200 import kv
+    if not oracle.ref_cuda_available():
+        return None
+    R = oracle.ref_cuda()
+    cap = CTX + 1
+    layers = []
+    for _ in range(LAYERS):
+        k = torch.empty(cap, KVH * HD, device=dev).normal_()
+        v = torch.empty(cap, KVH * HD, device=dev).normal_()
+        layers.append((k, v))
+    q = torch.randn(QH, HD, device=dev)
+    gate = torch.randn(QH, device=dev)
+    out = torch.empty(QH, HD, device=dev)
+
+    def rt(t):
+        return oracle.ref_tensor(t.data_ptr(), t.numel() * t.element_size())
+
+    def run(which, n):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        for rep in range(2):
+            torch.cuda.synchronize(dev)
+            e0.record()
+            for _ in range(n):
+                for k, v in layers:
+                    if which == "ref":
+                        R.sf37_cuda_attention_decode_heads_at(rt(out), rt(q), rt(k), rt(v), rt(gate), CTX, cap,
+                                                              QH, KVH, HD, 0, 512)
+                    else:
+                        kv.attention_decode_heads_at(out, q, k, v, gate, CTX, cap, QH, KVH, HD, 0, 512)
+            e1.record()
+            torch.cuda.synchronize(dev)
+        return e0.elapsed_time(e1) / n
+
+    n = max(2, min(steps, 5))
+    ms_ref = run("ref", n)
+    ms_ours = run("ours", n)
+    b = LAYERS * cap * KVH * HD * 4 * 2
+    peak, _ = _peaks()
+    del layers
+    torch.cuda.empty_cache()
+    return {"what": "cfg2 attention, fp32 caches, 48 per-layer calls of sf37_cuda_attention_decode_heads_at "
+                    "issued from the host (no graph), as sf37.c issues them",
+            "reference_kernels": {"tokens_per_s": 1000.0 / ms_ref, "kv_read_GBps": b / (ms_ref * 1e-3) / 1e9,
+                                  "frac": b / (ms_ref * 1e-3) / 1e9 / peak},
+            "dropin_f32": {"tokens_per_s": 1000.0 / ms_ours, "kv_read_GBps": b / (ms_ours * 1e-3) / 1e9,
+                           "frac": b / (ms_ours * 1e-3) / 1e9 / peak}}
+
+
+def per_layer_leg(args, dev):
+    """The engine's call pattern: in sf37.c each layer's q depends on the
+    previous layer's output, so a decode step is 48 SEQUENTIAL single-layer
+    attention calls (sf37.c:3285-3437), not one batched launch.  Config 2
+    caches (32768 + 1 rows), one step = 48 calls, each appending its row
+    and attending over 32769 rows.  Timed as CUDA-graph replays of the 48
+    calls (the reference engine captures its decode in a CUDA graph) for f16
+    caches (sf37kv_decode) and fp32 caches (the drop-in's kernel)."""
+    import torch
+    from sf37_b200 import kv
+    cap = CTX + 1
+    pos = CTX
+    peak, kind = _peaks()
+    res = {"what": "48 sequential single-layer decode calls per step (append + attention over 32769 rows), "
+                   "replayed from a CUDA graph"}
+    s = torch.cuda.Stream(dev)
+    for name, dt, tdt in (("f16", kv.F16, torch.float16), ("f32", kv.F32, torch.float32)):
+        g = torch.Generator(device=dev)
+        g.manual_seed(55)
+        ks = [torch.randn(cap, KVH * HD, device=dev, generator=g).to(tdt) for _ in range(LAYERS)]
+        vs = [torch.randn(cap, KVH * HD, device=dev, generator=g).to(tdt) for _ in range(LAYERS)]
+        q = torch.randn(LAYERS, QH, HD, device=dev, generator=g)
+        gate = torch.randn(LAYERS, QH, device=dev, generator=g)
+        kn = torch.randn(LAYERS, KVH * HD, device=dev, generator=g)
+        vn = torch.randn(LAYERS, KVH * HD, device=dev, generator=g)
+        out = torch.empty(LAYERS, QH, HD, device=dev)
+        descs = [kv.decode_layers_desc([dict(k_cache=ks[l], v_cache=vs[l], cap=cap, pos=pos, q=q[l], gate=gate[l],
+                                             out=out[l], k_new=kn[l], v_new=vn[l])]) for l in range(LAYERS)]
+        with torch.cuda.stream(s):
+            for _ in range(3):
+                for d in descs:
+                    kv.decode(d, QH, KVH, HD, dt, s)
+        torch.cuda.synchronize(dev)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=s):
+            for d in descs:
+                kv.decode(d, QH, KVH, HD, dt, s)
+        for _ in range(3):
+            graph.replay()
+        torch.cuda.synchronize(dev)
+        n = max(args.steps, 20)
+        clk = ClockSampler(dev.index).__enter__()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(s)
+        with torch.cuda.stream(s):
+            for _ in range(n):
+                graph.replay()
+        e1.record(s)
+        torch.cuda.synchronize(dev)
+        clk.__exit__()
+        ms = e0.elapsed_time(e1) / n
+        alg = LAYERS * (cap * KVH * HD * 2 * (2 if dt == kv.F16 else 4) + QH * HD * 8 + QH * 4)
+        ach = alg / (ms * 1e-3) / 1e9
+        res[name] = {"tokens_per_s": 1000.0 / ms, "ms_per_step": ms, "us_per_layer_call": ms * 1e3 / LAYERS,
+                     "roofline": {"bound": "hbm", "achieved": ach, "peak": peak, "peak_kind": kind, "unit": "GB/s",
+                                  "frac": ach / peak, "algorithmic_bytes_per_step": alg},
+                     "clocks": clk.summary()}
+        del ks, vs, graph, descs
+        torch.cuda.empty_cache()
+    return res
+
+
+def cfg1_leg(args, dev):
+    """BASELINE config 1: one layer, 2048 cached f16 rows + the appended row
+    at position 2048, 64 Q / 8 KV heads, d 128.  One step = one
+    sf37kv_decode (append + attention, one launch).  The 8.4 MB of K/V would
+    sit in the 126 MB L2, so steps rotate over 16 independent cache copies
+    (134 MB); the rotation is captured once in a CUDA graph."""
+    import torch
+    from sf37_b200 import kv
     cap, ncopy = 2049, 16
     g = torch.Generator(device=dev)
     g.manual_seed(3)
@@ -668,13 +877,11 @@ def run_cfg1(args, rank, world):
         out = torch.empty(QH, HD, device=dev)
         copies.append((kv.decode_layers_desc([dict(k_cache=k, v_cache=v, cap=cap, pos=2048, q=q, gate=gate,
                                                    out=out, k_new=kn, v_new=vn)]), k, v, q, gate, kn, vn, out))
-    stream = torch.cuda.current_stream(dev)
-    for i in range(args.warmup * ncopy):
-        kv.decode(copies[i % ncopy][0], QH, KVH, HD, kv.F16, stream)
-    torch.cuda.synchronize(dev)
-    # The rotation over the 16 copies is captured once in a CUDA graph (the
-    # steps are microseconds long; host launch latency is not the path's).
     gs = torch.cuda.Stream(dev)
+    with torch.cuda.stream(gs):
+        for i in range(args.warmup * ncopy):
+            kv.decode(copies[i % ncopy][0], QH, KVH, HD, kv.F16, gs)
+    torch.cuda.synchronize(dev)
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph, stream=gs):
         for i in range(ncopy):
@@ -682,17 +889,17 @@ def run_cfg1(args, rank, world):
     for _ in range(3):
         graph.replay()
     torch.cuda.synchronize(dev)
-    launches = 2 * args.steps * ncopy  # append + attention per step, replayed from the graph
+    reps = max(args.steps, 50)
+    clk = ClockSampler(dev.index).__enter__()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(gs)
     with torch.cuda.stream(gs):
-        for _ in range(args.steps):
+        for _ in range(reps):
             graph.replay()
     e1.record(gs)
     torch.cuda.synchronize(dev)
-    us = e0.elapsed_time(e1) * 1e3 / (args.steps * ncopy)
-    if rank != 0:
-        return
+    clk.__exit__()
+    us = e0.elapsed_time(e1) * 1e3 / (reps * ncopy)
     cpu = None
     import oracle
     if oracle.ref_available() and not args.no_cpu:
@@ -708,35 +915,95 @@ def run_cfg1(args, rank, world):
             n = oracle.ref_kv_cache_push(kc, vc, cap, 2048, k_new[None], v_new[None])
             oracle.ref_attention_decode(q, kc, vc, n, cap, QH, 0, gate)
             ts.append(time.perf_counter() - t0)
-        cpu = {"value": 1e6 / (min(ts) * 1e6), "unit": "steps/s", "cores": 1, "kind": "reference",
+        cpu = {"us_per_step": min(ts) * 1e6, "cores": 1, "kind": "reference",
                "sample": "one config-1 step (kv_cache_push + attention_decode + gate), best of 5"}
-    kvb = cap * KVH * HD * 2 * 2
+    alg = cap * KVH * HD * 2 * 2 + QH * HD * 8 + QH * 4 + KVH * HD * 8
     peak, kind = _peaks()
-    line = {"metric": "config-1 decode step (1 layer, 2049 rows)", "value": 1e6 / us, "unit": "steps/s",
-            "n_gpus": world, "steps": args.steps * ncopy, "warmup": args.warmup, "ms_per_step": us / 1e3,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
-            "data": "synthetic N(0,1)", "config": {"workload": "cfg1", "rows": cap,
-                                                   "l2": "16 rotating cache copies (134 MB > 126 MB L2)"},
-            "kv_read_GBps": kvb / (us * 1e-6) / 1e9,
-            "roofline": {"bound": "hbm", "kernel": "append + decode_f16_pipe_kernel", "achieved": kvb / (us * 1e-6) / 1e9,
-                         "peak": peak, "peak_kind": kind, "unit": "GB/s", "frac": kvb / (us * 1e-6) / 1e9 / peak},
-            "gpu_launches": launches}
-    if cpu:
-        line["cpu_baseline"] = cpu
-    print(json.dumps(line), flush=True)
+    ach = alg / (us * 1e-6) / 1e9
+    del copies, graph
+    torch.cuda.empty_cache()
+    return {"workload": "cfg1: 1 layer, 2048 cached rows + 1 appended, one sf37kv_decode per step",
+            "us_per_step": us, "steps_per_s": 1e6 / us, "launches_per_step": 1,
+            "l2": "16 rotating cache copies (134 MB > 126 MB L2), CUDA-graph replay",
+            "roofline": {"bound": "hbm", "kernel": "decode_f16_pipe_kernel", "achieved": ach, "peak": peak,
+                         "peak_kind": kind, "unit": "GB/s", "frac": ach / peak, "algorithmic_bytes_per_step": alg},
+            "cpu_baseline": cpu, "clocks": clk.summary()}
 
 
-def run_snapshot(args, rank, world):
+def prefill_leg(args, rank, world, dev, steps):
+    """BASELINE config 4: per layer, append an 8192-token chunk onto a
+    24576-token f16 prefix and run causal chunk attention (bf16 queries,
+    64 Q / 8 KV heads, d 128); one step = all layers.  Tensor-core bound."""
+    import torch
+    from sf37_b200 import kv
+    kvh_l, qh_l = KVH // world, QH // world
+    kd = kvh_l * HD
+    prefix, chunk, cap = 24576, 8192, 32768
+    g = torch.Generator(device=dev)
+    g.manual_seed(99 + rank)
+    kc = [torch.randn(cap, kd, device=dev, generator=g).half() for _ in range(LAYERS)]
+    vc = [torch.randn(cap, kd, device=dev, generator=g).half() for _ in range(LAYERS)]
+    kn = torch.randn(chunk, kd, device=dev, generator=g)
+    vn = torch.randn(chunk, kd, device=dev, generator=g)
+    q = torch.randn(chunk, qh_l, HD, device=dev, generator=g).to(torch.bfloat16)
+    gate = torch.randn(chunk, qh_l, device=dev, generator=g)
+    out = torch.empty(chunk, qh_l, HD, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        for l in range(LAYERS):
+            kv.append([dict(k_cache=kc[l], v_cache=vc[l], cap=cap, pos0=prefix, n_tok=chunk, k=kn, v=vn)],
+                      kd, kv.F16, stream)
+            kv.prefill(kc[l], vc[l], cap, q, gate, out, prefix, chunk, qh_l, kvh_l, HD, kv.F16,
+                       stream=stream)
+
+    for _ in range(args.warmup):
+        step()
+    _barrier(world, dev)
+    n0 = kv.launch_count()
+    clk = ClockSampler(dev.index).__enter__()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        step()
+    e1.record(stream)
+    _barrier(world, dev)
+    ms = _max_over_ranks(e0.elapsed_time(e1) / steps, world, dev)
+    launches = kv.launch_count() - n0
+    # attention kernel alone, CUDA events per launch
+    evs = []
+    for _ in range(16):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        kv.prefill(kc[0], vc[0], cap, q, gate, out, prefix, chunk, qh_l, kvh_l, HD, kv.F16, stream=stream)
+        b.record(stream)
+        evs.append((a, b))
+    torch.cuda.synchronize(dev)
+    clk.__exit__()
+    att_ms = _max_over_ranks(sum(a.elapsed_time(b) for a, b in evs) / len(evs), world, dev)
+    pairs = chunk * prefix + chunk * (chunk + 1) // 2
+    flops_layer = 4.0 * HD * pairs * qh_l
+    peak, kind = _tensor_peak()
+    ach = flops_layer / (att_ms * 1e-3) / 1e12
+    del kc, vc
+    torch.cuda.empty_cache()
+    return {"workload": "cfg4: 8192-token chunk on a 24576-token prefix, 48 layers (append + causal chunk "
+                        "attention per layer), f16 K/V, bf16 q, f32 accumulate",
+            "tokens_per_s": chunk / (ms * 1e-3), "ms_per_step": ms, "steps": steps, "gpu_launches": launches,
+            "roofline": {"bound": "tensor", "kernel": "prefill_tc05_kernel", "achieved": ach, "peak": peak,
+                         "peak_kind": kind, "unit": "TFLOP/s", "frac": ach / peak, "launch_ms": att_ms,
+                         "algorithmic_flops_per_launch": flops_layer},
+            "clocks": clk.summary()}
+
+
+def snapshot_leg(args, rank, world, dev):
     """BASELINE config 5b: pack the 32768-token prefix of 48 f16 layers into
     pinned host memory in both reference formats (raw f32 rows, int8-grouped
     payload rows), then restore it.  Reports the device-side pack kernel
     bandwidth (to a device buffer, HBM-bound) and the end-to-end host rates
     (sf37kv_pack_to_host / sf37kv_unpack_from_host, link-bound)."""
-    import ctypes
     import torch
     from sf37_b200 import _lib, kv
-    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
-    torch.cuda.set_device(dev)
     kd = (KVH // world) * HD
     rows = 32768
     g = torch.Generator(device=dev)
@@ -748,6 +1015,8 @@ def run_snapshot(args, rank, world):
         layers.append(dict(k_cache=k, v_cache=v, cap=rows, first_pos=0, rows=rows))
     res = {}
     stream = torch.cuda.current_stream(dev)
+    peak, kind = _peaks()
+    clk = ClockSampler(dev.index).__enter__()
     for fmt, name in ((kv.FMT_RAW, "raw_f32"), (kv.FMT_I8G, "i8_grouped")):
         arr, total = kv.pack_layers_desc(layers, kd, fmt)
         dbuf = torch.empty(total, dtype=torch.uint8, device=dev)
@@ -755,12 +1024,13 @@ def run_snapshot(args, rank, world):
             kv.pack(dbuf, arr, kd, kv.F16, fmt, stream=stream)
         torch.cuda.synchronize(dev)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        n = max(args.steps, 5)
         e0.record(stream)
-        for _ in range(args.steps):
+        for _ in range(n):
             kv.pack(dbuf, arr, kd, kv.F16, fmt, stream=stream)
         e1.record(stream)
         torch.cuda.synchronize(dev)
-        ms = e0.elapsed_time(e1) / args.steps
+        ms = e0.elapsed_time(e1) / n
         kv_read = LAYERS * rows * kd * 2 * 2
         del dbuf
         host = _lib.lib().sf37kv_host_alloc(total)
@@ -773,26 +1043,23 @@ def run_snapshot(args, rank, world):
         kv.unpack_from_host(host, arr, kd, kv.F16, fmt)
         t_unpack = time.perf_counter() - t0
         _lib.lib().sf37kv_host_free(host)
-        res[name] = {"bytes": total, "device_pack_ms": ms,
-                     "device_pack_GBps": (kv_read + total) / (ms * 1e-3) / 1e9,
+        dev_gbps = (kv_read + total) / (ms * 1e-3) / 1e9
+        res[name] = {"bytes": total, "device_pack_ms": ms, "device_pack_GBps": dev_gbps,
+                     "device_pack_frac": dev_gbps / peak,
                      "host_pack_s": t_pack, "host_pack_GBps": total / t_pack / 1e9,
                      "host_restore_s": t_unpack, "host_restore_GBps": total / t_unpack / 1e9}
-    sess = session_leg(dev, layers, kd, rows) if world == 1 else None
-    if rank != 0:
-        return
-    peak, kind = _peaks()
+    clk.__exit__()
+    sess = session_leg(dev, layers, kd, rows) if (world == 1 and not args.no_session) else None
+    del layers
+    torch.cuda.empty_cache()
     r = res["raw_f32"]
-    print(json.dumps({
-        "metric": "snapshot pack GB/s (config 5b: 32768-token prefix x 48 layers to pinned host)",
-        "value": r["host_pack_GBps"], "unit": "GB/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "f16 cache -> f32 rows / int8-grouped rows", "data": "synthetic N(0,1)",
-        "config": {"workload": "cfg5b snapshot pack/restore", "layers": LAYERS, "rows": rows},
-        "formats": res,
-        "roofline": {"bound": "hbm", "kernel": "pack_kernel (raw, device buffer)",
-                     "achieved": r["device_pack_GBps"], "peak": peak, "peak_kind": kind, "unit": "GB/s",
-                     "frac": r["device_pack_GBps"] / peak},
-        "session": sess}), flush=True)
+    return {"workload": "cfg5b: pack/restore the 32768-token prefix x 48 f16 layers (raw f32 snapshot rows and "
+                        "int8-grouped payload rows) to/from pinned host memory",
+            "formats": res,
+            "roofline": {"bound": "hbm", "kernel": "pack_kernel (raw, to a device buffer)",
+                         "achieved": r["device_pack_GBps"], "peak": peak, "peak_kind": kind, "unit": "GB/s",
+                         "frac": r["device_pack_GBps"] / peak},
+            "session": sess, "clocks": clk.summary()}
 
 
 def session_leg(dev, layers, kd, rows):
@@ -801,7 +1068,6 @@ def session_leg(dev, layers, kd, rows):
     raw snapshot written to pinned memory; beside it, the reference's own
     CUDA-backend per-row loops (two synchronous 4 KiB tensor reads per row,
     its own encoder and fwrite) timed on one fp32 layer and scaled to 48."""
-    import ctypes
     import shutil
     import tempfile
     import torch
@@ -870,80 +1136,71 @@ def session_leg(dev, layers, kd, rows):
     return out
 
 
-def run_prefill(args, rank, world):
-    """BASELINE config 4: per layer, append an 8192-token chunk onto a
-    24576-token f16 prefix and run causal chunk attention (bf16 queries,
-    64 Q / 8 KV heads, d 128); one step = all layers.  Tensor-core bound."""
+# ---------------------------------------------------------------- drivers
+def _compact_decode(line):
+    keep = ("value", "unit", "ms_per_step", "kv_read_GBps", "roofline", "e2e", "parity", "gpu_launches", "clocks")
+    d = {"workload": line["config"]["workload"], "ctx": line["config"]["ctx"]}
+    d.update({k: line[k] for k in keep if k in line})
+    return d
+
+
+def run_default(args, rank, world):
+    """The headline line (config 2) plus, after its timed region, the other
+    configs and the per-layer pattern as compact sub-objects."""
     import torch
-    from sf37_b200 import kv
-    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
-    torch.cuda.set_device(dev)
-    kvh_l, qh_l = KVH // world, QH // world
-    kd = kvh_l * HD
-    prefix, chunk, cap = 24576, 8192, 32768
-    g = torch.Generator(device=dev)
-    g.manual_seed(99 + rank)
-    kc = [torch.randn(cap, kd, device=dev, generator=g).half() for _ in range(LAYERS)]
-    vc = [torch.randn(cap, kd, device=dev, generator=g).half() for _ in range(LAYERS)]
-    kn = torch.randn(chunk, kd, device=dev, generator=g)
-    vn = torch.randn(chunk, kd, device=dev, generator=g)
-    q = torch.randn(chunk, qh_l, HD, device=dev, generator=g).to(torch.bfloat16)
-    gate = torch.randn(chunk, qh_l, device=dev, generator=g)
-    out = torch.empty(chunk, qh_l, HD, device=dev)
-    stream = torch.cuda.current_stream(dev)
-
-    def step():
-        for l in range(LAYERS):
-            kv.append([dict(k_cache=kc[l], v_cache=vc[l], cap=cap, pos0=prefix, n_tok=chunk, k=kn, v=vn)],
-                      kd, kv.F16, stream)
-            kv.prefill(kc[l], vc[l], cap, q, gate, out, prefix, chunk, qh_l, kvh_l, HD, kv.F16,
-                       stream=stream)
-
-    for _ in range(args.warmup):
-        step()
-    torch.cuda.synchronize(dev)
-    n0 = kv.launch_count()
-    clk = ClockSampler(dev.index).__enter__()
-    time.sleep(0.3)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(args.steps):
-        step()
-    e1.record(stream)
-    torch.cuda.synchronize(dev)
-    ms = e0.elapsed_time(e1) / args.steps
-    launches = kv.launch_count() - n0
-    # attention kernel alone, CUDA events per launch
-    evs = []
-    for _ in range(min(LAYERS, 16)):
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record(stream)
-        kv.prefill(kc[0], vc[0], cap, q, gate, out, prefix, chunk, qh_l, kvh_l, HD, kv.F16, stream=stream)
-        b.record(stream)
-        evs.append((a, b))
-    torch.cuda.synchronize(dev)
-    clk.__exit__()
-    att_ms = sum(a.elapsed_time(b) for a, b in evs) / len(evs)
-    pairs = chunk * prefix + chunk * (chunk + 1) // 2
-    flops_layer = 4.0 * HD * pairs * qh_l
-    if rank != 0:
+    dev = _dev()
+    line = decode_leg(args, rank, world, "decode", headline=True)
+    if line is None:
         return
-    peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json"))) \
-        if os.path.exists(os.path.join(ROOT, "MEASURED_PEAKS.json")) else {}
-    peak = float(peaks.get("bf16_tflops_sustained", 1400.0))
-    ach = flops_layer / (att_ms * 1e-3) / 1e12
-    print(json.dumps({
-        "metric": "prefill tokens/s (config 4: 8192-token chunk on a 24576-token prefix, 48 layers)",
-        "value": chunk * world / (ms * 1e-3) / world, "unit": "tokens/s", "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
-        "scaling": "strong", "vs_baseline": None, "dtype": "f16 K/V, bf16 q, f32 accumulate",
-        "data": "synthetic N(0,1), torch seeded CUDA generator",
-        "config": {"workload": "cfg4 chunked prefill", "layers": LAYERS, "prefix": prefix, "chunk": chunk},
-        "roofline": {"bound": "tensor", "kernel": "prefill_tc05_kernel", "achieved": ach,
-                     "peak": peak, "peak_kind": "measured sustained" if peaks else "fallback",
-                     "unit": "TFLOP/s", "frac": ach / peak, "launch_ms": att_ms,
-                     "algorithmic_flops_per_launch": flops_layer},
-        "gpu_launches": launches, "clocks": clk.summary()}), flush=True)
+    ok = line.get("parity", {}).get("ok", True)
+    if not args.headline_only:
+        configs = {}
+        sub_steps = max(3, min(args.steps, 10))
+        for wl, key in (("hybrid", "cfg3"), ("long", "cfg5a")):
+            sub = decode_leg(args, rank, world, wl, headline=False)
+            ok = ok and sub.get("parity", {}).get("ok", True)
+            configs[key] = _compact_decode(sub)
+        configs["cfg4"] = prefill_leg(args, rank, world, dev, max(2, min(args.steps, 3)))
+        configs["cfg5b"] = snapshot_leg(args, rank, world, dev)
+        if world == 1:
+            configs["cfg1"] = cfg1_leg(args, dev)
+            line["per_layer"] = per_layer_leg(args, dev)
+            if not args.no_ref_gpu:
+                line["reference_gpu"] = reference_gpu_leg(dev, sub_steps)
+        line["configs"] = configs
+    if world == 1 and not args.no_cpu and rank == 0:
+        line["cpu_baseline"] = cpu_baseline(CTX + 1)
+    _barrier(world, dev)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if not ok:
+        sys.stderr.write("bench: parity check FAILED (see the line's parity objects)\n")
+        sys.exit(3)
+
+
+def run_single(args, rank, world):
+    """--workload X: one line for that config alone."""
+    dev = _dev()
+    wl = args.workload
+    if wl in ("decode", "hybrid", "long"):
+        line = decode_leg(args, rank, world, wl, headline=True)
+        if line is None:
+            return
+    elif wl == "prefill":
+        line = prefill_leg(args, rank, world, dev, args.steps)
+    elif wl == "snapshot":
+        line = snapshot_leg(args, rank, world, dev)
+    elif wl == "cfg1":
+        line = cfg1_leg(args, dev)
+    elif wl == "per_layer":
+        line = per_layer_leg(args, dev)
+    _barrier(world, dev)
+    if rank == 0:
+        line.setdefault("workload", wl)
+        line.setdefault("n_gpus", world)
+        print(json.dumps(line), flush=True)
+    if not line.get("parity", {}).get("ok", True):
+        sys.exit(3)
 
 
 def main():
@@ -960,10 +1217,12 @@ def main():
                     help="decode workloads: fuse the q/k head norm + RoPE into the step (sf37kv_decode_prep)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
     ap.add_argument("--no-ref-gpu", action="store_true", help="skip the reference CUDA kernels leg")
-    ap.add_argument("--workload", default="decode",
-                    choices=["decode", "prefill", "hybrid", "long", "snapshot", "cfg1"],
-                    help="decode = BASELINE config 2 (default); hybrid = config 3; prefill = config 4; "
-                         "long = config 5a; snapshot = config 5b")
+    ap.add_argument("--no-session", action="store_true", help="skip the whole-session checkpoint leg")
+    ap.add_argument("--headline-only", action="store_true", help="default workload: skip the other configs")
+    ap.add_argument("--workload", default="all",
+                    choices=["all", "decode", "prefill", "hybrid", "long", "snapshot", "cfg1", "per_layer"],
+                    help="all = config 2 headline + every other config (default); decode = config 2; "
+                         "hybrid = config 3; prefill = config 4; long = config 5a; snapshot = config 5b")
     ap.add_argument("--quick", action="store_true",
                     help="timed steps only (no roofline/e2e/cpu legs): for profiler runs")
     ap.add_argument("--layers", type=int, default=48,
@@ -983,18 +1242,19 @@ def main():
         import torch.distributed as dist
         torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
         dist.init_process_group("nccl")
-    if args.workload == "prefill":
-        run_prefill(args, rank, world)
-    elif args.workload == "snapshot":
-        run_snapshot(args, rank, world)
-    elif args.workload == "cfg1":
-        run_cfg1(args, rank, world)
-    else:
-        run_ours(args, rank, world)
-    if world > 1:
-        import torch.distributed as dist
-        dist.barrier()
-        dist.destroy_process_group()
+    try:
+        if args.workload == "all":
+            if args.quick:
+                decode_leg(args, rank, world, "decode", headline=True)
+            else:
+                run_default(args, rank, world)
+        else:
+            run_single(args, rank, world)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+            dist.destroy_process_group()
 
 
 if __name__ == "__main__":
