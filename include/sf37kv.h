@@ -297,6 +297,43 @@ int sf37kv_oproj_reduce(const sf37kv_peer_gather *g, uint32_t n_layers, uint32_t
 /* Number of kernel launches this library has issued (process total). */
 uint64_t sf37kv_launch_count(void);
 
+/* ---- Decode cache sizing (the reference engine's rules) ----
+ * sf37kv_sliding_cache_cap: ring rows of a sliding-window layer for a context
+ * of ctx_size and a prefill chunk of prefill_cap: align256(512 + chunk),
+ * clamped to [window, min(ctx_size, 8192)] (cuda_sliding_cache_cap,
+ * sf37.c:3067-3081).  sf37kv_sliding_prefill_cap: the largest chunk such a
+ * ring prefills exactly, cache_cap - window (cuda_sliding_cache_prefill_cap,
+ * sf37.c:3083-3091).  sf37kv_kv_cache_bytes: K+V bytes of one layer's cache
+ * (cuda_decode_kv_bytes_for_cap, sf37.c:3093-3096, for dtype f32; f16 caches
+ * take half).  sf37kv_prefill_default_chunk: the chunk the engine picks from
+ * the device's free memory (4096 / 2048 / 1024 / 512 at 24 / 12 / 6 GiB,
+ * cuda_prefill_default_chunk, sf37.c:5131-5140; its environment override is
+ * the caller's).  sf37kv_plan_caches: every layer's cap as
+ * cuda_decode_state_init lays them out (sf37.c:3189-3211: layers il % 4 == 0
+ * hold the whole context, the others a sliding ring). */
+#define SF37KV_PLAN_MAX_LAYERS 64
+typedef struct {
+    uint32_t ctx_size;       /* clamped to [1, 262144] */
+    uint32_t window;         /* sliding window, min(512, ctx_size) */
+    uint32_t sliding_cap;    /* ring rows of every sliding layer */
+    uint32_t prefill_cap;    /* largest exact prefill chunk */
+    uint32_t full_layers, sliding_layers;
+    uint32_t cap[SF37KV_PLAN_MAX_LAYERS];
+    uint32_t sliding[SF37KV_PLAN_MAX_LAYERS];
+    uint64_t kv_cache_bytes; /* all layers, K and V, of the given dtype */
+} sf37kv_cache_plan;
+uint32_t sf37kv_sliding_cache_cap(uint32_t ctx_size, uint32_t prefill_cap);
+uint32_t sf37kv_sliding_prefill_cap(uint32_t ctx_size, uint32_t cache_cap);
+uint64_t sf37kv_kv_cache_bytes(uint32_t cap, uint32_t kv_heads, uint32_t head_dim, int dtype);
+uint32_t sf37kv_prefill_default_chunk(uint64_t free_bytes);
+int sf37kv_plan_caches(uint32_t ctx_size, uint32_t prefill_chunk, uint32_t n_layers, uint32_t kv_heads,
+                       uint32_t head_dim, int dtype, sf37kv_cache_plan *plan);
+/* The managed-KV-cache policy of sf37_cuda_should_use_managed_kv_cache
+ * (sf37_cuda.cu:1766-1800) on given free/total device bytes instead of a
+ * live cudaMemGetInfo: 1 = allocate the KV cache as managed memory. */
+int sf37kv_managed_kv_policy(uint64_t kv_cache_bytes, uint64_t context_bytes, uint64_t free_bytes,
+                             uint64_t total_bytes);
+
 #ifdef __cplusplus
 }
 #endif

@@ -358,3 +358,45 @@ def ref_cuda():
 
 def ref_tensor(ptr: int, nbytes: int):
     return ctypes.byref(RefTensor(ptr, nbytes))
+
+
+# ---------------------------------------------------------------- cache sizing
+def ref_sizing_available() -> bool:
+    return os.path.exists(os.path.join(HERE, "_ref", "libsf37ref_sizing.so"))
+
+
+_refs = None
+
+
+def ref_sizing():
+    """The reference engine's CUDA cache-sizing helpers (ref_sizing.c)."""
+    global _refs
+    if _refs is None:
+        R = ctypes.CDLL(os.path.join(HERE, "_ref", "libsf37ref_sizing.so"))
+        R.sf37ref_sliding_cache_cap.restype = _u32
+        R.sf37ref_sliding_cache_cap.argtypes = [_u32, _u32]
+        R.sf37ref_sliding_prefill_cap.restype = _u32
+        R.sf37ref_sliding_prefill_cap.argtypes = [_u32, _u32]
+        R.sf37ref_decode_kv_bytes_for_cap.restype = _u64
+        R.sf37ref_decode_kv_bytes_for_cap.argtypes = [_u32]
+        R.sf37ref_layer_is_full.restype = _int
+        R.sf37ref_layer_is_full.argtypes = [_u32]
+        _refs = R
+    return _refs
+
+
+def managed_kv_policy(kv_bytes, context_bytes, free_b, total_b):
+    """sf37_cuda_should_use_managed_kv_cache (sf37_cuda.cu:1766-1800) on given
+    free/total device bytes: 8 GiB KV or 8 GiB context thresholds, reserve
+    total/4 clamped to [8, 40] GiB."""
+    gib = 1 << 30
+    if kv_bytes == 0:
+        return 0
+    if kv_bytes >= 8 * gib:
+        return 1
+    if context_bytes < 8 * gib:
+        return 0
+    reserve = min(max(total_b // 4, 8 * gib), 40 * gib)
+    if context_bytes > free_b:
+        return 1
+    return int(free_b - context_bytes < reserve)

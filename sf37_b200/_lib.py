@@ -62,6 +62,12 @@ class Session(ctypes.Structure):
                 ("dtype", c_int), ("backend_kind", c_u32)]
 
 
+class CachePlan(ctypes.Structure):
+    _fields_ = [("ctx_size", c_u32), ("window", c_u32), ("sliding_cap", c_u32), ("prefill_cap", c_u32),
+                ("full_layers", c_u32), ("sliding_layers", c_u32), ("cap", c_u32 * 64), ("sliding", c_u32 * 64),
+                ("kv_cache_bytes", c_u64)]
+
+
 TP = ctypes.POINTER(Tensor)
 SP = ctypes.POINTER(Session)
 
@@ -135,6 +141,12 @@ SIGNATURES = {
     "sf37kv_decode_gather": (c_int, [ctypes.POINTER(DecodeLayer), c_u32, c_u32, c_u32, c_u32, c_int,
                                      ctypes.POINTER(PeerGather), c_u32, c_vp]),
     "sf37kv_gather_wait": (c_int, [ctypes.POINTER(PeerGather), c_u32, c_vp]),
+    "sf37kv_sliding_cache_cap": (c_u32, [c_u32, c_u32]),
+    "sf37kv_sliding_prefill_cap": (c_u32, [c_u32, c_u32]),
+    "sf37kv_kv_cache_bytes": (c_u64, [c_u32, c_u32, c_u32, c_int]),
+    "sf37kv_prefill_default_chunk": (c_u32, [c_u64]),
+    "sf37kv_plan_caches": (c_int, [c_u32, c_u32, c_u32, c_u32, c_u32, c_int, ctypes.POINTER(CachePlan)]),
+    "sf37kv_managed_kv_policy": (c_int, [c_u64, c_u64, c_u64, c_u64]),
     # include/sf37kv_session.h
     "sf37kv_session_layout_default": (SessionLayout, []),
     "sf37kv_session_snapshot_bytes": (c_u64, [SP]),

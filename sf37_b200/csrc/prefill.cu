@@ -62,6 +62,21 @@ extern "C" int sf37kv_prefill(const sf37kv_cache *cache, const void *q, int q_ty
     if (q_type != SF37KV_Q_F32 && q_type != SF37KV_Q_BF16)
         return set_error(SF37KV_EINVAL, "prefill: unknown q type %d", q_type);
     if (n_tok == 0) return SF37KV_OK;
+    if (cache->sliding) {
+        // The chunk's own append must not have overwritten a row that its
+        // first token attends to: the oldest row still in the ring,
+        // pos0 + n_tok - cap, may not be newer than that token's window
+        // start (the reference engine keeps chunks within cap - window,
+        // sf37.c:3083-3091, 3197-3200).
+        const uint64_t end = (uint64_t)pos0 + n_tok;
+        const uint64_t oldest = end > cache->cap ? end - cache->cap : 0;
+        const uint64_t first = (cache->window && pos0 + 1u > cache->window) ? pos0 + 1u - cache->window : 0;
+        if (oldest > first)
+            return set_error(SF37KV_EINVAL,
+                             "prefill: sliding ring of %u rows cannot hold a %u-token chunk with its %u-row window "
+                             "(needs cap >= window + n_tok - 1)",
+                             cache->cap, n_tok, cache->window);
+    }
     cudaStream_t s = stream ? (cudaStream_t)stream : current_stream();
     if (dtype == SF37KV_F16 && head_dim == 128) {
         bool handled = false;

@@ -266,23 +266,21 @@ extern "C" int sf37_cuda_tensor_fill_f32(sf37_cuda_tensor *tensor, float value, 
     return dropin_ok(cudaGetLastError(), "fill f32 launch");
 }
 
-// Policy restated from sf37_cuda.cu:1766-1800: managed memory once the KV
-// cache reaches 8 GiB, or when a >= 8 GiB context would leave less than the
-// reserve (total/4 clamped to [8, 40] GiB) free.
+// Policy of sf37_cuda.cu:1766-1800 (managed memory once the KV cache
+// reaches 8 GiB, or when a >= 8 GiB context would leave less than the
+// reserve, total/4 clamped to [8, 40] GiB, free), with the device's free and
+// total memory from cudaMemGetInfo; the arithmetic is
+// sf37kv_managed_kv_policy (sizing.cu).  A failed query answers 0, as the
+// reference does.
 extern "C" int sf37_cuda_should_use_managed_kv_cache(uint64_t kv_cache_bytes,
                                                      uint64_t context_bytes) {
     if (kv_cache_bytes == 0) return 0;
     const uint64_t gib = 1073741824ull;
-    if (kv_cache_bytes >= 8ull * gib) return 1;
-    if (context_bytes < 8ull * gib) return 0;
+    if (kv_cache_bytes < 8ull * gib && context_bytes < 8ull * gib) return 0;
     size_t free_b = 0, total_b = 0;
-    if (cudaMemGetInfo(&free_b, &total_b) != cudaSuccess) {
+    if (kv_cache_bytes < 8ull * gib && cudaMemGetInfo(&free_b, &total_b) != cudaSuccess) {
         (void)cudaGetLastError();
         return 0;
     }
-    uint64_t reserve = (uint64_t)total_b / 4u;
-    if (reserve < 8ull * gib) reserve = 8ull * gib;
-    if (reserve > 40ull * gib) reserve = 40ull * gib;
-    if (context_bytes > (uint64_t)free_b) return 1;
-    return (uint64_t)free_b - context_bytes < reserve;
+    return sf37kv_managed_kv_policy(kv_cache_bytes, context_bytes, free_b, total_b);
 }
