@@ -38,6 +38,7 @@
 #include <cstdlib>
 #include <algorithm>
 #include <cstring>
+#include <mutex>
 
 #include <cuda_bf16.h>
 #include <cmath>
@@ -73,6 +74,7 @@ struct JobDev {
     const uint16_t *qn, *kn;     // bf16 [128] norm weights
     uint32_t rotary, rope_idx;
     float eps;
+    uint32_t pre;                // rows may be streamed before griddepcontrol.wait
 };
 
 // RoPE cos/sin tables of one decode launch: one per distinct (rotary_dim,
@@ -144,13 +146,13 @@ __device__ __noinline__ void prep_heads(const float *rope, const JobDev &J, uint
     }
 }
 
-// The CTA owning the last split of (job, kvh) stores this KV head's slice of
-// the appended row (f32 -> T, round to nearest even) before any warp loads
+// The CTA whose rows end at the job's last row (end-1) stores this KV head's
+// slice of the appended row (f32 -> T, round to nearest even) before any warp loads
 // rows; __syncthreads() plus L2-coherent cp.async.cg loads make it visible.
 template <typename T>
-__device__ __forceinline__ void fused_append(const JobDev &J, uint32_t kvh, uint32_t split, uint32_t kv_heads,
+__device__ __forceinline__ void fused_append(const JobDev &J, uint32_t kvh, bool appender, uint32_t kv_heads,
                                              const float *kf = nullptr) {
-    if (!J.k_new || split + 1u != J.n_splits) return;
+    if (!appender) return;
     const uint32_t i = threadIdx.x;
     if (i >= 64u) return;
     // kf: the prepared K head in shared memory (prep_heads), else the raw row
@@ -179,6 +181,7 @@ struct DecodeParams {
     GatherDev gat;
     float rope[kMaxRope][128];  // q/k preparation tables (JobDev::rope_idx)
     uint32_t pdl;               // launched with programmatic stream serialization
+    int *err;                   // device error flag (a bounded wait gave up), or nullptr
 };
 
 // Programmatic dependent launch (sm_90+): a kernel launched with
@@ -265,129 +268,241 @@ __device__ __forceinline__ uint32_t ring_slot(uint32_t sb, uint32_t x, uint32_t 
     return s;
 }
 
+__device__ __forceinline__ void cp_async16(uint32_t smem_addr, const void *gptr) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr), "l"(gptr));
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N)); }
+
 // ------------------------------------------------------------ CTA epilogue
 // Shared memory used by the epilogue: per stream and head, O[128], m, l.
 //   Os[(stream * 16 + h) * 128 + d], Ms[stream*16 + h], Ls[stream*16 + h]
+// followed by X: W[stream*16 + h] (stream weights), PM[16], PL[16].
 // After the stream merge, the CTA's result is written either directly to the
 // output (single split) or to scratch followed by the last-CTA reduction.
+
+// Stream weights of each head h < G: M = max over streams of m, W[s][h] =
+// 2^(m_s - M), L = sum_s l_s W[s][h] (one thread per head).
+__device__ __forceinline__ void stream_weights(uint32_t G, uint32_t n_streams, const float *Ms, const float *Ls,
+                                               float *W, float *PM, float *PL) {
+    const uint32_t h = threadIdx.x;
+    if (h >= G) return;
+    float M = -INFINITY;
+    for (uint32_t s = 0; s < n_streams; s++) M = fmaxf(M, Ms[s * 16u + h]);
+    float L = 0.f;
+    for (uint32_t s = 0; s < n_streams; s++) {
+        const float w = M == -INFINITY ? 0.f : exp2f(Ms[s * 16u + h] - M);
+        W[s * 16u + h] = w;
+        L += Ls[s * 16u + h] * w;
+    }
+    PM[h] = M;
+    PL[h] = L;
+}
+
+// sum_s W[s][h] * O_s[h][d4 .. d4+3]
+__device__ __forceinline__ float4 stream_o(uint32_t n_streams, const float *Os, const float *W, uint32_t h,
+                                           uint32_t d4) {
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (uint32_t s = 0; s < n_streams; s++) {
+        const float w = W[s * 16u + h];
+        const float4 o = *reinterpret_cast<const float4 *>(Os + (s * 16u + h) * 128u + d4);
+        acc.x += o.x * w;
+        acc.y += o.y * w;
+        acc.z += o.z * w;
+        acc.w += o.w * w;
+    }
+    return acc;
+}
+
+__device__ __forceinline__ float4 finalize4(float4 acc, float L, float g) {
+    float4 r;
+    r.x = L > 0.f ? acc.x / L * g : 0.f;
+    r.y = L > 0.f ? acc.y / L * g : 0.f;
+    r.z = L > 0.f ? acc.z / L * g : 0.f;
+    r.w = L > 0.f ? acc.w / L * g : 0.f;
+    return r;
+}
+
+__device__ __forceinline__ float *epilogue_x(float *Ls, uint32_t G, uint32_t n_streams) {
+    float *X = Ls + 16u * n_streams * ((G + 7u) >> 3);
+    return reinterpret_cast<float *>((reinterpret_cast<uintptr_t>(X) + 15u) & ~uintptr_t(15));
+}
+
+// Bulk (TMA) copies for the split merge: one transaction per partial,
+// completion counted on an mbarrier.  Addresses and sizes are multiples of
+// 16 bytes (partials are part_stride floats, part_stride a multiple of 4).
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+                 "l"(src), "r"(bytes), "r"(bar)
+                 : "memory");
+}
+// Parity wait with an iteration bound (the copies are from this GPU's own
+// memory and complete in microseconds; the bound only keeps a fault from
+// hanging the kernel).  Returns false when it gave up.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t phase) {
+    const long long t0 = clock64();
+    for (;;) {
+        uint32_t ok;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}\n"
+            : "=r"(ok)
+            : "r"(bar), "r"(phase)
+            : "memory");
+        if (ok) return true;
+        if (clock64() - t0 > 4000000000ll) return false;
+    }
+}
+
+// The last CTA of a (job, KV head) merges its n split partials.  Thread 0
+// starts bulk copies of whole partials (O vectors and (m, l) pairs) into the
+// stage buffers, as many splits per pass as fit (all of them for the small-
+// launch plan), so a pass costs one L2 round trip; each thread then folds the
+// pass into its running (max, sum, O) with an online rescale.
+template <int NT>
+__device__ void merge_partials(const DecodeParams &P, const JobDev &J, uint32_t kvh, uint8_t *smem,
+                               uint32_t stage_bytes, const float *gate_s) {
+    const uint32_t G = P.group, n = J.n_splits, stride = P.part_stride, tid = threadIdx.x;
+    const float *P0 = P.part + (uint64_t)(J.cta_begin + kvh * n) * stride;
+    const uint32_t split_bytes = stride * 4u;
+    const uint32_t bar = (uint32_t)__cvta_generic_to_shared(smem + stage_bytes - 16u);
+    uint32_t cnt_max = (stage_bytes - 16u) / split_bytes;
+    if (cnt_max < 1) cnt_max = 1;
+    const uint32_t land = (uint32_t)__cvta_generic_to_shared(smem);
+    auto issue = [&](uint32_t s0) {
+        const uint32_t cnt = min(cnt_max, n - s0);
+        // the landing area was last touched by generic loads and stores
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        mbar_expect_tx(bar, cnt * split_bytes);
+        for (uint32_t s = 0; s < cnt; s++)
+            bulk_g2s(land + s * split_bytes, P0 + (uint64_t)(s0 + s) * stride, split_bytes, bar);
+    };
+    if (tid == 0) {
+        mbar_init(bar, 1);
+        // the partials were written by other CTAs' generic stores and are
+        // read here by the async proxy
+        asm volatile("fence.proxy.async.global;" ::: "memory");
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        issue(0);
+    }
+    __syncthreads();
+    const float *Lf = reinterpret_cast<const float *>(smem);
+    const float4 *L4 = reinterpret_cast<const float4 *>(smem);
+    constexpr int kPer = (16 * 32 + NT - 1) / NT;  // float4 outputs per thread (G <= 16)
+    float4 acc[kPer];
+    float Mr[kPer], Lr[kPer];
+#pragma unroll
+    for (int k = 0; k < kPer; k++) {
+        acc[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+        Mr[k] = -INFINITY;
+        Lr[k] = 0.f;
+    }
+    bool ok = true;
+    uint32_t phase = 0;
+    for (uint32_t s0 = 0; s0 < n; s0 += cnt_max) {
+        const uint32_t cnt = min(cnt_max, n - s0);
+        if (!mbar_wait(bar, phase)) ok = false;
+        phase ^= 1u;
+        if (ok) {
+#pragma unroll
+            for (int k = 0; k < kPer; k++) {
+                const uint32_t idx = tid + (uint32_t)k * NT;
+                if (idx >= G * 32u) continue;
+                const uint32_t ml = G * 128u + 2u * (idx >> 5);
+                float mp = -INFINITY;
+                for (uint32_t s = 0; s < cnt; s++) mp = fmaxf(mp, Lf[s * stride + ml]);
+                const float mnew = fmaxf(Mr[k], mp);
+                if (mnew == -INFINITY) continue;
+                const float sc = exp2f(Mr[k] - mnew);
+                acc[k].x *= sc;
+                acc[k].y *= sc;
+                acc[k].z *= sc;
+                acc[k].w *= sc;
+                Lr[k] *= sc;
+                for (uint32_t s = 0; s < cnt; s++) {
+                    const float w = exp2f(Lf[s * stride + ml] - mnew);
+                    const float4 v = L4[s * (stride / 4u) + idx];
+                    Lr[k] += Lf[s * stride + ml + 1u] * w;
+                    acc[k].x += v.x * w;
+                    acc[k].y += v.y * w;
+                    acc[k].z += v.z * w;
+                    acc[k].w += v.w * w;
+                }
+                Mr[k] = mnew;
+            }
+        }
+        __syncthreads();
+        if (s0 + cnt_max < n && tid == 0 && ok) issue(s0 + cnt_max);
+    }
+    if (!ok) {
+        if (tid == 0 && P.err) atomicExch(P.err, 3);
+        return;
+    }
+#pragma unroll
+    for (int k = 0; k < kPer; k++) {
+        const uint32_t idx = tid + (uint32_t)k * NT;
+        if (idx < G * 32u) {
+            const uint32_t h = idx >> 5, d4 = (idx & 31u) * 4u;
+            const uint32_t qh = kvh * G + h;
+            const float4 r = finalize4(acc[k], Lr[k], gate_s[h]);
+            *reinterpret_cast<float4 *>(J.out + (uint64_t)qh * 128u + d4) = r;
+            if (P.gat.world) gather_store4(P, J, (uint64_t)qh * 128u + d4, r);
+        }
+    }
+}
+
 template <int NT>
 __device__ void finish_cta(const DecodeParams &P, const JobDev &J, uint32_t j, uint32_t kvh,
                            uint32_t split, uint32_t cta, uint32_t n_streams, float *Os, float *Ms,
-                           float *Ls) {
+                           float *Ls, uint8_t *smem, uint32_t stage_bytes, const float *gate_s) {
     const uint32_t G = P.group;
     const uint32_t tid = threadIdx.x;
+    float *W = epilogue_x(Ls, G, n_streams), *PM = W + 256, *PL = PM + 16;
     __syncthreads();
-    // Merge streams: thread handles elements (h, d) with stride NT.
+    stream_weights(G, n_streams, Ms, Ls, W, PM, PL);
+    __syncthreads();
     const bool single = J.n_splits == 1;
     float *part = P.part + (uint64_t)cta * P.part_stride;
-    for (uint32_t idx = tid; idx < G * 128u; idx += NT) {
-        const uint32_t h = idx >> 7, d = idx & 127u;
-        float M = -INFINITY;
-        for (uint32_t s = 0; s < n_streams; s++) M = fmaxf(M, Ms[s * 16u + h]);
-        float L = 0.f, O = 0.f;
-        if (M != -INFINITY) {
-            for (uint32_t s = 0; s < n_streams; s++) {
-                const float w = exp2f(Ms[s * 16u + h] - M);
-                L += Ls[s * 16u + h] * w;
-                O += Os[(s * 16u + h) * 128u + d] * w;
-            }
-        }
+    for (uint32_t idx = tid; idx < G * 32u; idx += NT) {
+        const uint32_t h = idx >> 5, d4 = (idx & 31u) * 4u;
+        const float4 acc = stream_o(n_streams, Os, W, h, d4);
         if (single) {
             const uint32_t qh = kvh * G + h;
-            const float g = J.gate ? sigmoid_dev(J.gate[qh]) : 1.0f;
-            const float val = L > 0.f ? O / L * g : 0.f;
-            J.out[(uint64_t)qh * 128u + d] = val;
-            if (P.gat.world) gather_store(P, J, (uint64_t)qh * 128u + d, val);
+            const float4 r = finalize4(acc, PL[h], gate_s[h]);
+            *reinterpret_cast<float4 *>(J.out + (uint64_t)qh * 128u + d4) = r;
+            if (P.gat.world) gather_store4(P, J, (uint64_t)qh * 128u + d4, r);
         } else {
-            part[h * 128u + d] = O;
-            if (d == 0) {
-                part[G * 128u + 2u * h] = M;
-                part[G * 128u + 2u * h + 1u] = L;
-            }
+            __stcg(reinterpret_cast<float4 *>(part + h * 128u + d4), acc);
         }
     }
     if (single) {
         gather_group_done(P);
         return;
     }
+    if (tid < G) __stcg(reinterpret_cast<float2 *>(part + G * 128u + 2u * tid), make_float2(PM[tid], PL[tid]));
 
-    // Last-CTA election (threadFenceReduction pattern).
+    // Last-CTA election: every thread's partial stores precede the barrier;
+    // thread 0's release atomic publishes them (the grid-barrier pattern),
+    // and its acquire side orders the merging CTA's reads after the others'.
     __shared__ uint32_t s_last;
-    __threadfence();
     __syncthreads();
     uint32_t *ctr = P.counters + (uint64_t)j * P.kv_heads + kvh;
-    if (tid == 0) s_last = atomicAdd(ctr, 1u) == J.n_splits - 1u;
+    if (tid == 0) {
+        uint32_t prev;
+        asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(prev) : "l"(ctr) : "memory");
+        s_last = prev == J.n_splits - 1u;
+    }
     __syncthreads();
     if (!s_last) return;
     __threadfence();
-
-    const uint32_t n = J.n_splits;
-    const uint32_t base = J.cta_begin + kvh * n;
-    const float *P0 = P.part + (uint64_t)base * P.part_stride;
-    // Step 1: per head, global max, weights w[s][h] (into Os), total sum.
-    float *W = Os;          // n * G floats (n <= kMaxSplits, G <= 16)
-    float *Mh = Ms;         // G floats
-    float *Lh = Ls;         // G floats
-    const uint32_t lane = tid & 31u, warp = tid >> 5;
-    for (uint32_t h = warp; h < G; h += NT / 32) {
-        float m = -INFINITY;
-        for (uint32_t s = lane; s < n; s += 32)
-            m = fmaxf(m, __ldcg(P0 + (uint64_t)s * P.part_stride + G * 128u + 2u * h));
-        for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-        float l = 0.f;
-        for (uint32_t s = lane; s < n; s += 32) {
-            const float *ml = P0 + (uint64_t)s * P.part_stride + G * 128u + 2u * h;
-            const float w = m == -INFINITY ? 0.f : exp2f(__ldcg(ml) - m);
-            W[s * G + h] = w;
-            l += __ldcg(ml + 1) * w;
-        }
-        for (int o = 16; o; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
-        if (lane == 0) {
-            Mh[h] = m;
-            Lh[h] = l;
-        }
-    }
-    __syncthreads();
-    // Step 2: O = sum_s w[s][h] * O_s[h][d], four dims per thread.
-    for (uint32_t idx = tid; idx < G * 32u; idx += NT) {
-        const uint32_t h = idx >> 5, d4 = (idx & 31u) * 4u;
-        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-        uint32_t s = 0;
-        for (; s + 8 <= n; s += 8) {
-            float4 x[8];
-#pragma unroll
-            for (int u = 0; u < 8; u++)
-                x[u] = __ldcg(reinterpret_cast<const float4 *>(
-                    P0 + (uint64_t)(s + u) * P.part_stride + h * 128u + d4));
-#pragma unroll
-            for (int u = 0; u < 8; u++) {
-                const float w = W[(s + u) * G + h];
-                acc.x += x[u].x * w;
-                acc.y += x[u].y * w;
-                acc.z += x[u].z * w;
-                acc.w += x[u].w * w;
-            }
-        }
-        for (; s < n; s++) {
-            const float4 x = __ldcg(reinterpret_cast<const float4 *>(
-                P0 + (uint64_t)s * P.part_stride + h * 128u + d4));
-            const float w = W[s * G + h];
-            acc.x += x.x * w;
-            acc.y += x.y * w;
-            acc.z += x.z * w;
-            acc.w += x.w * w;
-        }
-        const uint32_t qh = kvh * G + h;
-        const float L = Lh[h];
-        const float g = J.gate ? sigmoid_dev(J.gate[qh]) : 1.0f;
-        float4 r;
-        r.x = L > 0.f ? acc.x / L * g : 0.f;
-        r.y = L > 0.f ? acc.y / L * g : 0.f;
-        r.z = L > 0.f ? acc.z / L * g : 0.f;
-        r.w = L > 0.f ? acc.w / L * g : 0.f;
-        *reinterpret_cast<float4 *>(J.out + (uint64_t)qh * 128u + d4) = r;
-        if (P.gat.world) gather_store4(P, J, (uint64_t)qh * 128u + d4, r);
-    }
+    merge_partials<NT>(P, J, kvh, smem, stage_bytes, gate_s);
     if (tid == 0) *ctr = 0u;  // ready for the next launch
     gather_group_done(P);
 }
@@ -420,12 +535,6 @@ __device__ void finish_cta(const DecodeParams &P, const JobDev &J, uint32_t j, u
 // rows 2t+{0,1,8,9}, chunks g/g+8) bank-conflict free for 128-bit loads.
 __device__ __forceinline__ uint32_t swz(uint32_t r) { return ((r & 1u) << 2) ^ (((r >> 1) & 3u) << 1); }
 
-__device__ __forceinline__ void cp_async16(uint32_t smem_addr, const void *gptr) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr), "l"(gptr));
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N)); }
 
 __device__ __forceinline__ uint4 lds128(uint32_t addr) {
     uint4 r;
@@ -495,13 +604,26 @@ __global__ void __launch_bounds__(NW * 32, 1) decode_f16_pipe_kernel(const __gri
     // row before any load can read it.
     float *Qf = reinterpret_cast<float *>(smem_raw + NW * S * kStage + 2 * 8 * 32 * 16), *Kf = Qf + 16 * 128;
     const bool prep = PREP && J.qn != nullptr;
-    const bool appender = J.k_new && split + 1u == J.n_splits;
-    // Under PDL nothing may be read before griddepcontrol.wait: the previous
-    // kernel's writes (to these caches too) are not yet guaranteed visible.
+    const bool appender = J.k_new && row0 < row1 && row1 == J.end;
+    // Under PDL the previous kernel on the stream may still be running until
+    // griddepcontrol.wait returns, and only then are its writes visible.  The
+    // host marks a job "pre" when that kernel cannot have written its cache
+    // (see attention_jobs): such a CTA starts streaming its first rows before
+    // the wait, overlapping the previous kernel's tail.  q, the gate and the
+    // appended row may come from the previous kernel and are read after it.
+    const bool pre_wait = J.pre != 0u && !appender;
+    if (pre_wait) {
+#pragma unroll
+        for (int s = 0; s < S - 1; s++) issue(s);
+    }
     griddep_wait();
     griddep_launch_dependents();
+    // The gate factors of this CTA's heads, loaded now so the epilogue does
+    // not wait on them (stored to shared memory after the q loads below).
+    __shared__ float gate_s[16];
+    const float gate_raw = (threadIdx.x < G && J.gate) ? J.gate[kvh * G + threadIdx.x] : 0.f;
     // A CTA that does not append starts its first loads before preparing q.
-    const bool early = !appender && prep;
+    const bool early = !pre_wait && !appender && prep;
     if (early) {
 #pragma unroll
         for (int s = 0; s < S - 1; s++) issue(s);
@@ -533,7 +655,8 @@ __global__ void __launch_bounds__(NW * 32, 1) decode_f16_pipe_kernel(const __gri
             Qs[(warp * 8 + kk) * 32 + lane] = make_uint4(r[0], r[1], r[2], r[3]);
         }
     }
-    fused_append<__half>(J, kvh, split, P.kv_heads, prep ? Kf : nullptr);
+    if (threadIdx.x < G) gate_s[threadIdx.x] = J.gate ? sigmoid_dev(gate_raw) : 1.0f;
+    fused_append<__half>(J, kvh, appender, P.kv_heads, prep ? Kf : nullptr);
     __syncthreads();
 
     float o[16][4];
@@ -541,7 +664,7 @@ __global__ void __launch_bounds__(NW * 32, 1) decode_f16_pipe_kernel(const __gri
     for (int i = 0; i < 16; i++) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
     float m_run = -INFINITY, l_run = 0.f;
 
-    if (!early) {
+    if (!early && !pre_wait) {
 #pragma unroll
         for (int s = 0; s < S - 1; s++) issue(s);
     }
@@ -645,7 +768,7 @@ __global__ void __launch_bounds__(NW * 32, 1) decode_f16_pipe_kernel(const __gri
             Ls[stream * 16u + hrow] = l_run;
         }
     }
-    finish_cta<NW * 32>(P, J, j, kvh, split, cta, n_streams, Os, Ms, Ls);
+    finish_cta<NW * 32>(P, J, j, kvh, split, cta, n_streams, Os, Ms, Ls, smem_raw, NW * S * kStage, gate_s);
 }
 
 // ------------------------------------------------------------ f32 kernel, tensor cores
@@ -736,13 +859,26 @@ __global__ void __launch_bounds__(NW * 32, 1) decode_f32_pipe_kernel(const __gri
     // row before any load can read it.
     float *Qf = reinterpret_cast<float *>(smem_raw + NW * S * kStage + 2 * 8 * 32 * 16), *Kf = Qf + 16 * 128;
     const bool prep = PREP && J.qn != nullptr;
-    const bool appender = J.k_new && split + 1u == J.n_splits;
-    // Under PDL nothing may be read before griddepcontrol.wait: the previous
-    // kernel's writes (to these caches too) are not yet guaranteed visible.
+    const bool appender = J.k_new && row0 < row1 && row1 == J.end;
+    // Under PDL the previous kernel on the stream may still be running until
+    // griddepcontrol.wait returns, and only then are its writes visible.  The
+    // host marks a job "pre" when that kernel cannot have written its cache
+    // (see attention_jobs): such a CTA starts streaming its first rows before
+    // the wait, overlapping the previous kernel's tail.  q, the gate and the
+    // appended row may come from the previous kernel and are read after it.
+    const bool pre_wait = J.pre != 0u && !appender;
+    if (pre_wait) {
+#pragma unroll
+        for (int s = 0; s < S - 1; s++) issue(s);
+    }
     griddep_wait();
     griddep_launch_dependents();
+    // The gate factors of this CTA's heads, loaded now so the epilogue does
+    // not wait on them (stored to shared memory after the q loads below).
+    __shared__ float gate_s[16];
+    const float gate_raw = (threadIdx.x < G && J.gate) ? J.gate[kvh * G + threadIdx.x] : 0.f;
     // A CTA that does not append starts its first loads before preparing q.
-    const bool early = !appender && prep;
+    const bool early = !pre_wait && !appender && prep;
     if (early) {
 #pragma unroll
         for (int s = 0; s < S - 1; s++) issue(s);
@@ -765,7 +901,8 @@ __global__ void __launch_bounds__(NW * 32, 1) decode_f32_pipe_kernel(const __gri
             Qs[(warp * 8 + kk) * 32 + lane] = make_uint4(r0, r1, r2, r3);
         }
     }
-    fused_append<float>(J, kvh, split, P.kv_heads, prep ? Kf : nullptr);
+    if (threadIdx.x < G) gate_s[threadIdx.x] = J.gate ? sigmoid_dev(gate_raw) : 1.0f;
+    fused_append<float>(J, kvh, appender, P.kv_heads, prep ? Kf : nullptr);
     __syncthreads();
 
     float o[16][4];
@@ -773,7 +910,7 @@ __global__ void __launch_bounds__(NW * 32, 1) decode_f32_pipe_kernel(const __gri
     for (int i = 0; i < 16; i++) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
     float m_run = -INFINITY, l_run = 0.f;
 
-    if (!early) {
+    if (!early && !pre_wait) {
 #pragma unroll
         for (int s = 0; s < S - 1; s++) issue(s);
     }
@@ -878,7 +1015,7 @@ __global__ void __launch_bounds__(NW * 32, 1) decode_f32_pipe_kernel(const __gri
             Ls[stream * 16u + hrow] = l_run;
         }
     }
-    finish_cta<NW * 32>(P, J, j, kvh, split, cta, n_streams, Os, Ms, Ls);
+    finish_cta<NW * 32>(P, J, j, kvh, split, cta, n_streams, Os, Ms, Ls, smem_raw, NW * S * kStage, gate_s);
 }
 
 // ------------------------------------------------------------ generic kernel
@@ -982,29 +1119,6 @@ static void rope_table(float *t, const RopeKey &k) {
     }
 }
 
-// Launches a pipelined decode kernel; with P.pdl set, with programmatic
-// stream serialization so that its CTAs start (and prefetch cached rows)
-// while the previous kernel on the stream drains.
-template <typename Kernel>
-static void launch_pipe(Kernel kernel, unsigned grid, unsigned block, size_t smem, cudaStream_t s,
-                        const DecodeParams &P) {
-    if (!P.pdl) {
-        kernel<<<grid, block, smem, s>>>(P);
-        return;
-    }
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(grid);
-    cfg.blockDim = dim3(block);
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = s;
-    cudaLaunchAttribute at[1];
-    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    at[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = at;
-    cfg.numAttrs = 1;
-    (void)cudaLaunchKernelEx(&cfg, kernel, P);
-}
-
 constexpr size_t kPrepSmem = (16 * 128 + 128) * 4;  // prepared q heads + K head (PREP kernels)
 static size_t smem_pipe(int nw, int stages) { return (size_t)nw * stages * 8192 + 2 * 8 * 32 * 16; }
 static size_t smem_pipe32(int nw, int stages) { return (size_t)nw * stages * 16384 + 2 * 8 * 32 * 16; }
@@ -1032,6 +1146,92 @@ static int launch_generic(const AttnJob *jobs, uint32_t n, uint32_t q_heads, uin
         if (int rc = check_cuda(cudaGetLastError(), "generic attention launch")) return rc;
     }
     return SF37KV_OK;
+}
+
+// Batched f16 kernel: 4 warps, two CTAs per SM.  Small-launch f16 kernel:
+// 8 warps, one CTA per SM (its stage buffers hold every split partial of a
+// group for the merge).  f32 kernel: 4 warps, one CTA per SM.
+static const size_t kSmemF16 = smem_pipe(4, 3), kSmemF16Wide = smem_pipe(8, 3), kSmemF32 = smem_pipe32(4, 3);
+
+// What the last decode kernel launched on each stream appended to.  The
+// decode kernels trigger their dependents early (PDL), so the next decode on
+// the same stream may start while one is still running; a job of the new
+// launch may stream its rows before griddepcontrol.wait only if the running
+// kernel cannot write them, i.e. it appended to neither of the job's caches
+// (sf37kv_decode_noalloc's kernel records its appends here too).  Kernels
+// that this file does not launch (other libraries', this library's appends
+// and prefills) trigger no early start, so a decode that follows one of them
+// starts after it has completed whatever the record says; with no record for
+// a stream, no job streams early.
+struct StreamRecord {
+    cudaStream_t stream;
+    bool used;
+    uint32_t n;
+    const void *caches[2 * kMaxJobs];
+};
+static StreamRecord g_stream_rec[8];
+static uint32_t g_stream_rec_next = 0;
+static std::mutex g_stream_rec_mu;
+
+// Marks each job of a launch on `s` that may stream before the wait.
+static void mark_pre(cudaStream_t s, JobDev *jobs, uint32_t n) {
+    std::lock_guard<std::mutex> lk(g_stream_rec_mu);
+    const StreamRecord *r = nullptr;
+    for (const StreamRecord &x : g_stream_rec)
+        if (x.used && x.stream == s) r = &x;
+    for (uint32_t i = 0; i < n; i++) {
+        bool ok = r != nullptr;
+        for (uint32_t c = 0; ok && r && c < r->n; c++) ok = r->caches[c] != jobs[i].k && r->caches[c] != jobs[i].v;
+        jobs[i].pre = ok ? 1u : 0u;
+    }
+}
+
+void note_stream_appends(cudaStream_t s, const JobDev *jobs, uint32_t n) {
+    std::lock_guard<std::mutex> lk(g_stream_rec_mu);
+    StreamRecord *r = nullptr;
+    for (StreamRecord &x : g_stream_rec)
+        if (x.used && x.stream == s) r = &x;
+    if (!r) {
+        r = &g_stream_rec[g_stream_rec_next];
+        g_stream_rec_next = (g_stream_rec_next + 1u) % 8u;
+    }
+    r->stream = s;
+    r->used = true;
+    r->n = 0;
+    for (uint32_t i = 0; i < n && r->n + 2u <= 2u * kMaxJobs; i++) {
+        if (!jobs[i].k_new) continue;
+        r->caches[r->n++] = jobs[i].k;
+        r->caches[r->n++] = jobs[i].v;
+    }
+}
+
+// Launches a pipelined decode kernel of `warps` warps; with P.pdl, with
+// programmatic stream serialization (its CTAs start while the previous kernel
+// on the stream drains and wait in griddepcontrol.wait).
+template <typename Kernel>
+static void launch_decode(Kernel kernel, unsigned grid, unsigned warps, size_t smem, cudaStream_t s,
+                          const DecodeParams &P) {
+    // Kernel attributes, once per kernel instance (the instances share one
+    // function-pointer type, so they are told apart by address).
+    static const void *done[16];
+    static int n_done = 0;
+    bool seen = false;
+    for (int i = 0; i < n_done; i++) seen |= done[i] == (const void *)kernel;
+    if (!seen) {
+        cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (n_done < 16) done[n_done++] = (const void *)kernel;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(warps * 32u);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = P.pdl ? 1 : 0;
+    (void)cudaLaunchKernelEx(&cfg, kernel, P);
 }
 
 int attention_jobs(const AttnJob *jobs, uint32_t n, uint32_t q_heads, uint32_t kv_heads,
@@ -1146,18 +1346,36 @@ int attention_jobs(const AttnJob *jobs, uint32_t n, uint32_t q_heads, uint32_t k
         P.qscale = kLog2e / sqrtf(128.0f);
         for (uint32_t f = 0; f < n_keys; f++) rope_table(P.rope[f], keys[f]);
         P.gat = g_gather_cur ? *g_gather_cur : GatherDev{};
-        if (P.gat.world) P.gat.total_groups = m * kv_heads;
+        // Small launches (a single layer or a few: at most one (job, KV
+        // head) group per two SMs) run one CTA per SM: the f16 kernel in its
+        // 8-warp form, and ns = SMs / groups splits per group, so the split
+        // partials of a group fit the merging CTA's stage buffers in one
+        // pass.  Larger launches keep the plan above.
+        const uint32_t groups = m * kv_heads;
+        const bool small = groups * 2u <= (uint32_t)sms;
+        const int slot = (dtype == SF37KV_F16 ? 0 : 2) + (any_prep ? 1 : 0);
+        P.err = device_error_flag();
         uint32_t ctas = 0;
         bool any_split = false;
         for (uint32_t i = 0; i < m; i++) {
             const AttnJob &A = jobs[base + i];
             const uint32_t rows = A.end - A.start;
-            uint64_t ns = (rows + per - 1) / per;
-            if (ns < 1) ns = 1;
-            if (ns > kMaxSplits) ns = kMaxSplits;
-            uint32_t sr = (uint32_t)((rows + ns - 1) / ns);
-            sr = (sr + 127u) & ~127u;
-            if (sr == 0) sr = 128;
+            uint64_t ns;
+            uint32_t sr;
+            if (small) {
+                ns = (uint32_t)sms / groups;
+                if (ns > kMaxSplits) ns = kMaxSplits;
+                sr = (uint32_t)((rows + ns - 1) / ns);
+                sr = (sr + 15u) & ~15u;
+                if (sr == 0) sr = 16;
+            } else {
+                ns = (rows + per - 1) / per;
+                if (ns < 1) ns = 1;
+                if (ns > kMaxSplits) ns = kMaxSplits;
+                sr = (uint32_t)((rows + ns - 1) / ns);
+                sr = (sr + 127u) & ~127u;
+                if (sr == 0) sr = 128;
+            }
             ns = (rows + sr - 1) / sr;
             if (ns < 1) ns = 1;
             if (ns > 1) any_split = true;
@@ -1177,6 +1395,7 @@ int attention_jobs(const AttnJob *jobs, uint32_t n, uint32_t q_heads, uint32_t k
             ctas += (uint32_t)ns * kv_heads;
         }
         P.total_ctas = ctas;
+        if (P.gat.world) P.gat.total_groups = groups;
         Scratch S;
         if (any_split) {
             if (int rc = scratch_get((uint64_t)ctas * P.part_stride * 4u, (uint64_t)m * kv_heads, &S))
@@ -1184,31 +1403,18 @@ int attention_jobs(const AttnJob *jobs, uint32_t n, uint32_t q_heads, uint32_t k
         }
         P.part = S.part;
         P.counters = S.counters;
-        // Pipelined kernels, 4 warps x 3 cp.async stages; launched with
-        // programmatic dependent launch (PDL).
+        // Pipelined kernels, launched with programmatic dependent launch (PDL).
         P.pdl = 1;
-        if (dtype == SF37KV_F16) {
-            static bool attr = false;
-            if (!attr) {
-                cudaFuncSetAttribute(decode_f16_pipe_kernel<4, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     (int)smem_pipe(4, 3));
-                cudaFuncSetAttribute(decode_f16_pipe_kernel<4, 3, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     (int)(smem_pipe(4, 3) + kPrepSmem));
-                attr = true;
-            }
-            if (any_prep) launch_pipe(decode_f16_pipe_kernel<4, 3, true>, ctas, 128, smem_pipe(4, 3) + kPrepSmem, stream, P);
-            else launch_pipe(decode_f16_pipe_kernel<4, 3>, ctas, 128, smem_pipe(4, 3), stream, P);
-        } else {
-            static bool attr = false;
-            if (!attr) {
-                cudaFuncSetAttribute(decode_f32_pipe_kernel<4, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     (int)smem_pipe32(4, 3));
-                cudaFuncSetAttribute(decode_f32_pipe_kernel<4, 3, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     (int)(smem_pipe32(4, 3) + kPrepSmem));
-                attr = true;
-            }
-            if (any_prep) launch_pipe(decode_f32_pipe_kernel<4, 3, true>, ctas, 128, smem_pipe32(4, 3) + kPrepSmem, stream, P);
-            else launch_pipe(decode_f32_pipe_kernel<4, 3>, ctas, 128, smem_pipe32(4, 3), stream, P);
+        mark_pre(stream, P.job, m);
+        note_stream_appends(stream, P.job, m);
+        switch (slot * 2 + (small ? 1 : 0)) {
+            case 0: launch_decode(decode_f16_pipe_kernel<4, 3, false>, ctas, 4, kSmemF16, stream, P); break;
+            case 1: launch_decode(decode_f16_pipe_kernel<8, 3, false>, ctas, 8, kSmemF16Wide, stream, P); break;
+            case 2: launch_decode(decode_f16_pipe_kernel<4, 3, true>, ctas, 4, kSmemF16 + kPrepSmem, stream, P); break;
+            case 3: launch_decode(decode_f16_pipe_kernel<8, 3, true>, ctas, 8, kSmemF16Wide + kPrepSmem, stream, P); break;
+            case 4:
+            case 5: launch_decode(decode_f32_pipe_kernel<4, 3, false>, ctas, 4, kSmemF32, stream, P); break;
+            default: launch_decode(decode_f32_pipe_kernel<4, 3, true>, ctas, 4, kSmemF32 + kPrepSmem, stream, P); break;
         }
         g_launches++;
         if (int rc = check_cuda(cudaGetLastError(), "attention launch")) return rc;
@@ -1397,6 +1603,7 @@ int attention_jobs_prealloc(const AttnJob *jobs, uint32_t n, uint32_t q_heads, u
     if (per < 256) per = 256;
     DecodeParams P;
     P.pdl = 0;
+    P.err = nullptr;  // no allocation here (the flag would be allocated on first use)
     for (;;) {
         P.n_jobs = n;
         P.q_heads = q_heads;
@@ -1436,6 +1643,7 @@ int attention_jobs_prealloc(const AttnJob *jobs, uint32_t n, uint32_t q_heads, u
         return rc;
     // The same pipelined kernels as sf37kv_decode's defaults (f16: 4 warps x
     // 3 stages; f32: the bf16 hi/lo tensor-core kernel), without PDL.
+    note_stream_appends(stream, P.job, n);
     if (dtype == SF37KV_F16) {
         cudaFuncSetAttribute(decode_f16_pipe_kernel<4, 3>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)smem_pipe(4, 3));

@@ -419,7 +419,7 @@ __global__ void __launch_bounds__(576, 1) prefill_tc05_kernel(const __grid_const
                         xa = fmaxf(xa, x0);
                         xb = fmaxf(xb, x1);
                         const float p0 = fast_exp2(x0);
-                        const float p1 = (POLY > 0 && (i % POLY) == 0) ? exp2_fma(x1) : fast_exp2(x1);
+                        const float p1 = (POLY > 0 && (i % (POLY > 0 ? POLY : 1)) == 0) ? exp2_fma(x1) : fast_exp2(x1);
                         la += p0;
                         lb += p1;
                         w[q2][i] = pack_h2(p0, p1);
@@ -436,7 +436,7 @@ __global__ void __launch_bounds__(576, 1) prefill_tc05_kernel(const __grid_const
                         xa = fmaxf(xa, x0);
                         xb = fmaxf(xb, x1);
                         const float p0 = fast_exp2(x0);
-                        const float p1 = (POLY > 0 && (i % POLY) == 0) ? exp2_fma(x1) : fast_exp2(x1);
+                        const float p1 = (POLY > 0 && (i % (POLY > 0 ? POLY : 1)) == 0) ? exp2_fma(x1) : fast_exp2(x1);
                         la += p0;
                         lb += p1;
                         w[q2][i] = pack_h2(p0, p1);
