@@ -321,8 +321,11 @@ def decode_parity(rank, world, dev, stream, kc, vc, caps, sliding, pos, qh_l, kv
                                            window=512, pos=pos, q=q[l], gate=gate[l], out=out[l])
                                       for l in range(n_layers)])
         if pg is not None:
+            # the kernels write this rank's heads into its own slot of the
+            # peer buffer and store the same values into every other rank's
             pg.step(desc, kv.F16, stream)
             peer = pg.gathered[pg.epoch & 1].clone()
+            out = peer[rank].contiguous()
         else:
             kv.decode(desc, qh_l, kvh_l, HD, kv.F16, stream)
         if world > 1:
@@ -649,6 +652,11 @@ def decode_leg(args, rank, world, wl, headline):
     }
     if parity is not None:
         line["parity"] = parity
+    if world > 1:
+        # max over ranks of each: the whole step, and the decode kernel timed
+        # alone (no append, no gather); the rest is the output gather and
+        # rank skew
+        line["phases"] = {"step_ms": ms, "decode_kernel_ms": att_ms, "gather_and_skew_ms": ms - att_ms}
     if op_line:
         line["oproj"] = op_line
     del kc, vc, all_desc, e2e_desc, bufs
@@ -1138,7 +1146,8 @@ def session_leg(dev, layers, kd, rows):
 
 # ---------------------------------------------------------------- drivers
 def _compact_decode(line):
-    keep = ("value", "unit", "ms_per_step", "kv_read_GBps", "roofline", "e2e", "parity", "gpu_launches", "clocks")
+    keep = ("value", "unit", "ms_per_step", "kv_read_GBps", "roofline", "e2e", "parity", "phases", "gpu_launches",
+            "clocks")
     d = {"workload": line["config"]["workload"], "ctx": line["config"]["ctx"]}
     d.update({k: line[k] for k in keep if k in line})
     return d

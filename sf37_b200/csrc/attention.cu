@@ -1307,7 +1307,14 @@ int attention_jobs(const AttnJob *jobs, uint32_t n, uint32_t q_heads, uint32_t k
             per = ((per + 127) / 128) * 128;
             if (per < 128) per = 128;
             const uint64_t ctas1 = (uint64_t)m * kv_heads;
-            if (ctas1 <= slots) {
+            uint64_t longest = 0;
+            for (uint32_t i = 0; i < m; i++) longest = std::max<uint64_t>(longest, jobs[base + i].end - jobs[base + i].start);
+            // Jobs of very different lengths (full and sliding layers): size
+            // CTAs by rows, not by jobs, so one long job's splits do not pile
+            // onto a few SMs (config 3 on 2 GPUs: 192 groups, 48 of them 65K
+            // rows, the rest 512).
+            const bool mixed = longest * ctas1 > 2u * total;
+            if (ctas1 <= slots && !mixed) {
                 // Per-job split count (jobs of similar length): the one whose
                 // CTAs fill whole waves best, i.e. the fewest waves per unit of
                 // work, ceil(ns * ctas1 / slots) / ns; ties go to fewer splits
@@ -1322,18 +1329,16 @@ int attention_jobs(const AttnJob *jobs, uint32_t n, uint32_t q_heads, uint32_t k
                         ns = c;
                     }
                 }
-                uint64_t longest = 0;
-                for (uint32_t i = 0; i < m; i++) longest = std::max<uint64_t>(longest, jobs[base + i].end - jobs[base + i].start);
                 per = ((longest + ns - 1) / ns + 127) / 128 * 128;
                 if (per < 128) per = 128;
-            } else if (per > 8192) {
+            } else if (per > 8192 || mixed) {
                 // More (layer, head) groups than one wave holds, with a few
                 // long jobs among many short ones (config 3: 12 full layers of
                 // 65K rows and 36 sliding layers of 512): one-wave sizing makes
                 // the long jobs' CTAs huge, and their tail cannot overlap the
                 // next launch.  Measured on config 3: 21.6K rows per CTA 1682
                 // tok/s, 8192 rows 2002 tok/s.
-                per = 8192;
+                if (per > 8192) per = 8192;
             }
         }
         DecodeParams P;
@@ -1363,7 +1368,9 @@ int attention_jobs(const AttnJob *jobs, uint32_t n, uint32_t q_heads, uint32_t k
             uint64_t ns;
             uint32_t sr;
             if (small) {
-                ns = (uint32_t)sms / groups;
+                // splits in proportion to the job's share of all rows
+                ns = (uint64_t)sms * rows / (total ? total : 1);
+                if (ns < 1) ns = 1;
                 if (ns > kMaxSplits) ns = kMaxSplits;
                 sr = (uint32_t)((rows + ns - 1) / ns);
                 sr = (sr + 15u) & ~15u;

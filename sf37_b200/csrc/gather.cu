@@ -21,6 +21,11 @@ namespace sf37kv {
 
 extern unsigned long long g_launches;
 
+// Launched with programmatic stream serialization right behind the decode
+// kernel (which triggers its dependents at its start), so it is resident and
+// polling while the decode runs.  It returns only after griddepcontrol.wait,
+// i.e. after the decode kernel has completed, so work after it on the stream
+// sees a finished step.
 __global__ void gather_wait_kernel(const uint32_t *flags, uint32_t world, uint32_t epoch, int *err) {
     const uint32_t p = threadIdx.x;
     bool ok = true;
@@ -38,6 +43,7 @@ __global__ void gather_wait_kernel(const uint32_t *flags, uint32_t world, uint32
         }
     }
     if (!ok) atomicExch(err, 2);
+    asm volatile("griddepcontrol.wait;" ::: "memory");
 }
 
 }  // namespace sf37kv
@@ -127,7 +133,16 @@ extern "C" int sf37kv_gather_wait(const sf37kv_peer_gather *g, uint32_t epoch, v
     int *err = device_error_flag();
     if (!err) return set_error(SF37KV_ECUDA, "gather_wait: no device error flag");
     cudaStream_t s = stream ? (cudaStream_t)stream : current_stream();
-    gather_wait_kernel<<<1, 32, 0, s>>>((const uint32_t *)g->my_flags, g->world, epoch, err);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(1);
+    cfg.blockDim = dim3(32);
+    cfg.stream = s;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    (void)cudaLaunchKernelEx(&cfg, gather_wait_kernel, (const uint32_t *)g->my_flags, g->world, epoch, err);
     g_launches++;
     return check_cuda(cudaGetLastError(), "gather wait launch");
 }
