@@ -89,6 +89,49 @@ int sf37kv_session_save_payload(const sf37kv_session *s, int fd, char *err, size
 int sf37kv_session_load_payload(sf37kv_session *s, int fd, uint64_t payload_bytes, char *err,
                                 size_t errlen);
 
+/* ---- sf37_kvstore records (the files the server's disk KV cache holds) ----
+ * Record = 48-byte header, 4-byte little-endian text length, the cached
+ * text, then the session payload (format 3) and an optional trailer owned
+ * by the server's hooks.  The file is named "<sha1 of text>.kv".
+ *   sf37kv_kvstore_fill_header  <- sf37_kvstore_fill_header (sf37_kvstore.c:399-421)
+ *   sf37kv_kvstore_parse_header <- sf37_kvstore_read_header (sf37_kvstore.c:423-446):
+ *                                  1 when magic/version/ABI match, tokens != 0
+ *                                  and quant_bits == 3; h holds the header
+ *                                  and the text length (52 bytes)
+ *   sf37kv_sha1_hex             <- sf37_kvstore_sha1_bytes_hex (sf37_kvstore.c:327)
+ *   sf37kv_kvstore_save         <- the record write of sf37_kvstore_store_live_prefix_text
+ *                                  (sf37_kvstore.c:1052-1079), without the trailer:
+ *                                  writes at fd's current offset; the payload
+ *                                  streams from the device caches (no staging
+ *                                  file); model 37, quant 3, hits 0, created =
+ *                                  last used = now
+ *   sf37kv_kvstore_load         <- the checks and payload load of
+ *                                  sf37_kvstore_try_load_text (sf37_kvstore.c:1249-1303),
+ *                                  reading from fd's current offset; prompt is
+ *                                  the incoming prompt text, sha_expected the
+ *                                  file's name key or NULL.  Messages are the
+ *                                  reference's ("invalid header", "cached text
+ *                                  hash mismatch", ...). */
+#define SF37KV_KVSTORE_HEADER 48
+#define SF37KV_KVSTORE_MODEL_ID 37
+#define SF37KV_KVSTORE_QUANT_BITS 3
+#define SF37KV_KVSTORE_REASON_MAX 6
+typedef struct {
+    uint8_t quant_bits, model_id, reason, ext_flags;
+    uint32_t tokens, hits, ctx_size, text_bytes;
+    uint64_t created_at, last_used, payload_bytes;
+} sf37kv_kvstore_entry;
+void sf37kv_kvstore_fill_header(uint8_t h[SF37KV_KVSTORE_HEADER], uint8_t model_id, uint8_t quant_bits,
+                                uint8_t reason, uint8_t ext_flags, uint32_t tokens, uint32_t hits,
+                                uint32_t ctx_size, uint64_t created_at, uint64_t last_used,
+                                uint64_t payload_bytes);
+int sf37kv_kvstore_parse_header(const uint8_t h[SF37KV_KVSTORE_HEADER + 4], sf37kv_kvstore_entry *e);
+void sf37kv_sha1_hex(const void *data, size_t len, char out[41]);
+int sf37kv_kvstore_save(const sf37kv_session *s, int fd, const char *text, uint32_t text_len, uint8_t reason,
+                        uint8_t ext_flags, uint64_t now, uint64_t *record_bytes, char *err, size_t errlen);
+int sf37kv_kvstore_load(sf37kv_session *s, int fd, const char *prompt, size_t prompt_len,
+                        const char *sha_expected, uint32_t *tokens_loaded, char *err, size_t errlen);
+
 #ifdef __cplusplus
 }
 #endif

@@ -273,3 +273,40 @@ void sf37ref_qk_prep(float *x, uint32_t n_head, const float *w, uint32_t rotary_
     head_rms_norm_weight1(x, n_head, SF37_HEAD_DIM, w, SF37_RMS_EPS);
     apply_rope_one(x, n_head, SF37_HEAD_DIM, rotary_dim, theta, llama3 != 0, pos);
 }
+
+/* ---- sf37_kvstore records through the reference's own store path ----
+ * sf37_kvstore_store_live_prefix_text (sf37_kvstore.c:929-1158) on a
+ * CPU-backend session, with the text given (cache_text_override), into a
+ * kvstore opened on `dir` (min_tokens 1).  The record lands in
+ * dir/<sha1(text)>.kv.  Returns 1 when the reference stored it. */
+#include "sf37_kvstore.h"
+
+int sf37ref_kvstore_store(const char *dir, int ctx, const int *tokens, int n_tokens, float *logits,
+                          float *hidden, float **k, float **v, const uint32_t *n_rows, const char *text,
+                          char *err, size_t errlen) {
+    sf37_session s;
+    sf37ref_session_init(&s, ctx, tokens, n_tokens, logits, hidden, k, v, n_rows);
+    sf37_kvstore kc;
+    sf37_kvstore_options opt = sf37_kvstore_default_options();
+    opt.min_tokens = 1;
+    int ok = 0;
+    if (sf37_kvstore_open(&kc, dir, 1u << 20, false, opt, "ref", NULL, NULL)) {
+        sf37_tokens tk = {0};
+        for (int i = 0; i < n_tokens; i++) sf37_tokens_push(&tk, tokens[i]);
+        ok = sf37_kvstore_store_live_prefix_text(&kc, NULL, &s, &tk, n_tokens, "cold", text, 0, NULL, NULL, err,
+                                                 errlen) ? 1 : 0;
+        sf37_tokens_free(&tk);
+        sf37_kvstore_close(&kc);
+    }
+    free(s.checkpoint.v);
+    return ok;
+}
+
+void sf37ref_kvstore_fill_header(uint8_t *h, uint8_t model_id, uint8_t quant_bits, uint8_t reason,
+                                 uint8_t ext_flags, uint32_t tokens, uint32_t hits, uint32_t ctx_size,
+                                 uint64_t created_at, uint64_t last_used, uint64_t payload_bytes) {
+    sf37_kvstore_fill_header(h, model_id, quant_bits, reason, ext_flags, tokens, hits, ctx_size, created_at,
+                             last_used, payload_bytes);
+}
+
+void sf37ref_sha1_hex(const void *p, size_t n, char out[41]) { sf37_kvstore_sha1_bytes_hex(p, n, out); }

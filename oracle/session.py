@@ -236,3 +236,35 @@ def slice_columns(kind, kv=1024, group=64, col0=0, width=1024):
         return [(4 * col0, 4 * width)]
     groups = kv // group
     return [(4 * (col0 // group), 4 * (width // group)), (4 * groups + col0, width)]
+
+
+def ref_kvstore_store(directory, ctx, tokens, logits, hidden, k_rows, v_rows, text):
+    """The reference's own sf37_kvstore_store_live_prefix_text on a CPU
+    session (45 layers; k_rows[il] the layer's live rows in position order)
+    with the cached text given.  Returns the record file's bytes."""
+    import hashlib
+    import os
+    R = ref()
+    if not getattr(R, "_kvstore_bound", False):
+        R.sf37ref_kvstore_store.restype = ctypes.c_int
+        R.sf37ref_kvstore_store.argtypes = [ctypes.c_char_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_int,
+                                            ctypes.c_void_p, ctypes.c_void_p, _fpp, _fpp, ctypes.c_void_p,
+                                            ctypes.c_char_p, ctypes.c_char_p, ctypes.c_size_t]
+        R._kvstore_bound = True
+    n = LAYOUT["n_layers"]
+    toks = np.ascontiguousarray(tokens, np.int32)
+    lg = np.ascontiguousarray(logits, np.float32)
+    hd = np.ascontiguousarray(hidden, np.float32)
+    ks = [np.ascontiguousarray(k, np.float32) for k in k_rows]
+    vs = [np.ascontiguousarray(v, np.float32) for v in v_rows]
+    kp = (ctypes.c_void_p * n)(*[k.ctypes.data for k in ks])
+    vp = (ctypes.c_void_p * n)(*[v.ctypes.data for v in vs])
+    nr = np.array([k.shape[0] for k in ks], np.uint32)
+    err = ctypes.create_string_buffer(512)
+    tb = text.encode() if isinstance(text, str) else bytes(text)
+    if not R.sf37ref_kvstore_store(directory.encode(), ctx, _ptr(toks), len(toks), _ptr(lg), _ptr(hd), kp, vp,
+                                   _ptr(nr), tb, err, 512):
+        raise LoadError(err.value.decode() or "reference kvstore store failed")
+    path = os.path.join(directory, hashlib.sha1(tb).hexdigest() + ".kv")
+    with open(path, "rb") as f:
+        return f.read()

@@ -62,6 +62,12 @@ class Session(ctypes.Structure):
                 ("dtype", c_int), ("backend_kind", c_u32)]
 
 
+class KvstoreEntry(ctypes.Structure):
+    _fields_ = [("quant_bits", ctypes.c_uint8), ("model_id", ctypes.c_uint8), ("reason", ctypes.c_uint8),
+                ("ext_flags", ctypes.c_uint8), ("tokens", c_u32), ("hits", c_u32), ("ctx_size", c_u32),
+                ("text_bytes", c_u32), ("created_at", c_u64), ("last_used", c_u64), ("payload_bytes", c_u64)]
+
+
 class CachePlan(ctypes.Structure):
     _fields_ = [("ctx_size", c_u32), ("window", c_u32), ("sliding_cap", c_u32), ("prefill_cap", c_u32),
                 ("full_layers", c_u32), ("sliding_layers", c_u32), ("cap", c_u32 * 64), ("sliding", c_u32 * 64),
@@ -156,6 +162,14 @@ SIGNATURES = {
     "sf37kv_session_load_snapshot": (c_int, [SP, c_vp, c_u64, ctypes.c_char_p, ctypes.c_size_t]),
     "sf37kv_session_save_payload": (c_int, [SP, c_int, ctypes.c_char_p, ctypes.c_size_t]),
     "sf37kv_session_load_payload": (c_int, [SP, c_int, c_u64, ctypes.c_char_p, ctypes.c_size_t]),
+    "sf37kv_kvstore_fill_header": (None, [c_vp, ctypes.c_uint8, ctypes.c_uint8, ctypes.c_uint8, ctypes.c_uint8,
+                                          c_u32, c_u32, c_u32, c_u64, c_u64, c_u64]),
+    "sf37kv_kvstore_parse_header": (c_int, [c_vp, ctypes.POINTER(KvstoreEntry)]),
+    "sf37kv_sha1_hex": (None, [c_vp, ctypes.c_size_t, ctypes.c_char_p]),
+    "sf37kv_kvstore_save": (c_int, [SP, c_int, ctypes.c_char_p, c_u32, ctypes.c_uint8, ctypes.c_uint8, c_u64,
+                                    ctypes.POINTER(c_u64), ctypes.c_char_p, ctypes.c_size_t]),
+    "sf37kv_kvstore_load": (c_int, [SP, c_int, ctypes.c_char_p, ctypes.c_size_t, ctypes.c_char_p,
+                                    ctypes.POINTER(c_u32), ctypes.c_char_p, ctypes.c_size_t]),
 }
 
 _lib = None

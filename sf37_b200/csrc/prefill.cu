@@ -22,6 +22,14 @@ int prefill_tc05(const sf37kv_cache *cache, const void *q, const float *gate, fl
 int prefill_tc(const sf37kv_cache *cache, const void *q, int q_type, const float *gate, float *out,
                uint32_t pos0, uint32_t n_tok, uint32_t q_heads, uint32_t kv_heads,
                cudaStream_t stream, bool *handled);
+int prefill_tc32(const sf37kv_cache *cache, const float *q, const float *gate, float *out, uint32_t pos0,
+                 uint32_t n_tok, uint32_t q_heads, uint32_t kv_heads, cudaStream_t stream, bool *handled);
+
+// f32 caches: the tensor-core kernel where its shape conditions hold, else
+// every token as a split-K decode job.
+static int prefill_f32_any(const sf37kv_cache *c, const float *q, const float *gate, float *out, uint32_t pos0,
+                           uint32_t n_tok, uint32_t q_heads, uint32_t kv_heads, uint32_t head_dim,
+                           cudaStream_t stream);
 
 __global__ static void bf16_to_f32_kernel(const uint16_t *src, float *dst, uint64_t n) {
     const uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -106,8 +114,22 @@ extern "C" int sf37kv_prefill(const sf37kv_cache *cache, const void *q, int q_ty
         if (int rc = check_cuda(cudaGetLastError(), "bf16 convert launch")) return rc;
         qf = g_qconv;
     }
+    if (dtype == SF37KV_F32) return prefill_f32_any(cache, qf, gate, out, pos0, n_tok, q_heads, kv_heads, head_dim, s);
     return prefill_jobs(cache, qf, gate, out, pos0, n_tok, q_heads, kv_heads, head_dim, dtype, s);
 }
+
+namespace sf37kv {
+static int prefill_f32_any(const sf37kv_cache *c, const float *q, const float *gate, float *out, uint32_t pos0,
+                           uint32_t n_tok, uint32_t q_heads, uint32_t kv_heads, uint32_t head_dim,
+                           cudaStream_t stream) {
+    if (head_dim == 128) {
+        bool handled = false;
+        if (int rc = prefill_tc32(c, q, gate, out, pos0, n_tok, q_heads, kv_heads, stream, &handled)) return rc;
+        if (handled) return SF37KV_OK;
+    }
+    return prefill_jobs(c, q, gate, out, pos0, n_tok, q_heads, kv_heads, head_dim, SF37KV_F32, stream);
+}
+}  // namespace sf37kv
 
 extern "C" int sf37_cuda_attention_prefill_heads(sf37_cuda_tensor *out_heads, const sf37_cuda_tensor *q,
                                                  const sf37_cuda_tensor *k_cache,
@@ -126,8 +148,8 @@ extern "C" int sf37_cuda_attention_prefill_heads(sf37_cuda_tensor *out_heads, co
         k_cache->bytes < (uint64_t)cache_cap * kv_dim * 4 || v_cache->bytes < (uint64_t)cache_cap * kv_dim * 4)
         return 0;
     sf37kv_cache c{k_cache->ptr, v_cache->ptr, cache_cap, (uint32_t)(sliding != 0), window, 0};
-    if (prefill_jobs(&c, (const float *)q->ptr, (const float *)head_gate->ptr, (float *)out_heads->ptr,
-                     pos0, n_tok, q_heads, kv_heads, head_dim, SF37KV_F32, current_stream())) {
+    if (prefill_f32_any(&c, (const float *)q->ptr, (const float *)head_gate->ptr, (float *)out_heads->ptr,
+                        pos0, n_tok, q_heads, kv_heads, head_dim, current_stream())) {
         fprintf(stderr, "sf37: attention_prefill_heads failed: %s\n", sf37kv_last_error());
         return 0;
     }

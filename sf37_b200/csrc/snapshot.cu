@@ -14,6 +14,7 @@
 // These kernels are HBM- (device buffer) or link- (mapped host buffer) bound.
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 #include <thread>
 #include <vector>
 
@@ -465,27 +466,48 @@ static int launch_layers(void *buf, const sf37kv_pack_layer *layers, uint32_t n,
 }
 
 // ---------------------------------------------------------------- host staging
-// Two device staging buffers and a copy stream, created on first use and
-// kept for the process (freed by sf37_cuda_cleanup via staging_release()).
+// Per device: two device staging buffers, two pinned host buffers, a work
+// stream and events, created on first use on that device and kept for the
+// process (freed by sf37_cuda_cleanup via staging_release()).  A mutex per
+// device serializes the pipelines that share them (host threads calling
+// concurrently on one device wait for each other).
 constexpr uint64_t kStageBytes = 64ull << 20;
-static void *g_stage[2] = {nullptr, nullptr};
-static cudaStream_t g_copy_stream = nullptr, g_work_stream = nullptr;
-static cudaEvent_t g_ev_packed[2], g_ev_copied[2], g_ev_start;
+struct Staging {
+    bool ready = false, host_ready = false;
+    void *stage[2] = {nullptr, nullptr};
+    cudaStream_t copy = nullptr, work = nullptr;
+    cudaEvent_t ev_packed[2], ev_copied[2], ev_start;
+    void *hbuf[2] = {nullptr, nullptr};
+    cudaEvent_t ev_host[2];
+    std::mutex mu;
+};
+constexpr int kMaxStagingDevices = 64;
+static Staging g_staging[kMaxStagingDevices];
 
-static int staging_init() {
-    if (g_stage[0]) return SF37KV_OK;
+// The current device's staging set (not yet initialized).
+static int current_staging(Staging **out) {
+    int dev = 0;
+    if (int rc = check_cuda(cudaGetDevice(&dev), "staging get device")) return rc;
+    if (dev < 0 || dev >= kMaxStagingDevices)
+        return set_error(SF37KV_EUNSUPPORTED, "staging: device %d out of range", dev);
+    *out = &g_staging[dev];
+    return SF37KV_OK;
+}
+
+static int staging_init(Staging &S) {
+    if (S.ready) return SF37KV_OK;
     for (int i = 0; i < 2; i++)
-        if (int rc = check_cuda(cudaMalloc(&g_stage[i], kStageBytes), "staging alloc")) return rc;
-    if (int rc = check_cuda(cudaStreamCreateWithFlags(&g_copy_stream, cudaStreamNonBlocking), "stream"))
-        return rc;
-    if (int rc = check_cuda(cudaStreamCreateWithFlags(&g_work_stream, cudaStreamNonBlocking), "stream"))
-        return rc;
+        if (int rc = check_cuda(cudaMalloc(&S.stage[i], kStageBytes), "staging alloc")) return rc;
+    if (int rc = check_cuda(cudaStreamCreateWithFlags(&S.copy, cudaStreamNonBlocking), "stream")) return rc;
+    if (int rc = check_cuda(cudaStreamCreateWithFlags(&S.work, cudaStreamNonBlocking), "stream")) return rc;
     for (int i = 0; i < 2; i++) {
-        cudaEventCreateWithFlags(&g_ev_packed[i], cudaEventDisableTiming);
-        cudaEventCreateWithFlags(&g_ev_copied[i], cudaEventDisableTiming);
+        cudaEventCreateWithFlags(&S.ev_packed[i], cudaEventDisableTiming);
+        cudaEventCreateWithFlags(&S.ev_copied[i], cudaEventDisableTiming);
     }
-    cudaEventCreateWithFlags(&g_ev_start, cudaEventDisableTiming);
-    return check_cuda(cudaGetLastError(), "staging events");
+    cudaEventCreateWithFlags(&S.ev_start, cudaEventDisableTiming);
+    if (int rc = check_cuda(cudaGetLastError(), "staging events")) return rc;
+    S.ready = true;
+    return SF37KV_OK;
 }
 
 // Splits each layer's section into chunks of at most kStageBytes and runs
@@ -494,14 +516,18 @@ static int host_pipeline(void *host, const sf37kv_pack_layer *layers, uint32_t n
                          int dtype, int fmt, uint32_t group, int variant, int dir) {
     if (int rc = validate(kv_dim, dtype, fmt, group)) return rc;
     if (!host && n) return set_error(SF37KV_EINVAL, "pack: host buffer is NULL");
-    if (int rc = staging_init()) return rc;
+    Staging *SP = nullptr;
+    if (int rc = current_staging(&SP)) return rc;
+    Staging &S = *SP;
+    std::lock_guard<std::mutex> lk(S.mu);
+    if (int rc = staging_init(S)) return rc;
     const uint64_t rb = row_bytes_of(kv_dim, fmt, group);
     const uint64_t chunk_rows = kStageBytes / (2 * rb);
     if (chunk_rows == 0) return set_error(SF37KV_EUNSUPPORTED, "pack: row larger than staging");
     // Order after everything already queued on the library stream.
-    cudaEventRecord(g_ev_start, current_stream());
-    cudaStreamWaitEvent(g_work_stream, g_ev_start, 0);
-    cudaStreamWaitEvent(g_copy_stream, g_ev_start, 0);
+    cudaEventRecord(S.ev_start, current_stream());
+    cudaStreamWaitEvent(S.work, S.ev_start, 0);
+    cudaStreamWaitEvent(S.copy, S.ev_start, 0);
     int buf = 0;
     bool used[2] = {false, false};
     for (uint32_t i = 0; i < n; i++) {
@@ -515,34 +541,34 @@ static int host_pipeline(void *host, const sf37kv_pack_layer *layers, uint32_t n
             const uint64_t bytes = 2ull * nr * rb;
             uint8_t *h = (uint8_t *)host + L.offset + 2ull * r0 * rb;
             if (dir == 0) {
-                if (used[buf]) cudaStreamWaitEvent(g_work_stream, g_ev_copied[buf], 0);
-                if (int rc = launch_layers(g_stage[buf], &c, 1, kv_dim, dtype, fmt, group, variant, 0,
-                                           g_work_stream))
+                if (used[buf]) cudaStreamWaitEvent(S.work, S.ev_copied[buf], 0);
+                if (int rc = launch_layers(S.stage[buf], &c, 1, kv_dim, dtype, fmt, group, variant, 0,
+                                           S.work))
                     return rc;
-                cudaEventRecord(g_ev_packed[buf], g_work_stream);
-                cudaStreamWaitEvent(g_copy_stream, g_ev_packed[buf], 0);
-                if (int rc = check_cuda(cudaMemcpyAsync(h, g_stage[buf], bytes, cudaMemcpyDeviceToHost,
-                                                        g_copy_stream), "pack D2H"))
+                cudaEventRecord(S.ev_packed[buf], S.work);
+                cudaStreamWaitEvent(S.copy, S.ev_packed[buf], 0);
+                if (int rc = check_cuda(cudaMemcpyAsync(h, S.stage[buf], bytes, cudaMemcpyDeviceToHost,
+                                                        S.copy), "pack D2H"))
                     return rc;
-                cudaEventRecord(g_ev_copied[buf], g_copy_stream);
+                cudaEventRecord(S.ev_copied[buf], S.copy);
             } else {
-                if (used[buf]) cudaStreamWaitEvent(g_copy_stream, g_ev_packed[buf], 0);
-                if (int rc = check_cuda(cudaMemcpyAsync(g_stage[buf], h, bytes, cudaMemcpyHostToDevice,
-                                                        g_copy_stream), "unpack H2D"))
+                if (used[buf]) cudaStreamWaitEvent(S.copy, S.ev_packed[buf], 0);
+                if (int rc = check_cuda(cudaMemcpyAsync(S.stage[buf], h, bytes, cudaMemcpyHostToDevice,
+                                                        S.copy), "unpack H2D"))
                     return rc;
-                cudaEventRecord(g_ev_copied[buf], g_copy_stream);
-                cudaStreamWaitEvent(g_work_stream, g_ev_copied[buf], 0);
-                if (int rc = launch_layers(g_stage[buf], &c, 1, kv_dim, dtype, fmt, group, variant, 1,
-                                           g_work_stream))
+                cudaEventRecord(S.ev_copied[buf], S.copy);
+                cudaStreamWaitEvent(S.work, S.ev_copied[buf], 0);
+                if (int rc = launch_layers(S.stage[buf], &c, 1, kv_dim, dtype, fmt, group, variant, 1,
+                                           S.work))
                     return rc;
-                cudaEventRecord(g_ev_packed[buf], g_work_stream);
+                cudaEventRecord(S.ev_packed[buf], S.work);
             }
             used[buf] = true;
             buf ^= 1;
         }
     }
-    if (int rc = check_cuda(cudaStreamSynchronize(g_copy_stream), "pack copy sync")) return rc;
-    if (int rc = check_cuda(cudaStreamSynchronize(g_work_stream), "pack work sync")) return rc;
+    if (int rc = check_cuda(cudaStreamSynchronize(S.copy), "pack copy sync")) return rc;
+    if (int rc = check_cuda(cudaStreamSynchronize(S.work), "pack work sync")) return rc;
     // Later work on the library stream must see restored caches.
     return SF37KV_OK;
 }
@@ -554,17 +580,15 @@ static int host_pipeline(void *host, const sf37kv_pack_layer *layers, uint32_t n
 // host produces chunk c while the device copies in and unpacks chunk c-1
 // (unpack).  A chunk is a run of whole rows of one or more consecutive layer
 // sections, so the callback sees the sections' bytes in order.
-static void *g_hbuf[2] = {nullptr, nullptr};
-static cudaEvent_t g_ev_host[2];
-
-static int host_buffers_init() {
-    if (int rc = staging_init()) return rc;
-    if (g_hbuf[0]) return SF37KV_OK;
+static int host_buffers_init(Staging &S) {
+    if (int rc = staging_init(S)) return rc;
+    if (S.host_ready) return SF37KV_OK;
     for (int i = 0; i < 2; i++) {
-        if (int rc = check_cuda(cudaHostAlloc(&g_hbuf[i], kStageBytes, cudaHostAllocDefault), "pinned stream buffer"))
+        if (int rc = check_cuda(cudaHostAlloc(&S.hbuf[i], kStageBytes, cudaHostAllocDefault), "pinned stream buffer"))
             return rc;
-        if (int rc = check_cuda(cudaEventCreateWithFlags(&g_ev_host[i], cudaEventDisableTiming), "event")) return rc;
+        if (int rc = check_cuda(cudaEventCreateWithFlags(&S.ev_host[i], cudaEventDisableTiming), "event")) return rc;
     }
+    S.host_ready = true;
     return SF37KV_OK;
 }
 
@@ -618,62 +642,70 @@ struct Chunker {
 int pack_stream(const sf37kv_pack_layer *layers, uint32_t n, uint32_t kv_dim, int dtype, int fmt,
                 uint32_t group, int (*sink)(const void *, uint64_t, void *), void *ctx) {
     if (int rc = validate(kv_dim, dtype, fmt, group)) return rc;
-    if (int rc = host_buffers_init()) return rc;
+    Staging *SP = nullptr;
+    if (int rc = current_staging(&SP)) return rc;
+    Staging &S = *SP;
+    std::lock_guard<std::mutex> lk(S.mu);
+    if (int rc = host_buffers_init(S)) return rc;
     const uint64_t rb = row_bytes_of(kv_dim, fmt, group);
     Chunker ck{layers, n, 0, 0, rb, kStageBytes / (2 * rb)};
     if (ck.cap_rows == 0) return set_error(SF37KV_EUNSUPPORTED, "pack: row larger than staging");
-    cudaEventRecord(g_ev_start, current_stream());
-    cudaStreamWaitEvent(g_work_stream, g_ev_start, 0);
+    cudaEventRecord(S.ev_start, current_stream());
+    cudaStreamWaitEvent(S.work, S.ev_start, 0);
     Chunk c;
     uint64_t pending[2] = {0, 0};
     int b = 0, rc = SF37KV_OK;
     bool have_prev = false;
     while (rc == SF37KV_OK && ck.next(&c)) {
         // buffer b was consumed by the host before the previous iteration ended
-        rc = launch_layers(g_stage[b], c.piece, c.n, kv_dim, dtype, fmt, group, 1, 0, g_work_stream);
-        if (!rc) rc = check_cuda(cudaMemcpyAsync(g_hbuf[b], g_stage[b], c.bytes, cudaMemcpyDeviceToHost,
-                                                 g_work_stream), "stream D2H");
-        if (!rc) rc = check_cuda(cudaEventRecord(g_ev_host[b], g_work_stream), "event");
+        rc = launch_layers(S.stage[b], c.piece, c.n, kv_dim, dtype, fmt, group, 1, 0, S.work);
+        if (!rc) rc = check_cuda(cudaMemcpyAsync(S.hbuf[b], S.stage[b], c.bytes, cudaMemcpyDeviceToHost,
+                                                 S.work), "stream D2H");
+        if (!rc) rc = check_cuda(cudaEventRecord(S.ev_host[b], S.work), "event");
         pending[b] = c.bytes;
         if (!rc && have_prev) {
-            rc = check_cuda(cudaEventSynchronize(g_ev_host[b ^ 1]), "stream sync");
-            if (!rc && sink(g_hbuf[b ^ 1], pending[b ^ 1], ctx)) rc = SF37KV_EINVAL;
+            rc = check_cuda(cudaEventSynchronize(S.ev_host[b ^ 1]), "stream sync");
+            if (!rc && sink(S.hbuf[b ^ 1], pending[b ^ 1], ctx)) rc = SF37KV_EINVAL;
         }
         have_prev = true;
         b ^= 1;
     }
     if (!rc && have_prev) {
-        rc = check_cuda(cudaEventSynchronize(g_ev_host[b ^ 1]), "stream sync");
-        if (!rc && sink(g_hbuf[b ^ 1], pending[b ^ 1], ctx)) rc = SF37KV_EINVAL;
+        rc = check_cuda(cudaEventSynchronize(S.ev_host[b ^ 1]), "stream sync");
+        if (!rc && sink(S.hbuf[b ^ 1], pending[b ^ 1], ctx)) rc = SF37KV_EINVAL;
     }
-    (void)cudaStreamSynchronize(g_work_stream);
+    (void)cudaStreamSynchronize(S.work);
     return rc;
 }
 
 int unpack_stream(const sf37kv_pack_layer *layers, uint32_t n, uint32_t kv_dim, int dtype, int fmt,
                   uint32_t group, int (*source)(void *, uint64_t, void *), void *ctx) {
     if (int rc = validate(kv_dim, dtype, fmt, group)) return rc;
-    if (int rc = host_buffers_init()) return rc;
+    Staging *SP = nullptr;
+    if (int rc = current_staging(&SP)) return rc;
+    Staging &S = *SP;
+    std::lock_guard<std::mutex> lk(S.mu);
+    if (int rc = host_buffers_init(S)) return rc;
     const uint64_t rb = row_bytes_of(kv_dim, fmt, group);
     Chunker ck{layers, n, 0, 0, rb, kStageBytes / (2 * rb)};
     if (ck.cap_rows == 0) return set_error(SF37KV_EUNSUPPORTED, "pack: row larger than staging");
-    cudaEventRecord(g_ev_start, current_stream());
-    cudaStreamWaitEvent(g_work_stream, g_ev_start, 0);
+    cudaEventRecord(S.ev_start, current_stream());
+    cudaStreamWaitEvent(S.work, S.ev_start, 0);
     Chunk c;
     int b = 0, rc = SF37KV_OK;
     bool used[2] = {false, false};
     while (rc == SF37KV_OK && ck.next(&c)) {
         // the H2D copy of chunk c-2 out of this host buffer must be done
-        if (used[b]) rc = check_cuda(cudaEventSynchronize(g_ev_host[b]), "stream sync");
-        if (!rc && source(g_hbuf[b], c.bytes, ctx)) rc = SF37KV_EINVAL;
-        if (!rc) rc = check_cuda(cudaMemcpyAsync(g_stage[b], g_hbuf[b], c.bytes, cudaMemcpyHostToDevice,
-                                                 g_work_stream), "stream H2D");
-        if (!rc) rc = check_cuda(cudaEventRecord(g_ev_host[b], g_work_stream), "event");
-        if (!rc) rc = launch_layers(g_stage[b], c.piece, c.n, kv_dim, dtype, fmt, group, 1, 1, g_work_stream);
+        if (used[b]) rc = check_cuda(cudaEventSynchronize(S.ev_host[b]), "stream sync");
+        if (!rc && source(S.hbuf[b], c.bytes, ctx)) rc = SF37KV_EINVAL;
+        if (!rc) rc = check_cuda(cudaMemcpyAsync(S.stage[b], S.hbuf[b], c.bytes, cudaMemcpyHostToDevice,
+                                                 S.work), "stream H2D");
+        if (!rc) rc = check_cuda(cudaEventRecord(S.ev_host[b], S.work), "event");
+        if (!rc) rc = launch_layers(S.stage[b], c.piece, c.n, kv_dim, dtype, fmt, group, 1, 1, S.work);
         used[b] = true;
         b ^= 1;
     }
-    const int rs = check_cuda(cudaStreamSynchronize(g_work_stream), "stream sync");
+    const int rs = check_cuda(cudaStreamSynchronize(S.work), "stream sync");
     return rc ? rc : rs;
 }
 
@@ -754,57 +786,63 @@ static int slice_pipeline(void *host, const sf37kv_pack_layer *layers, uint32_t 
         (fmt == SF37KV_FMT_I8_GROUPED && col0 % group))
         return set_error(SF37KV_EINVAL, "pack slice: columns [%u, %u) do not fit %u (payload: group-aligned)", col0,
                          col0 + kv_dim, full_kv_dim);
-    if (int rc = host_buffers_init()) return rc;
+    Staging *SP = nullptr;
+    if (int rc = current_staging(&SP)) return rc;
+    Staging &S = *SP;
+    std::lock_guard<std::mutex> lk(S.mu);
+    if (int rc = host_buffers_init(S)) return rc;
     SliceGeom G{kv_dim, full_kv_dim, col0, group, fmt, row_bytes_of(kv_dim, fmt, group),
                 row_bytes_of(full_kv_dim, fmt, group)};
     Chunker ck{layers, n, 0, 0, G.rb, kStageBytes / (2 * G.rb)};
-    cudaEventRecord(g_ev_start, current_stream());
-    cudaStreamWaitEvent(g_work_stream, g_ev_start, 0);
+    cudaEventRecord(S.ev_start, current_stream());
+    cudaStreamWaitEvent(S.work, S.ev_start, 0);
     uint8_t *h = (uint8_t *)host;
     Chunk c[2];
     int b = 0, rc = SF37KV_OK;
     bool have_prev = false, used[2] = {false, false};
     while (rc == SF37KV_OK && ck.next(&c[b])) {
         if (dir == 0) {
-            rc = launch_layers(g_stage[b], c[b].piece, c[b].n, kv_dim, dtype, fmt, group, variant, 0, g_work_stream);
-            if (!rc) rc = check_cuda(cudaMemcpyAsync(g_hbuf[b], g_stage[b], c[b].bytes, cudaMemcpyDeviceToHost,
-                                                     g_work_stream), "slice D2H");
-            if (!rc) rc = check_cuda(cudaEventRecord(g_ev_host[b], g_work_stream), "event");
+            rc = launch_layers(S.stage[b], c[b].piece, c[b].n, kv_dim, dtype, fmt, group, variant, 0, S.work);
+            if (!rc) rc = check_cuda(cudaMemcpyAsync(S.hbuf[b], S.stage[b], c[b].bytes, cudaMemcpyDeviceToHost,
+                                                     S.work), "slice D2H");
+            if (!rc) rc = check_cuda(cudaEventRecord(S.ev_host[b], S.work), "event");
             if (!rc && have_prev) {  // scatter the previous chunk while this one packs
-                rc = check_cuda(cudaEventSynchronize(g_ev_host[b ^ 1]), "slice sync");
-                if (!rc) scatter_gather(c[b ^ 1], layers, G, (uint8_t *)g_hbuf[b ^ 1], h, true);
+                rc = check_cuda(cudaEventSynchronize(S.ev_host[b ^ 1]), "slice sync");
+                if (!rc) scatter_gather(c[b ^ 1], layers, G, (uint8_t *)S.hbuf[b ^ 1], h, true);
             }
         } else {
-            if (used[b]) rc = check_cuda(cudaEventSynchronize(g_ev_host[b]), "slice sync");
-            if (!rc) scatter_gather(c[b], layers, G, (uint8_t *)g_hbuf[b], h, false);
-            if (!rc) rc = check_cuda(cudaMemcpyAsync(g_stage[b], g_hbuf[b], c[b].bytes, cudaMemcpyHostToDevice,
-                                                     g_work_stream), "slice H2D");
-            if (!rc) rc = check_cuda(cudaEventRecord(g_ev_host[b], g_work_stream), "event");
-            if (!rc) rc = launch_layers(g_stage[b], c[b].piece, c[b].n, kv_dim, dtype, fmt, group, 1, 1, g_work_stream);
+            if (used[b]) rc = check_cuda(cudaEventSynchronize(S.ev_host[b]), "slice sync");
+            if (!rc) scatter_gather(c[b], layers, G, (uint8_t *)S.hbuf[b], h, false);
+            if (!rc) rc = check_cuda(cudaMemcpyAsync(S.stage[b], S.hbuf[b], c[b].bytes, cudaMemcpyHostToDevice,
+                                                     S.work), "slice H2D");
+            if (!rc) rc = check_cuda(cudaEventRecord(S.ev_host[b], S.work), "event");
+            if (!rc) rc = launch_layers(S.stage[b], c[b].piece, c[b].n, kv_dim, dtype, fmt, group, 1, 1, S.work);
             used[b] = true;
         }
         have_prev = true;
         b ^= 1;
     }
     if (!rc && dir == 0 && have_prev) {
-        rc = check_cuda(cudaEventSynchronize(g_ev_host[b ^ 1]), "slice sync");
-        if (!rc) scatter_gather(c[b ^ 1], layers, G, (uint8_t *)g_hbuf[b ^ 1], h, true);
+        rc = check_cuda(cudaEventSynchronize(S.ev_host[b ^ 1]), "slice sync");
+        if (!rc) scatter_gather(c[b ^ 1], layers, G, (uint8_t *)S.hbuf[b ^ 1], h, true);
     }
-    const int rs = check_cuda(cudaStreamSynchronize(g_work_stream), "slice sync");
+    const int rs = check_cuda(cudaStreamSynchronize(S.work), "slice sync");
     return rc ? rc : rs;
 }
 
 void staging_release() {
-    for (int i = 0; i < 2; i++) {
-        if (g_stage[i]) {
-            cudaFree(g_stage[i]);
-            g_stage[i] = nullptr;
+    for (Staging &S : g_staging) {
+        std::lock_guard<std::mutex> lk(S.mu);
+        for (int i = 0; i < 2; i++) {
+            if (S.stage[i]) cudaFree(S.stage[i]);
+            S.stage[i] = nullptr;
+            if (S.hbuf[i]) {
+                cudaFreeHost(S.hbuf[i]);
+                cudaEventDestroy(S.ev_host[i]);
+            }
+            S.hbuf[i] = nullptr;
         }
-        if (g_hbuf[i]) {
-            cudaFreeHost(g_hbuf[i]);
-            g_hbuf[i] = nullptr;
-            cudaEventDestroy(g_ev_host[i]);
-        }
+        S.ready = S.host_ready = false;
     }
 }
 

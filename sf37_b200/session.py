@@ -131,3 +131,36 @@ class Session:
         if lib().sf37kv_session_load_payload(ctypes.byref(s), fd, nbytes, err, 512):
             raise SessionError(err.value.decode())
         self.n_tokens = s.n_tokens
+
+    def kvstore_save(self, f, text, reason=1, ext_flags=0, now=None):
+        """An sf37_kvstore record (header, text, payload) to a file object or
+        descriptor at its current offset; returns the record's bytes."""
+        import time as _time
+        fd = f if isinstance(f, int) else f.fileno()
+        if not isinstance(f, int):
+            f.flush()
+        self._sync_in()
+        tb = text.encode() if isinstance(text, str) else bytes(text)
+        n = ctypes.c_uint64(0)
+        err = ctypes.create_string_buffer(512)
+        now = int(_time.time()) if now is None else int(now)
+        if lib().sf37kv_kvstore_save(ctypes.byref(self._struct()), fd, tb, len(tb), reason, ext_flags, now,
+                                     ctypes.byref(n), err, 512):
+            raise SessionError(err.value.decode())
+        return n.value
+
+    def kvstore_load(self, f, prompt, sha=None):
+        """Restores a record whose text is a byte prefix of prompt; returns
+        the tokens restored (raises SessionError with the reference's
+        message otherwise)."""
+        fd = f if isinstance(f, int) else f.fileno()
+        self._sync_in()
+        s = self._struct()
+        pb = prompt.encode() if isinstance(prompt, str) else bytes(prompt)
+        got = ctypes.c_uint32(0)
+        err = ctypes.create_string_buffer(512)
+        if lib().sf37kv_kvstore_load(ctypes.byref(s), fd, pb, len(pb), None if sha is None else sha.encode(),
+                                     ctypes.byref(got), err, 512):
+            raise SessionError(err.value.decode())
+        self.n_tokens = s.n_tokens
+        return got.value

@@ -74,3 +74,42 @@ def test_tensor_core_prefill_bf16(G, pos0, n_tok, cap, sliding):
         want = oracle.attention_prefill(qf, kref, vref, g, pos0, n_tok, cap, qh, kvh, hd, sliding, 512,
                                         t0=a, t1=b)
         assert_close(got[a:b], want[a:b], what=f"tokens {a}..{b}")
+
+
+@pytest.mark.parametrize("G,pos0,n_tok,cap,sliding", [(8, 0, 64, 64, 0), (8, 300, 130, 1024, 0),
+                                                      (8, 1000, 200, 768, 1), (4, 5, 1, 16, 0),
+                                                      (8, 2000, 257, 2400, 1), (4, 700, 100, 750, 0),
+                                                      (8, 90, 70, 128, 0)])
+def test_dropin_prefill_f32_tensor_cores(G, pos0, n_tok, cap, sliding):
+    # fp32 caches and fp32 q (the engine's sf37_cuda_attention_prefill_heads
+    # call, sf37.c:5919): the bf16 hi/lo tensor-core kernel, held to the
+    # reference tests' fp32 tolerance; (700, 100, 750) and (90, 70, 128) wrap
+    # the ring inside the chunk.
+    kvh = 8 if G == 8 else 4
+    qh, hd = G * kvh, 128
+    kd = kvh * hd
+    k = synth.normal(61 + G + pos0, (cap, kd))
+    v = synth.normal(62 + G + pos0, (cap, kd))
+    q = synth.normal(63 + pos0, (n_tok, qh * hd))
+    g = synth.normal(64, (n_tok, qh))
+    out = torch.empty(n_tok, qh * hd, device="cuda")
+    assert kv.attention_prefill_heads(out, dev(q), dev(k), dev(v), dev(g), pos0, n_tok, cap, qh, kvh, hd,
+                                      sliding, 512)
+    want = oracle.attention_prefill(q, k, v, g, pos0, n_tok, cap, qh, kvh, hd, sliding, 512)
+    assert_close(host(out).reshape(n_tok, qh, hd), want, atol=6e-5, rtol=1e-4, what=f"G={G}")
+
+
+def test_native_prefill_f32_cache_bf16_q():
+    # f32 cache + bf16 queries through sf37kv_prefill: q widened, then the
+    # fp32 tensor-core kernel
+    qh, kvh, hd, cap, pos0, n_tok = 64, 8, 128, 4096, 3000, 300
+    kd = kvh * hd
+    k = synth.normal(71, (cap, kd))
+    v = synth.normal(72, (cap, kd))
+    tq = dev(synth.normal(73, (n_tok, qh, hd))).to(torch.bfloat16)
+    qf = tq.float().cpu().numpy()
+    g = synth.normal(74, (n_tok, qh))
+    out = torch.empty(n_tok, qh, hd, device="cuda")
+    kv.prefill(dev(k), dev(v), cap, tq, dev(g), out, pos0, n_tok, qh, kvh, hd, kv.F32)
+    want = oracle.attention_prefill(qf, k, v, g, pos0, n_tok, cap, qh, kvh, hd)
+    assert_close(host(out), want, atol=6e-5, rtol=1e-4)

@@ -194,3 +194,41 @@ def test_kv_head_slices_fill_one_record(dtype, fmt):
                 torch.cuda.synchronize()
                 assert torch.equal(sl[i]["k_cache"], full_k[:, r * kd:(r + 1) * kd])
                 assert torch.equal(sl[i]["v_cache"], full_v[:, r * kd:(r + 1) * kd])
+
+
+def test_kv_head_slice_spans_several_chunks():
+    # A slice record larger than three 64 MiB staging chunks (and far more
+    # than 4096 rows, so several host threads scatter): one KV head of a
+    # 200000-row f16 layer, raw f32 format.  Exercises the double-buffered
+    # pipeline (scatter of chunk c-1 while chunk c packs; the in-use wait on
+    # restore) against pack_to_host / unpack_from_host of the full caches.
+    from sf37_b200 import _lib
+    rows, kd, full = 200000, 128, 1024
+    g = torch.Generator(device="cuda")
+    g.manual_seed(9)
+    k = torch.randn(rows, full, device="cuda", generator=g).half()
+    v = torch.randn(rows, full, device="cuda", generator=g).half()
+    L = [dict(k_cache=k, v_cache=v, cap=rows, first_pos=0, rows=rows)]
+    arr, total = kv.pack_layers_desc(L, full, kv.FMT_RAW)
+    assert 2 * rows * 4 * kd > 3 * (64 << 20)
+    whole = np.empty(total, np.uint8)
+    kv.pack_to_host(whole.ctypes.data, arr, full, kv.F16, kv.FMT_RAW)
+    r = 5
+    ks = k[:, r * kd:(r + 1) * kd].contiguous()
+    vs = v[:, r * kd:(r + 1) * kd].contiguous()
+    sarr = (_lib.PackLayer * 1)(_lib.PackLayer(kv.cache_desc(ks, vs, rows), 0, rows, 0))
+    rec = np.zeros(total, np.uint8)
+    assert _lib.lib().sf37kv_pack_slice_to_host(rec.ctypes.data, sarr, 1, kd, full, r * kd, kv.F16, kv.FMT_RAW,
+                                                64, 1) == 0, _lib.last_error()
+    # only this head's columns of every row were written
+    rb = full * 4
+    recv = rec.reshape(2 * rows, rb)
+    wv = whole.reshape(2 * rows, rb)
+    assert np.array_equal(recv[:, 4 * r * kd:4 * (r + 1) * kd], wv[:, 4 * r * kd:4 * (r + 1) * kd])
+    assert not recv[:, :4 * r * kd].any() and not recv[:, 4 * (r + 1) * kd:].any()
+    ks.zero_()
+    vs.zero_()
+    assert _lib.lib().sf37kv_unpack_slice_from_host(whole.ctypes.data, sarr, 1, kd, full, r * kd, kv.F16,
+                                                    kv.FMT_RAW, 64) == 0, _lib.last_error()
+    torch.cuda.synchronize()
+    assert torch.equal(ks, k[:, r * kd:(r + 1) * kd]) and torch.equal(vs, v[:, r * kd:(r + 1) * kd])
