@@ -1004,6 +1004,92 @@ def prefill_leg(args, rank, world, dev, steps):
             "clocks": clk.summary()}
 
 
+def prefill_f32_leg(dev):
+    """The call the reference engine makes for chunked prefill
+    (sf37.c:5919): sf37_cuda_attention_prefill_heads with fp32 caches and
+    fp32 q, one layer, a 2048-token chunk on a 24576-token prefix (64 Q /
+    8 KV heads, d 128).  Timed through this library's drop-in of the symbol
+    (tensor-core tiles, bf16 hi/lo operand split) and through the
+    reference's own CUDA kernel (oracle/_ref/libsf37ref_cuda.so, a warp per
+    (token, head), sf37_cuda.cu:3163-3317) on the same inputs; the two
+    outputs are compared at the north-star tolerance."""
+    import torch
+    import oracle
+    from sf37_b200 import kv
+    prefix, chunk = 24576, 2048
+    cap = prefix + chunk
+    g = torch.Generator(device=dev)
+    g.manual_seed(21)
+    k = torch.randn(cap, KVH * HD, device=dev, generator=g)
+    v = torch.randn(cap, KVH * HD, device=dev, generator=g)
+    q = torch.randn(chunk, QH, HD, device=dev, generator=g)
+    gate = torch.randn(chunk, QH, device=dev, generator=g)
+    out = torch.empty(chunk, QH, HD, device=dev)
+    pairs = chunk * prefix + chunk * (chunk + 1) // 2
+    flops = 4.0 * HD * pairs * QH
+    peak, kind = _tensor_peak()
+
+    def ours():
+        if not kv.attention_prefill_heads(out, q, k, v, gate, prefix, chunk, cap, QH, KVH, HD, 0, 512):
+            raise RuntimeError("drop-in prefill failed")
+
+    for _ in range(3):
+        ours()
+    torch.cuda.synchronize(dev)
+    clk = ClockSampler(dev.index).__enter__()
+    reps = 10
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        ours()
+    e1.record()
+    torch.cuda.synchronize(dev)
+    clk.__exit__()
+    ms = e0.elapsed_time(e1) / reps
+    ach = flops / (ms * 1e-3) / 1e12
+    res = {"what": "sf37_cuda_attention_prefill_heads, fp32 caches + fp32 q, one layer: 2048-token chunk on a "
+                   "24576-token prefix (the engine's prefill call, sf37.c:5919)",
+           "dropin_ms": ms, "dropin_tokens_per_s": chunk / (ms * 1e-3),
+           "roofline": {"bound": "tensor", "kernel": "prefill_tc32 (mma.sync bf16, 3-term hi/lo split)",
+                        "achieved": ach, "peak": peak, "peak_kind": kind, "unit": "TFLOP/s", "frac": ach / peak,
+                        "algorithmic_flops_per_launch": flops,
+                        "note": "algorithmic flops count one fp32 product; the kernel issues three bf16 products"},
+           "clocks": clk.summary()}
+    try:
+        if not oracle.ref_cuda_available():
+            raise RuntimeError("oracle/_ref/libsf37ref_cuda.so not built")
+        R = oracle.ref_cuda()
+
+        def rt(t):
+            return oracle.ref_tensor(t.data_ptr(), t.numel() * t.element_size())
+        theirs = torch.empty_like(out)
+        args = (rt(theirs), rt(q), rt(k), rt(v), rt(gate), prefix, chunk, cap, QH, KVH, HD, 0, 512)
+        if not R.sf37_cuda_attention_prefill_heads(*args):
+            raise RuntimeError("reference prefill failed")
+        torch.cuda.synchronize(dev)
+        e0.record()
+        rreps = 2
+        for _ in range(rreps):
+            R.sf37_cuda_attention_prefill_heads(*args)
+        e1.record()
+        torch.cuda.synchronize(dev)
+        rms = e0.elapsed_time(e1) / rreps
+        ours()
+        torch.cuda.synchronize(dev)
+        d = (out - theirs).abs()
+        ok = bool(((d <= ATOL) | (d <= RTOL * theirs.abs())).all())
+        res["reference_kernel"] = {"ms": rms, "tokens_per_s": chunk / (rms * 1e-3),
+                                   "TFLOPs": flops / (rms * 1e-3) / 1e12}
+        res["speedup_vs_reference_kernel"] = rms / ms
+        res["parity_vs_reference_kernel"] = {"max_abs": float(d.max()), "ok": ok,
+                                             "tolerance": f"abs {ATOL} or rel {RTOL}"}
+    except Exception as e:
+        res["reference_kernel"] = {"unavailable": str(e)}
+    del k, v, q, out
+    torch.cuda.empty_cache()
+    return res
+
+
 def snapshot_leg(args, rank, world, dev):
     """BASELINE config 5b: pack the 32768-token prefix of 48 f16 layers into
     pinned host memory in both reference formats (raw f32 rows, int8-grouped
@@ -1174,6 +1260,8 @@ def run_default(args, rank, world):
         if world == 1:
             configs["cfg1"] = cfg1_leg(args, dev)
             line["per_layer"] = per_layer_leg(args, dev)
+            line["prefill_dropin"] = prefill_f32_leg(dev)
+            ok = ok and line["prefill_dropin"].get("parity_vs_reference_kernel", {}).get("ok", True)
             if not args.no_ref_gpu:
                 line["reference_gpu"] = reference_gpu_leg(dev, sub_steps)
         line["configs"] = configs
@@ -1203,6 +1291,8 @@ def run_single(args, rank, world):
         line = cfg1_leg(args, dev)
     elif wl == "per_layer":
         line = per_layer_leg(args, dev)
+    elif wl == "prefill_dropin":
+        line = prefill_f32_leg(dev)
     _barrier(world, dev)
     if rank == 0:
         line.setdefault("workload", wl)
@@ -1229,7 +1319,7 @@ def main():
     ap.add_argument("--no-session", action="store_true", help="skip the whole-session checkpoint leg")
     ap.add_argument("--headline-only", action="store_true", help="default workload: skip the other configs")
     ap.add_argument("--workload", default="all",
-                    choices=["all", "decode", "prefill", "hybrid", "long", "snapshot", "cfg1", "per_layer"],
+                    choices=["all", "decode", "prefill", "hybrid", "long", "snapshot", "cfg1", "per_layer", "prefill_dropin"],
                     help="all = config 2 headline + every other config (default); decode = config 2; "
                          "hybrid = config 3; prefill = config 4; long = config 5a; snapshot = config 5b")
     ap.add_argument("--quick", action="store_true",

@@ -49,6 +49,11 @@ def test_record_matches_reference_store(ctx, n):
     # CPU-specific .5 ties (see _tie_only_diffs)
     head = 52 + len(TEXT)
     assert mine[:head] == ref[:head]
+    # payload header word 10 is the backend kind (sf37.c:6942): 1 for a
+    # session on CUDA caches, 0 for the reference's CPU session
+    w10 = head + 40
+    assert mine[w10:w10 + 4] == (1).to_bytes(4, "little") and ref[w10:w10 + 4] == bytes(4)
+    mine = mine[:w10] + bytes(4) + mine[w10 + 4:]
     _tie_only_diffs(mine[head:], ref[head:], (15 + C.LAYERS + n + C.VOCAB + C.EMBD) * 4,
                     _payload_src(kc, vc, n, ctx, caps))
 
