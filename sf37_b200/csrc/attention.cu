@@ -8,28 +8,29 @@
 // a job is one layer's query (decode) or one prefill token (fallback path)
 // and a split is a contiguous run of rows.  Every CTA serves all G query
 // heads of its KV head, so each K/V byte is read from HBM once per group.
-// Inside a CTA the warps take interleaved 16-row blocks, keep an online
-// softmax state each, and merge through shared memory.  Split partials
-// (O, max, sum) are merged one of two ways:
-//  * large launches (many layers): each CTA writes its partial to scratch
-//    and the last CTA of the group (atomic counter) merges them, so a whole
-//    multi-layer step is one launch;
-//  * small launches (one layer or a few): the splits of a group form one
-//    thread-block cluster and merge through distributed shared memory
-//    (finish_cluster), with no scratch and no atomics.
-// Scores are kept in the log2 domain (q pre-scaled by log2(e)/sqrt(d)); a
-// running max is only raised when a block's max exceeds it by more than 8
-// (2^8 headroom), which removes almost all O rescaling.
+// Inside a CTA the warps take interleaved 16-row (f16) or 4/8-row (f32)
+// blocks, keep an online softmax state each, and merge through shared memory.
+// With more than one split per (job, kv head), each CTA writes a partial
+// (O, max, sum) to scratch; the last CTA to finish (atomic counter) merges
+// the partials and writes the output, so a whole multi-layer step is one
+// launch.  Scores are kept in the log2 domain (q pre-scaled by
+// log2(e)/sqrt(d)); a running max is only raised when a block's max exceeds
+// it by more than 8 (2^8 headroom), which removes almost all O rescaling.
 //
-// K/V blocks are staged through a per-warp ring of shared-memory stages
-// filled by 16-byte cp.async copies; QK^T and PV run on mma.sync tiles:
-//  * f16 caches (head_dim 128, G <= 16): f16 operands, q and P split into
-//    f16 hi + lo rows of the M dimension (about 22 significant bits);
-//  * f32 caches (the reference-compatible type): every fp32 operand split
-//    into bf16 hi + lo, four products, fp32 accumulate.
-// The kernels are launched with programmatic dependent launch; a CTA whose
-// rows the previous kernel cannot write stages its first blocks (and
-// prefetches the next into L2) before griddepcontrol.wait.
+// f16 caches (the throughput path, head_dim 128, G <= 16): QK^T and PV are
+// mma.sync m16n8k16 tiles fed straight from 128-bit global loads in
+// registers (no shared-memory staging: the dimension order inside a head is
+// permuted so each thread's loaded words already are its mma fragments).
+// The 16 M-rows of a tile hold 8 query heads twice: rows 0-7 carry the f16
+// "hi" part of q (and of P), rows 8-15 the f16 remainder "lo", so q.K and
+// P.V are computed to ~22 mantissa bits with fp32 accumulation at no extra
+// mma cost.  This is a bandwidth-bound gather; the tensor cores only keep the
+// FMA count out of the way.
+//
+// f32 caches (the reference-compatible path): CUDA-core fp32 kernel, lanes
+// over the head dimension, partial dot products of several rows x heads
+// reduced with a transposing butterfly (N values over 32 lanes in N-1
+// shuffles).
 //
 // Anything else (head_dim != 128, other G): a generic warp-per-head kernel.
 #include <cfloat>
@@ -39,7 +40,6 @@
 #include <cstring>
 #include <mutex>
 
-#include <cooperative_groups.h>
 #include <cuda_bf16.h>
 #include <cmath>
 
@@ -53,18 +53,6 @@ extern unsigned long long g_launches;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr uint32_t kMaxSplits = 256;
 constexpr float kRescaleSlack = 8.0f;
-// Blocks per warp prefetched into L2 before griddepcontrol.wait, beyond the
-// S - 1 staged ones (16 rows of K and V each: 8 KB f16, 16 KB f32).
-#ifndef SF37KV_PREFETCH_F16
-#define SF37KV_PREFETCH_F16 3
-#endif
-#ifndef SF37KV_PREFETCH_F32
-#define SF37KV_PREFETCH_F32 2
-#endif
-constexpr uint32_t kPrefetchF16 = SF37KV_PREFETCH_F16, kPrefetchF32 = SF37KV_PREFETCH_F32;
-// A CTA's partial for the cluster merge, at the end of its stage buffers:
-// G <= 16 heads x (128 O + m + l) floats.
-constexpr uint32_t kClusterPartBytes = 16u * 130u * 4u + 96u;
 
 // Set by attention_jobs_gather for the duration of one attention_jobs call.
 static const GatherDev *g_gather_cur = nullptr;
@@ -519,69 +507,6 @@ __device__ void finish_cta(const DecodeParams &P, const JobDev &J, uint32_t j, u
     gather_group_done(P);
 }
 
-// Cluster form of the split merge (small launches): the n_splits CTAs of a
-// (job, KV head) group form one thread-block cluster.  Each CTA folds its
-// warp streams into a partial (O[G][128], m[G], l[G]) in its own shared
-// memory; after a cluster barrier, CTA c of the cluster reads every CTA's
-// partial through distributed shared memory and writes output float4s
-// c, c + C, c + 2C, ... of the group; a second barrier keeps the partials
-// alive until all reads are done.  No global scratch, counters or atomics:
-// the group finishes together, one barrier round trip after its slowest CTA.
-template <int NT>
-__device__ void finish_cluster(const DecodeParams &P, const JobDev &J, uint32_t kvh, uint32_t n_streams,
-                               float *Os, float *Ms, float *Ls, float *part, const float *gate_s) {
-    namespace cg = cooperative_groups;
-    cg::cluster_group cl = cg::this_cluster();
-    const uint32_t G = P.group, tid = threadIdx.x;
-    float *W = epilogue_x(Ls, G, n_streams), *PM = W + 256, *PL = PM + 16;
-    __syncthreads();
-    stream_weights(G, n_streams, Ms, Ls, W, PM, PL);
-    __syncthreads();
-    for (uint32_t idx = tid; idx < G * 32u; idx += NT) {
-        const uint32_t h = idx >> 5, d4 = (idx & 31u) * 4u;
-        *reinterpret_cast<float4 *>(part + h * 128u + d4) = stream_o(n_streams, Os, W, h, d4);
-    }
-    if (tid < G) {
-        part[G * 128u + 2u * tid] = PM[tid];
-        part[G * 128u + 2u * tid + 1u] = PL[tid];
-    }
-    cl.sync();
-    const uint32_t C = cl.num_blocks(), me = cl.block_rank();
-    for (uint32_t idx = me + tid * C; idx < G * 32u; idx += NT * C) {
-        const uint32_t h = idx >> 5, d4 = (idx & 31u) * 4u;
-        float M = -INFINITY;
-        for (uint32_t c = 0; c < C; c++) M = fmaxf(M, cl.map_shared_rank(part, c)[G * 128u + 2u * h]);
-        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-        float L = 0.f;
-        if (M != -INFINITY) {
-            for (uint32_t c = 0; c < C; c++) {
-                const float *rp = cl.map_shared_rank(part, c);
-                const float w = exp2f(rp[G * 128u + 2u * h] - M);
-                const float4 v = *reinterpret_cast<const float4 *>(rp + h * 128u + d4);
-                L += rp[G * 128u + 2u * h + 1u] * w;
-                acc.x += v.x * w;
-                acc.y += v.y * w;
-                acc.z += v.z * w;
-                acc.w += v.w * w;
-            }
-        }
-        const uint32_t qh = kvh * G + h;
-        *reinterpret_cast<float4 *>(J.out + (uint64_t)qh * 128u + d4) = finalize4(acc, L, gate_s[h]);
-    }
-    cl.sync();
-}
-
-// L2 prefetch of one 16-row block of this warp's stream (K rows on lanes
-// 0-15, V rows on lanes 16-31; `bytes` per row and head).
-__device__ __forceinline__ void prefetch_block(const char *kbase, const char *vbase, uint32_t bb, uint32_t row1,
-                                               uint32_t cap, uint64_t row_bytes, uint32_t lane, uint32_t bytes) {
-    const uint32_t r = lane & 15u;
-    if (bb + r >= row1) return;
-    const uint32_t slot = ring_slot(bb % cap, r, cap);
-    const char *p = (lane < 16u ? kbase : vbase) + (uint64_t)slot * row_bytes;
-    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
-}
-
 // ------------------------------------------------------------ f16 kernel: register fragments
 // NW warps; warp w handles M-tile (w % n_mt) (query heads 8*mt .. 8*mt+7 of
 // the group) and row stream (w / n_mt).  Thread (g = lane/4, t = lane%4).
@@ -617,7 +542,7 @@ __device__ __forceinline__ uint4 lds128(uint32_t addr) {
     return r;
 }
 
-template <int NW, int S, bool PREP = false, bool CL = false>
+template <int NW, int S, bool PREP = false>
 __global__ void __launch_bounds__(NW * 32, 1) decode_f16_pipe_kernel(const __grid_constant__ DecodeParams P) {
     extern __shared__ __align__(128) uint8_t smem_raw[];
     constexpr uint32_t kStage = 8192;  // 16 rows x 256 B for K, then V
@@ -690,11 +615,6 @@ __global__ void __launch_bounds__(NW * 32, 1) decode_f16_pipe_kernel(const __gri
     if (pre_wait) {
 #pragma unroll
         for (int s = 0; s < S - 1; s++) issue(s);
-        // and the next blocks into L2: this CTA may have started when the
-        // previous kernel's CTA on this SM exited, so these reads keep HBM
-        // busy through that kernel's tail and this one's start-up
-        for (uint32_t it = S - 1; it < S - 1 + kPrefetchF16 && it < nblk; it++)
-            prefetch_block(kbase, vbase, b_first + it * bstep, row1, cap, row_bytes, lane, 256u);
     }
     griddep_wait();
     griddep_launch_dependents();
@@ -848,11 +768,7 @@ __global__ void __launch_bounds__(NW * 32, 1) decode_f16_pipe_kernel(const __gri
             Ls[stream * 16u + hrow] = l_run;
         }
     }
-    if constexpr (CL)
-        finish_cluster<NW * 32>(P, J, kvh, n_streams, Os, Ms, Ls,
-                                reinterpret_cast<float *>(smem_raw + NW * S * kStage - kClusterPartBytes), gate_s);
-    else
-        finish_cta<NW * 32>(P, J, j, kvh, split, cta, n_streams, Os, Ms, Ls, smem_raw, NW * S * kStage, gate_s);
+    finish_cta<NW * 32>(P, J, j, kvh, split, cta, n_streams, Os, Ms, Ls, smem_raw, NW * S * kStage, gate_s);
 }
 
 // ------------------------------------------------------------ f32 kernel, tensor cores
@@ -884,7 +800,7 @@ __device__ __forceinline__ void split2(float a, float b, uint32_t &hi, uint32_t 
     lo = *reinterpret_cast<const uint32_t *>(&l);
 }
 
-template <int NW, int S, bool PREP = false, bool CL = false>
+template <int NW, int S, bool PREP = false>
 __global__ void __launch_bounds__(NW * 32, 1) decode_f32_pipe_kernel(const __grid_constant__ DecodeParams P) {
     extern __shared__ __align__(128) uint8_t smem_raw[];
     constexpr uint32_t kStage = 16384;  // 16 rows x 512 B for K, then V
@@ -954,11 +870,6 @@ __global__ void __launch_bounds__(NW * 32, 1) decode_f32_pipe_kernel(const __gri
     if (pre_wait) {
 #pragma unroll
         for (int s = 0; s < S - 1; s++) issue(s);
-        // and the next blocks into L2: this CTA may have started when the
-        // previous kernel's CTA on this SM exited, so these reads keep HBM
-        // busy through that kernel's tail and this one's start-up
-        for (uint32_t it = S - 1; it < S - 1 + kPrefetchF32 && it < nblk; it++)
-            prefetch_block(kbase, vbase, b_first + it * bstep, row1, cap, row_bytes, lane, 512u);
     }
     griddep_wait();
     griddep_launch_dependents();
@@ -1104,11 +1015,7 @@ __global__ void __launch_bounds__(NW * 32, 1) decode_f32_pipe_kernel(const __gri
             Ls[stream * 16u + hrow] = l_run;
         }
     }
-    if constexpr (CL)
-        finish_cluster<NW * 32>(P, J, kvh, n_streams, Os, Ms, Ls,
-                                reinterpret_cast<float *>(smem_raw + NW * S * kStage - kClusterPartBytes), gate_s);
-    else
-        finish_cta<NW * 32>(P, J, j, kvh, split, cta, n_streams, Os, Ms, Ls, smem_raw, NW * S * kStage, gate_s);
+    finish_cta<NW * 32>(P, J, j, kvh, split, cta, n_streams, Os, Ms, Ls, smem_raw, NW * S * kStage, gate_s);
 }
 
 // ------------------------------------------------------------ generic kernel
@@ -1303,7 +1210,7 @@ void note_stream_appends(cudaStream_t s, const JobDev *jobs, uint32_t n) {
 // on the stream drains and wait in griddepcontrol.wait).
 template <typename Kernel>
 static void launch_decode(Kernel kernel, unsigned grid, unsigned warps, size_t smem, cudaStream_t s,
-                          const DecodeParams &P, unsigned cluster = 0) {
+                          const DecodeParams &P) {
     // Kernel attributes, once per kernel instance (the instances share one
     // function-pointer type, so they are told apart by address).
     static const void *done[16];
@@ -1319,58 +1226,12 @@ static void launch_decode(Kernel kernel, unsigned grid, unsigned warps, size_t s
     cfg.blockDim = dim3(warps * 32u);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = s;
-    cudaLaunchAttribute at[2];
-    unsigned na = 0;
-    if (P.pdl) {
-        at[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-        at[na++].val.programmaticStreamSerializationAllowed = 1;
-    }
-    if (cluster) {
-        at[na].id = cudaLaunchAttributeClusterDimension;
-        at[na].val.clusterDim.x = cluster;
-        at[na].val.clusterDim.y = 1;
-        at[na++].val.clusterDim.z = 1;
-    }
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = at;
-    cfg.numAttrs = na;
+    cfg.numAttrs = P.pdl ? 1 : 0;
     (void)cudaLaunchKernelEx(&cfg, kernel, P);
-}
-
-// Cluster size for the cluster-merge form of a small launch of `groups`
-// (job, KV head) groups, one CTA per SM: the largest power of two <= 16 with
-// groups x C <= SMs whose clusters can all be resident at once (occupancy
-// query, per kernel and group count, cached); 0 when none >= 2 qualifies.
-template <typename Kernel>
-static unsigned cluster_size(Kernel kernel, unsigned warps, size_t smem, uint32_t groups, int sms) {
-    struct Entry { const void *k; uint32_t groups; unsigned c; };
-    static Entry cache[32];
-    static int n_cache = 0;
-    static std::mutex mu;
-    std::lock_guard<std::mutex> lk(mu);
-    for (int i = 0; i < n_cache; i++)
-        if (cache[i].k == (const void *)kernel && cache[i].groups == groups) return cache[i].c;
-    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    cudaFuncSetAttribute(kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
-    unsigned pick = 0;
-    for (unsigned c = 16; c >= 2 && !pick; c /= 2) {
-        if ((uint64_t)groups * c > (uint64_t)sms) continue;
-        cudaLaunchConfig_t cfg = {};
-        cfg.gridDim = dim3(groups * c);
-        cfg.blockDim = dim3(warps * 32u);
-        cfg.dynamicSmemBytes = smem;
-        cudaLaunchAttribute at;
-        at.id = cudaLaunchAttributeClusterDimension;
-        at.val.clusterDim.x = c;
-        at.val.clusterDim.y = 1;
-        at.val.clusterDim.z = 1;
-        cfg.attrs = &at;
-        cfg.numAttrs = 1;
-        int n = 0;
-        if (cudaOccupancyMaxActiveClusters(&n, kernel, &cfg) == cudaSuccess && (uint32_t)n >= groups) pick = c;
-    }
-    (void)cudaGetLastError();
-    if (n_cache < 32) cache[n_cache++] = Entry{(const void *)kernel, groups, pick};
-    return pick;
 }
 
 int attention_jobs(const AttnJob *jobs, uint32_t n, uint32_t q_heads, uint32_t kv_heads,
@@ -1498,17 +1359,6 @@ int attention_jobs(const AttnJob *jobs, uint32_t n, uint32_t q_heads, uint32_t k
         const uint32_t groups = m * kv_heads;
         const bool small = groups * 2u <= (uint32_t)sms;
         const int slot = (dtype == SF37KV_F16 ? 0 : 2) + (any_prep ? 1 : 0);
-        // Small launches without a peer gather merge their splits inside a
-        // thread-block cluster (finish_cluster): C splits per group.
-        unsigned cl = 0;
-        if (small && !P.gat.world) {
-            switch (slot) {
-                case 0: cl = cluster_size(decode_f16_pipe_kernel<8, 3, false, true>, 8, kSmemF16Wide, groups, sms); break;
-                case 1: cl = cluster_size(decode_f16_pipe_kernel<8, 3, true, true>, 8, kSmemF16Wide + kPrepSmem, groups, sms); break;
-                case 2: cl = cluster_size(decode_f32_pipe_kernel<4, 3, false, true>, 4, kSmemF32, groups, sms); break;
-                default: cl = cluster_size(decode_f32_pipe_kernel<4, 3, true, true>, 4, kSmemF32 + kPrepSmem, groups, sms); break;
-            }
-        }
         P.err = device_error_flag();
         uint32_t ctas = 0;
         bool any_split = false;
@@ -1517,12 +1367,7 @@ int attention_jobs(const AttnJob *jobs, uint32_t n, uint32_t q_heads, uint32_t k
             const uint32_t rows = A.end - A.start;
             uint64_t ns;
             uint32_t sr;
-            if (cl) {
-                ns = cl;
-                sr = (uint32_t)((rows + ns - 1) / ns);
-                sr = (sr + 15u) & ~15u;
-                if (sr == 0) sr = 16;
-            } else if (small) {
+            if (small) {
                 // splits in proportion to the job's share of all rows
                 ns = (uint64_t)sms * rows / (total ? total : 1);
                 if (ns < 1) ns = 1;
@@ -1538,9 +1383,9 @@ int attention_jobs(const AttnJob *jobs, uint32_t n, uint32_t q_heads, uint32_t k
                 sr = (sr + 127u) & ~127u;
                 if (sr == 0) sr = 128;
             }
-            if (!cl) ns = (rows + sr - 1) / sr;  // a cluster keeps all C splits (some may be empty)
+            ns = (rows + sr - 1) / sr;
             if (ns < 1) ns = 1;
-            if (ns > 1 && !cl) any_split = true;
+            if (ns > 1) any_split = true;
             JobDev &D = P.job[i];
             D = JobDev{A.k, A.v, A.q, A.gate, A.out, A.start, A.end, A.cap, sr, (uint32_t)ns, ctas,
                        fuses ? A.k_new : nullptr, fuses ? A.v_new : nullptr,
@@ -1569,14 +1414,6 @@ int attention_jobs(const AttnJob *jobs, uint32_t n, uint32_t q_heads, uint32_t k
         P.pdl = 1;
         mark_pre(stream, P.job, m);
         note_stream_appends(stream, P.job, m);
-        if (cl) {
-            switch (slot) {
-                case 0: launch_decode(decode_f16_pipe_kernel<8, 3, false, true>, ctas, 8, kSmemF16Wide, stream, P, cl); break;
-                case 1: launch_decode(decode_f16_pipe_kernel<8, 3, true, true>, ctas, 8, kSmemF16Wide + kPrepSmem, stream, P, cl); break;
-                case 2: launch_decode(decode_f32_pipe_kernel<4, 3, false, true>, ctas, 4, kSmemF32, stream, P, cl); break;
-                default: launch_decode(decode_f32_pipe_kernel<4, 3, true, true>, ctas, 4, kSmemF32 + kPrepSmem, stream, P, cl); break;
-            }
-        } else
         switch (slot * 2 + (small ? 1 : 0)) {
             case 0: launch_decode(decode_f16_pipe_kernel<4, 3, false>, ctas, 4, kSmemF16, stream, P); break;
             case 1: launch_decode(decode_f16_pipe_kernel<8, 3, false>, ctas, 8, kSmemF16Wide, stream, P); break;
