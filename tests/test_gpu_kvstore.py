@@ -94,7 +94,7 @@ def test_record_roundtrip_and_checks():
             assert np.array_equal(gv[slots], ok_v[il][slots])
         assert np.array_equal(r.tokens[:n], toks)
         for prompt, key, msg in (("What", sha, "cached text is longer than prompt"),
-                                 ("<|user|>What is the capital of Spain?<|assistant|>", sha,
+                                 ("<|user|>What is the capital of Sweden?<|assistant|>", sha,
                                   "cached text prefix mismatch"),
                                  (TEXT, "0" * 40, "cached text hash mismatch")):
             f.seek(3)
