@@ -268,6 +268,19 @@ __device__ __forceinline__ uint32_t ring_slot(uint32_t sb, uint32_t x, uint32_t 
     return s;
 }
 
+// Streaming copy of K/V rows with an L2 evict-first policy: a decode step
+// reads far more K/V than L2 holds, and without the hint the stream evicts
+// what the kernel's tail needs hot -- its own instructions, q, the split
+// partials and counters -- so every cold access of the epilogue waits behind
+// the HBM queue.
+__device__ __forceinline__ uint64_t evict_first_policy() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+__device__ __forceinline__ void cp_async16_ef(uint32_t smem_addr, const void *gptr, uint64_t pol) {
+    asm volatile("cp.async.cg.shared.global.L2::cache_hint [%0], [%1], 16, %2;" ::"r"(smem_addr), "l"(gptr), "l"(pol));
+}
 __device__ __forceinline__ void cp_async16(uint32_t smem_addr, const void *gptr) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr), "l"(gptr));
 }
@@ -277,27 +290,43 @@ __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_gr
 
 // ------------------------------------------------------------ CTA epilogue
 // Shared memory used by the epilogue: per stream and head, O[128], m, l.
-//   Os[(stream * 16 + h) * 128 + d], Ms[stream*16 + h], Ls[stream*16 + h]
+//   Os[os_at(stream * 16 + h, d)], Ms[stream*16 + h], Ls[stream*16 + h]
 // followed by X: W[stream*16 + h] (stream weights), PM[16], PL[16].
 // After the stream merge, the CTA's result is written either directly to the
 // output (single split) or to scratch followed by the last-CTA reduction.
 
+// Float index of dimension d of row `row` (= stream * 16 + head) in Os: rows
+// of 128 floats whose 16-byte chunks are permuted by chunk ^ (row & 7) ^
+// ((chunk >> 3) & 3).  The warps' fragment stores (8 heads x 4 column groups
+// per instruction) then spread over the banks instead of landing 16- or
+// 32-fold on one, and float4 reads of a row stay whole and conflict free.
+__device__ __forceinline__ uint32_t os_at(uint32_t row, uint32_t d) {
+    const uint32_t c = d >> 2;
+    return row * 128u + ((c ^ (row & 7u) ^ ((c >> 3) & 3u)) << 2) + (d & 3u);
+}
+
 // Stream weights of each head h < G: M = max over streams of m, W[s][h] =
-// 2^(m_s - M), L = sum_s l_s W[s][h] (one thread per head).
+// 2^(m_s - M), L = sum_s l_s W[s][h].  Warp w takes heads w, w + nw, ...;
+// lane s takes stream s (n_streams <= 32), reductions by shuffles.
 __device__ __forceinline__ void stream_weights(uint32_t G, uint32_t n_streams, const float *Ms, const float *Ls,
                                                float *W, float *PM, float *PL) {
-    const uint32_t h = threadIdx.x;
-    if (h >= G) return;
-    float M = -INFINITY;
-    for (uint32_t s = 0; s < n_streams; s++) M = fmaxf(M, Ms[s * 16u + h]);
-    float L = 0.f;
-    for (uint32_t s = 0; s < n_streams; s++) {
-        const float w = M == -INFINITY ? 0.f : exp2f(Ms[s * 16u + h] - M);
-        W[s * 16u + h] = w;
-        L += Ls[s * 16u + h] * w;
+    const uint32_t lane = threadIdx.x & 31u, nw = blockDim.x >> 5;
+    for (uint32_t h = threadIdx.x >> 5; h < G; h += nw) {
+        const bool on = lane < n_streams;
+        const float m = on ? Ms[lane * 16u + h] : -INFINITY;
+        float M = m;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+        const float w = (M == -INFINITY || !on) ? 0.f : fast_exp2(m - M);
+        float L = on ? Ls[lane * 16u + h] * w : 0.f;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
+        if (on) W[lane * 16u + h] = w;
+        if (lane == 0) {
+            PM[h] = M;
+            PL[h] = L;
+        }
     }
-    PM[h] = M;
-    PL[h] = L;
 }
 
 // sum_s W[s][h] * O_s[h][d4 .. d4+3]
@@ -306,7 +335,7 @@ __device__ __forceinline__ float4 stream_o(uint32_t n_streams, const float *Os, 
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
     for (uint32_t s = 0; s < n_streams; s++) {
         const float w = W[s * 16u + h];
-        const float4 o = *reinterpret_cast<const float4 *>(Os + (s * 16u + h) * 128u + d4);
+        const float4 o = *reinterpret_cast<const float4 *>(Os + os_at(s * 16u + h, d4));
         acc.x += o.x * w;
         acc.y += o.y * w;
         acc.z += o.z * w;
@@ -364,16 +393,22 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t phase) {
 // The last CTA of a (job, KV head) merges its n split partials.  Thread 0
 // starts bulk copies of whole partials (O vectors and (m, l) pairs) into the
 // stage buffers, as many splits per pass as fit (all of them for the small-
-// launch plan), so a pass costs one L2 round trip; each thread then folds the
-// pass into its running (max, sum, O) with an online rescale.
+// launch plan), so a pass costs one L2 round trip.  Per pass the weights are
+// computed once per (split, head) in parallel -- running max M_h, the old
+// state's rescale 2^(M_old - M_h), w[s][h] = 2^(m_s - M_h) -- and each
+// thread then folds its float4s of O with independent multiply-adds.
+constexpr uint32_t kMergePass = 48;  // splits per pass at most
 template <int NT>
 __device__ void merge_partials(const DecodeParams &P, const JobDev &J, uint32_t kvh, uint8_t *smem,
                                uint32_t stage_bytes, const float *gate_s) {
+    __shared__ float mw[kMergePass * 16];        // w[s][h]
+    __shared__ float mM[16], mScale[16], mL[16];  // running max, rescale of the old state, running sum
     const uint32_t G = P.group, n = J.n_splits, stride = P.part_stride, tid = threadIdx.x;
     const float *P0 = P.part + (uint64_t)(J.cta_begin + kvh * n) * stride;
     const uint32_t split_bytes = stride * 4u;
     const uint32_t bar = (uint32_t)__cvta_generic_to_shared(smem + stage_bytes - 16u);
     uint32_t cnt_max = (stage_bytes - 16u) / split_bytes;
+    if (cnt_max > kMergePass) cnt_max = kMergePass;
     if (cnt_max < 1) cnt_max = 1;
     const uint32_t land = (uint32_t)__cvta_generic_to_shared(smem);
     auto issue = [&](uint32_t s0) {
@@ -392,18 +427,17 @@ __device__ void merge_partials(const DecodeParams &P, const JobDev &J, uint32_t 
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         issue(0);
     }
+    if (tid < 16) {
+        mM[tid] = -INFINITY;
+        mL[tid] = 0.f;
+    }
     __syncthreads();
     const float *Lf = reinterpret_cast<const float *>(smem);
     const float4 *L4 = reinterpret_cast<const float4 *>(smem);
     constexpr int kPer = (16 * 32 + NT - 1) / NT;  // float4 outputs per thread (G <= 16)
     float4 acc[kPer];
-    float Mr[kPer], Lr[kPer];
 #pragma unroll
-    for (int k = 0; k < kPer; k++) {
-        acc[k] = make_float4(0.f, 0.f, 0.f, 0.f);
-        Mr[k] = -INFINITY;
-        Lr[k] = 0.f;
-    }
+    for (int k = 0; k < kPer; k++) acc[k] = make_float4(0.f, 0.f, 0.f, 0.f);
     bool ok = true;
     uint32_t phase = 0;
     for (uint32_t s0 = 0; s0 < n; s0 += cnt_max) {
@@ -411,31 +445,50 @@ __device__ void merge_partials(const DecodeParams &P, const JobDev &J, uint32_t 
         if (!mbar_wait(bar, phase)) ok = false;
         phase ^= 1u;
         if (ok) {
+            // per head (warp w: heads w, w + nw, ...; lanes over the pass's
+            // splits): running max, rescale of the old state, split
+            // weights and the running sum, all by shuffles
+            const uint32_t lane = tid & 31u, nw = NT / 32u;
+            for (uint32_t h = tid >> 5; h < G; h += nw) {
+                float mp = -INFINITY;
+                for (uint32_t s = lane; s < cnt; s += 32u) mp = fmaxf(mp, Lf[s * stride + G * 128u + 2u * h]);
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) mp = fmaxf(mp, __shfl_xor_sync(0xffffffffu, mp, o));
+                const float mo = mM[h], mn = fmaxf(mo, mp);
+                float L = 0.f;
+                for (uint32_t s = lane; s < cnt; s += 32u) {
+                    const float w = mn == -INFINITY ? 0.f : fast_exp2(Lf[s * stride + G * 128u + 2u * h] - mn);
+                    mw[s * 16u + h] = w;
+                    L += Lf[s * stride + G * 128u + 2u * h + 1u] * w;
+                }
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
+                __syncwarp();
+                if (lane == 0) {
+                    const float sc = mo == -INFINITY ? 0.f : fast_exp2(mo - mn);
+                    mScale[h] = sc;
+                    mL[h] = mL[h] * sc + L;
+                    mM[h] = mn;
+                }
+            }
+            __syncthreads();
 #pragma unroll
             for (int k = 0; k < kPer; k++) {
                 const uint32_t idx = tid + (uint32_t)k * NT;
                 if (idx >= G * 32u) continue;
-                const uint32_t ml = G * 128u + 2u * (idx >> 5);
-                float mp = -INFINITY;
-                for (uint32_t s = 0; s < cnt; s++) mp = fmaxf(mp, Lf[s * stride + ml]);
-                const float mnew = fmaxf(Mr[k], mp);
-                if (mnew == -INFINITY) continue;
-                const float sc = exp2f(Mr[k] - mnew);
-                acc[k].x *= sc;
-                acc[k].y *= sc;
-                acc[k].z *= sc;
-                acc[k].w *= sc;
-                Lr[k] *= sc;
+                const uint32_t h = idx >> 5;
+                const float sc = mScale[h];
+                float4 a = make_float4(acc[k].x * sc, acc[k].y * sc, acc[k].z * sc, acc[k].w * sc);
+#pragma unroll 4
                 for (uint32_t s = 0; s < cnt; s++) {
-                    const float w = exp2f(Lf[s * stride + ml] - mnew);
+                    const float w = mw[s * 16u + h];
                     const float4 v = L4[s * (stride / 4u) + idx];
-                    Lr[k] += Lf[s * stride + ml + 1u] * w;
-                    acc[k].x += v.x * w;
-                    acc[k].y += v.y * w;
-                    acc[k].z += v.z * w;
-                    acc[k].w += v.w * w;
+                    a.x = fmaf(v.x, w, a.x);
+                    a.y = fmaf(v.y, w, a.y);
+                    a.z = fmaf(v.z, w, a.z);
+                    a.w = fmaf(v.w, w, a.w);
                 }
-                Mr[k] = mnew;
+                acc[k] = a;
             }
         }
         __syncthreads();
@@ -451,7 +504,7 @@ __device__ void merge_partials(const DecodeParams &P, const JobDev &J, uint32_t 
         if (idx < G * 32u) {
             const uint32_t h = idx >> 5, d4 = (idx & 31u) * 4u;
             const uint32_t qh = kvh * G + h;
-            const float4 r = finalize4(acc[k], Lr[k], gate_s[h]);
+            const float4 r = finalize4(acc[k], mL[h], gate_s[h]);
             *reinterpret_cast<float4 *>(J.out + (uint64_t)qh * 128u + d4) = r;
             if (P.gat.world) gather_store4(P, J, (uint64_t)qh * 128u + d4, r);
         }
@@ -501,7 +554,7 @@ __device__ void finish_cta(const DecodeParams &P, const JobDev &J, uint32_t j, u
     }
     __syncthreads();
     if (!s_last) return;
-    __threadfence();
+    // (thread 0's acquire above orders the bulk copies it issues next)
     merge_partials<NT>(P, J, kvh, smem, stage_bytes, gate_s);
     if (tid == 0) *ctr = 0u;  // ready for the next launch
     gather_group_done(P);
@@ -579,6 +632,7 @@ __global__ void __launch_bounds__(NW * 32, 1) decode_f16_pipe_kernel(const __gri
 
     // Copy block `it` (rows b_first + it*bstep ...) into stage it % S.
     // Lane copies chunks c = lane + 32*i (i < 8) of K and of V: row c>>4, chunk c&15.
+    const uint64_t pol = evict_first_policy();
     auto issue = [&](uint32_t it) {
         if (it < nblk) {
             const uint32_t bb = b_first + it * bstep;
@@ -591,8 +645,8 @@ __global__ void __launch_bounds__(NW * 32, 1) decode_f16_pipe_kernel(const __gri
                 const uint32_t slot = bb + r < row1 ? ring_slot(sb, r, cap) : sb;
                 const uint64_t go = (uint64_t)slot * row_bytes + ch * 16u;
                 const uint32_t so = r * 256u + ((ch ^ swz(r)) * 16u);
-                cp_async16(st + so, kbase + go);
-                cp_async16(st + 4096u + so, vbase + go);
+                cp_async16_ef(st + so, kbase + go, pol);
+                cp_async16_ef(st + 4096u + so, vbase + go, pol);
             }
         }
         cp_async_commit();
@@ -753,7 +807,7 @@ __global__ void __launch_bounds__(NW * 32, 1) decode_f16_pipe_kernel(const __gri
     l_run += __shfl_xor_sync(0xffffffffu, l_run, 1);
     l_run += __shfl_xor_sync(0xffffffffu, l_run, 2);
     const uint32_t hrow = mt * 8u + g;
-    float *Ow = Os + (stream * 16u + hrow) * 128u;
+    const uint32_t orow = stream * 16u + hrow;
     if (hrow < G) {
 #pragma unroll
         for (int jt = 0; jt < 16; jt++)
@@ -761,7 +815,7 @@ __global__ void __launch_bounds__(NW * 32, 1) decode_f16_pipe_kernel(const __gri
             for (int e = 0; e < 2; e++) {
                 const uint32_t c = 2u * t + e;
                 const uint32_t dim = jt < 8 ? 8u * c + jt : 64u + 8u * c + (jt - 8);
-                Ow[dim] = o[jt][e] + o[jt][e + 2];
+                Os[os_at(orow, dim)] = o[jt][e] + o[jt][e + 2];
             }
         if (t == 0) {
             Ms[stream * 16u + hrow] = m_run;
@@ -834,6 +888,7 @@ __global__ void __launch_bounds__(NW * 32, 1) decode_f32_pipe_kernel(const __gri
     const uint32_t b_first = row0 + stream * 16u;
     const uint32_t nblk = b_first < row1 ? (row1 - b_first + bstep - 1) / bstep : 0u;
 
+    const uint64_t pol = evict_first_policy();
     auto issue = [&](uint32_t it) {
         if (it < nblk) {
             const uint32_t bb = b_first + it * bstep;
@@ -846,8 +901,8 @@ __global__ void __launch_bounds__(NW * 32, 1) decode_f32_pipe_kernel(const __gri
                 const uint32_t slot = bb + r < row1 ? ring_slot(sb, r, cap) : sb;
                 const uint64_t go = (uint64_t)slot * row_bytes + ch * 16u;
                 const uint32_t so = r * 512u + ((ch ^ swz32(r)) * 16u);
-                cp_async16(st + so, kbase + go);
-                cp_async16(st + 8192u + so, vbase + go);
+                cp_async16_ef(st + so, kbase + go, pol);
+                cp_async16_ef(st + 8192u + so, vbase + go, pol);
             }
         }
         cp_async_commit();
@@ -1004,12 +1059,12 @@ __global__ void __launch_bounds__(NW * 32, 1) decode_f32_pipe_kernel(const __gri
     l_run += __shfl_xor_sync(0xffffffffu, l_run, 1);
     l_run += __shfl_xor_sync(0xffffffffu, l_run, 2);
     const uint32_t hrow = mt * 8u + g;
-    float *Ow = Os + (stream * 16u + hrow) * 128u;
+    const uint32_t orow = stream * 16u + hrow;
     if (hrow < G) {
 #pragma unroll
         for (int jt = 0; jt < 16; jt++)
 #pragma unroll
-            for (int e = 0; e < 2; e++) Ow[16u * (2u * t + e) + jt] = o[jt][e] + o[jt][e + 2];
+            for (int e = 0; e < 2; e++) Os[os_at(orow, 16u * (2u * t + e) + jt)] = o[jt][e] + o[jt][e + 2];
         if (t == 0) {
             Ms[stream * 16u + hrow] = m_run;
             Ls[stream * 16u + hrow] = l_run;
