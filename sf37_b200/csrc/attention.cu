@@ -203,16 +203,23 @@ __device__ __forceinline__ void gather_store4(const DecodeParams &P, const JobDe
         if (p != P.gat.rank) *reinterpret_cast<float4 *>(P.gat.peer[p] + J.gather_off + idx) = v;
 }
 // Called by every CTA that wrote final outputs of one (job, kv head) group.
+// Thread 0's system-scope acq_rel atomic publishes the CTA's peer stores
+// (they precede it through the barrier); the last group's acquire has seen
+// every group's, and one system fence then releases all flag stores at once
+// (a release store per peer would pay a fence per peer).  Measured at 8
+// GPUs: gather launch 145 -> 140 us with the atomic in place of a system
+// fence per group.
 __device__ __forceinline__ void gather_group_done(const DecodeParams &P) {
     if (!P.gat.world) return;
-    __threadfence_system();
     __syncthreads();
     if (threadIdx.x == 0) {
-        if (atomicAdd(P.gat.done, 1u) == P.gat.total_groups - 1u) {
-            __threadfence_system();
+        uint32_t prev;
+        asm volatile("atom.acq_rel.sys.global.add.u32 %0, [%1], 1;" : "=r"(prev) : "l"(P.gat.done) : "memory");
+        if (prev == P.gat.total_groups - 1u) {
+            asm volatile("fence.acq_rel.sys;" ::: "memory");
             for (uint32_t p = 0; p < P.gat.world; p++) {
                 uint32_t *f = P.gat.peer_flags[p] + P.gat.rank;
-                asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(f), "r"(P.gat.epoch) : "memory");
+                asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(f), "r"(P.gat.epoch) : "memory");
             }
             *P.gat.done = 0u;
         }

@@ -25,8 +25,12 @@ extern unsigned long long g_launches;
 // kernel (which triggers its dependents at its start), so it is resident and
 // polling while the decode runs.  It returns only after griddepcontrol.wait,
 // i.e. after the decode kernel has completed, so work after it on the stream
-// sees a finished step.
+// sees a finished step.  It triggers its own dependents at once: the next
+// step's decode CTAs then launch into free SMs and wait in their own
+// griddepcontrol.wait for this kernel, hiding that launch (measured at 8
+// GPUs: 150 -> 147-149 us per step).
 __global__ void gather_wait_kernel(const uint32_t *flags, uint32_t world, uint32_t epoch, int *err) {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const uint32_t p = threadIdx.x;
     bool ok = true;
     if (p < world) {

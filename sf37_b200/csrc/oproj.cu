@@ -196,13 +196,16 @@ __global__ void __launch_bounds__(kWarps * 32) oproj_q8_0_kernel(const __grid_co
             for (uint32_t p = 0; p < P.red.world; p++)
                 if (p != P.red.rank) P.red.peer[p][J.red_off + r0 + i] = v;
         }
-        __threadfence_system();
+        // publish: system acq_rel atomic per CTA, one fence before the flags
         __syncthreads();
-        if (threadIdx.x == 0 && atomicAdd(P.red.done, 1u) == P.red.total_groups - 1u) {
-            __threadfence_system();
+        uint32_t prev = 0;
+        if (threadIdx.x == 0)
+            asm volatile("atom.acq_rel.sys.global.add.u32 %0, [%1], 1;" : "=r"(prev) : "l"(P.red.done) : "memory");
+        if (threadIdx.x == 0 && prev == P.red.total_groups - 1u) {
+            asm volatile("fence.acq_rel.sys;" ::: "memory");
             for (uint32_t p = 0; p < P.red.world; p++) {
                 uint32_t *f = P.red.peer_flags[p] + P.red.rank;
-                asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(f), "r"(P.red.epoch) : "memory");
+                asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(f), "r"(P.red.epoch) : "memory");
             }
             *P.red.done = 0u;
         }
