@@ -148,13 +148,15 @@ __device__ __forceinline__ void encode8(const PackParams &P, const float (&x)[8]
     // The reference clamps the code to [-127, 127]; that clamp never fires:
     // every finite v has |v| <= m, so |v * inv| <= 127 (1 + 4 ulp) < 127.5
     // and rint gives at most 127 (likewise for v / scale).  Non-finite v are
-    // encoded as 0.  The low byte of the int is the int8 code.
+    // encoded as 0.  y + 1.5 * 2^23 rounds y to the nearest even integer
+    // (as rint), whose two's-complement low byte is the sum's low byte: the
+    // int8 code, computed on the FMA pipe rather than the conversion unit.
     uint32_t q[8];
 #pragma unroll
     for (int i = 0; i < 8; i++) {
         const float v = fabsf(x[i]) < INFINITY ? x[i] : 0.f;
         const float y = (P.variant == 1 || m <= 0.f) ? __fmul_rn(v, inv) : __fdiv_rn(v, scale);
-        q[i] = (uint32_t)__float2int_rn(y);
+        q[i] = __float_as_uint(__fadd_rn(y, 12582912.0f));  // rint by 1.5 * 2^23 (|y| <= 127)
     }
     const uint32_t lo = __byte_perm(__byte_perm(q[0], q[1], 0x0040u), __byte_perm(q[2], q[3], 0x0040u), 0x5410u);
     const uint32_t hi = __byte_perm(__byte_perm(q[4], q[5], 0x0040u), __byte_perm(q[6], q[7], 0x0040u), 0x5410u);
@@ -343,7 +345,10 @@ __global__ void __launch_bounds__(128) pack_i8x16_kernel(uint8_t *dst, const __g
             for (int i = 0; i < 16; i++) {
                 const float v = fabsf(x[i]) < INFINITY ? x[i] : 0.f;
                 const float y = (P.variant == 1 || m <= 0.f) ? __fmul_rn(v, inv) : __fdiv_rn(v, scale);
-                q[i] = (uint32_t)__float2int_rn(y);
+                // round to nearest even by adding 1.5 * 2^23 (|y| <= 127): the
+                // sum's low byte is the int8 code, as rint's would be, and
+                // the add runs on the FMA pipe instead of the conversion unit
+                q[i] = __float_as_uint(__fadd_rn(y, 12582912.0f));
             }
             uint32_t w[4];
 #pragma unroll
