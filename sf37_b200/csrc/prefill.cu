@@ -2,10 +2,12 @@
 // pos0 + t over rows start_at(pos0+t) .. pos0+t (attention_prefill_heads128
 // _warp_kernel, sf37_cuda.cu:3163-3239; entry point 3241-3317).
 //
-// This file holds the entry points and the query-per-job path (every token
-// runs the split-K decode kernels; K/V are re-read from L2 per token).  The
-// tensor-core tile kernel for f16 caches lives in prefill_tc.cu and is used
-// when its shape conditions hold.
+// This file holds the entry points, the dispatch and the query-per-job
+// fallback (every token runs the split-K decode kernels; K/V are re-read from
+// L2 per token), used only for shapes the tile kernels do not take (head_dim
+// other than 128, other groups).  The tile kernels: prefill_tc05.cu (tcgen05,
+// f16 caches + bf16 q), prefill_tc.cu (mma.sync: f16 caches with wrapping
+// rings or f32 q, and fp32 caches + fp32 q, the engine's drop-in call).
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
